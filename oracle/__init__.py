@@ -1,0 +1,182 @@
+"""CPU oracle for the masked-selection path -- TEST INFRASTRUCTURE ONLY.
+
+A plain-C restatement (``oracle.c``) of the reference's own CPU/PyTorch
+implementation of the path, wrapped with ctypes and numpy.  Only the tests,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` use it, and
+only as the checker or the timed CPU baseline: the shipped library never calls
+it and has no CPU fallback.
+
+Reference functions restated (file:line in karthikeyansura/bitmask-speculation):
+
+* ``mask_count``    -- grammar/density.py:23-48 ``packed_mask_count``
+* ``reduce_rows``   -- benchmarks/reductions.py:9-17 ``torch_reduce`` with the
+  native token/status convention of csrc/argmax.cu:77-98
+* ``sample_rows``   -- kernels/reference.py:10-52 ``masked_sample_reference``
+  (status codes of csrc/sample.cu:24-25)
+* ``fsum``          -- CPython ``math.fsum`` used by reference.py:42
+* ``budget``        -- decoding/scheduling.py:40-46 ``DensityPolicy.budget``
+* ``verify``        -- decoding/verification.py:18-48 ``verify_prefix`` over
+  per-row targets (models/transformers.py:181-201)
+
+The oracle is pinned against golden vectors produced by the reference itself
+(``tests/golden/``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+SOURCE = HERE / "oracle.c"
+LIBRARY = HERE / "_build" / "liboracle.so"
+
+DTYPE_CODES = {"float32": 0, "bfloat16": 1, "float16": 2}
+_lock = threading.Lock()
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile ``oracle.c`` with gcc + OpenMP into ``oracle/_build``."""
+    LIBRARY.parent.mkdir(parents=True, exist_ok=True)
+    if force or not LIBRARY.exists() or LIBRARY.stat().st_mtime < SOURCE.stat().st_mtime:
+        tmp = LIBRARY.with_suffix(f".{os.getpid()}.tmp")
+        subprocess.run(["gcc", "-O2", "-fopenmp", "-fPIC", "-shared", "-std=c11",
+                        "-fno-fast-math", "-ffp-contract=off", "-o", str(tmp), str(SOURCE), "-lm"],
+                       check=True)
+        os.replace(tmp, LIBRARY)
+    return LIBRARY
+
+
+def _load():
+    global _lib
+    with _lock:
+        if _lib is None:
+            lib = ctypes.CDLL(str(build()))
+            p, i64, i32, f64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_double
+            lib.orc_mask_count.argtypes = [p, i64]
+            lib.orc_mask_count.restype = i64
+            lib.orc_reduce_rows.argtypes = [p, ctypes.c_int, p, i64, i64, p, p, p, ctypes.c_int]
+            lib.orc_sample_rows.argtypes = [p, ctypes.c_int, p, i64, i64, f64, p, p, p, ctypes.c_int]
+            lib.orc_fsum.argtypes = [p, i64]
+            lib.orc_fsum.restype = f64
+            lib.orc_budget.argtypes = [i32, f64, f64, i32, i32, f64]
+            lib.orc_budget.restype = i32
+            lib.orc_budget_rows.argtypes = [i32, f64, f64, i32, i32, p, i64, i64, p, p]
+            lib.orc_verify.argtypes = [p, p, i64, i64, p, p, p, p, p, p]
+            lib.orc_widen.argtypes = [p, ctypes.c_int, i64, p]
+            lib.orc_max_threads.restype = ctypes.c_int
+            _lib = lib
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _logit_array(logits, dtype: str | None):
+    """Accept a numpy array (float32, or uint16 bit patterns with ``dtype``)."""
+    a = np.ascontiguousarray(logits)
+    if dtype is None:
+        if a.dtype != np.float32:
+            raise TypeError("pass float32 logits, or uint16 bit patterns with dtype=")
+        dtype = "float32"
+    elif dtype != "float32" and a.dtype != np.uint16:
+        raise TypeError("bfloat16/float16 logits are passed as uint16 bit patterns")
+    return a, DTYPE_CODES[dtype]
+
+
+def max_threads() -> int:
+    return int(_load().orc_max_threads())
+
+
+def mask_count(mask: np.ndarray, vocab: int) -> int:
+    m = np.ascontiguousarray(mask, dtype=np.int32)
+    if m.ndim != 1 or m.size != (vocab + 31) // 32:
+        raise ValueError("mask must hold ceil(vocab / 32) words")
+    return int(_load().orc_mask_count(_ptr(m), vocab))
+
+
+def reduce_rows(logits, masks, *, dtype: str | None = None, threads: int = 0):
+    """Masked argmax + valid count + status per row: (tokens, counts, status)."""
+    a, code = _logit_array(logits, dtype)
+    m = np.ascontiguousarray(masks, dtype=np.int32)
+    rows, vocab = a.shape
+    if m.shape != (rows, (vocab + 31) // 32):
+        raise ValueError("mask shape must be [rows, ceil(vocab / 32)]")
+    tokens = np.empty(rows, np.int64)
+    counts = np.empty(rows, np.int64)
+    status = np.empty(rows, np.int32)
+    if rows:
+        _load().orc_reduce_rows(_ptr(a), code, _ptr(m), rows, vocab, _ptr(tokens), _ptr(counts),
+                                _ptr(status), threads)
+    return tokens, counts, status
+
+
+def sample_rows(logits, masks, temperature: float, uniforms, *, dtype: str | None = None,
+                threads: int = 0):
+    """Inverse-CDF masked softmax sample per row with explicit uniforms: (tokens, status)."""
+    a, code = _logit_array(logits, dtype)
+    m = np.ascontiguousarray(masks, dtype=np.int32)
+    rows, vocab = a.shape
+    u = np.ascontiguousarray(uniforms, dtype=np.float64).reshape(rows)
+    tokens = np.empty(rows, np.int64)
+    status = np.empty(rows, np.int32)
+    if rows:
+        _load().orc_sample_rows(_ptr(a), code, _ptr(m), rows, vocab, float(temperature), _ptr(u),
+                                _ptr(tokens), _ptr(status), threads)
+    return tokens, status
+
+
+def fsum(values) -> float:
+    v = np.ascontiguousarray(values, dtype=np.float64)
+    return float(_load().orc_fsum(_ptr(v), v.size))
+
+
+def budget(density: float, *, kind: int = 0, low: float = 0.005, high: float = 0.02,
+           min_budget: int = 1, max_budget: int = 8) -> int:
+    return int(_load().orc_budget(kind, low, high, min_budget, max_budget, density))
+
+
+def budget_rows(counts, vocab: int, *, kind: int = 0, low: float = 0.005, high: float = 0.02,
+                min_budget: int = 1, max_budget: int = 8):
+    c = np.ascontiguousarray(counts, dtype=np.int64)
+    density = np.empty(c.size, np.float64)
+    k = np.empty(c.size, np.int32)
+    _load().orc_budget_rows(kind, low, high, min_budget, max_budget, _ptr(c), c.size, vocab,
+                            _ptr(density), _ptr(k))
+    return density, k
+
+
+def verify(row_tokens, row_status, proposals, lengths):
+    """Longest-prefix acceptance per sequence.
+
+    ``row_tokens``/``row_status`` are [S*(K+1)] per-row targets and statuses,
+    ``proposals`` is [S, K] and ``lengths`` [S].  Returns (accept_len, token,
+    kind, seq_status) with kind 0 correction, 1 bonus, 2 fallback.
+    """
+    p = np.ascontiguousarray(proposals, dtype=np.int64)
+    seqs, k = p.shape
+    t = np.ascontiguousarray(row_tokens, dtype=np.int64).reshape(seqs * (k + 1))
+    s = np.ascontiguousarray(row_status, dtype=np.int32).reshape(seqs * (k + 1))
+    ln = np.ascontiguousarray(lengths, dtype=np.int32).reshape(seqs)
+    accept = np.empty(seqs, np.int32)
+    token = np.empty(seqs, np.int64)
+    kind = np.empty(seqs, np.int32)
+    seq_status = np.empty(seqs, np.int32)
+    _load().orc_verify(_ptr(t), _ptr(s), seqs, k + 1, _ptr(p), _ptr(ln), _ptr(accept),
+                       _ptr(token), _ptr(kind), _ptr(seq_status))
+    return accept, token, kind, seq_status
+
+
+def widen(logits, dtype: str) -> np.ndarray:
+    """Exact float32 widening of float32 / bfloat16 / float16 bit patterns."""
+    a, code = _logit_array(logits, dtype)
+    out = np.empty(a.shape, np.float32)
+    _load().orc_widen(_ptr(a), code, a.size, _ptr(out))
+    return out
