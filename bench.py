@@ -1,0 +1,585 @@
+"""Benchmark of the masked-selection path on B200.
+
+Default workload (the batched verification round, 256 sequences x (K+1) = 9
+rows of bfloat16 logits at V = 248,320 per GPU): one step is one verification
+round -- the fused masked argmax + popcount kernel over all 2,304 rows plus the
+acceptance/budget epilogue -- on inputs already resident in HBM.  Other
+workloads: ``argmax`` (6 rows fp32, the reference's CPU-runnable case),
+``sample`` (8 rows fp16 at T = 0.7, rotated through enough batches to exceed
+L2) and ``scale`` (row-sharded bf16 rows).
+
+Printed JSON keys beyond the driver contract: ``roofline`` (dominant kernel's
+algorithmic bytes / its CUDA-event duration vs the measured HBM copy peak),
+``cpu_baseline`` (the CPU oracle on this host's cores), ``clocks`` (nvidia-smi
+samples during the measurement), ``gpu_launches`` and ``e2e`` (same metric
+through the public API: masks, drafts and lengths copied host->device from
+pinned memory and results read back every step; logits stay device-resident
+as the model's output, exactly as the reference's select_token receives them).
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+oracle, all host threads) on the same workload instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "bitmask-speculation_b200"))
+sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the selection kernel on the
+# verification workload (ncu capture summarised in profiles/); None until captured.
+NCU_TRAFFIC_PER_ROW = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["verify", "argmax", "sample", "scale"], default="verify")
+    ap.add_argument("--seqs", type=int, default=256, help="verification sequences per GPU")
+    ap.add_argument("--rows", type=int, default=8192, help="rows per GPU for the scale workload")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--roofline-seconds", type=float, default=1.5)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- environment
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s, p in zip(sm, power) if p >= statistics.median(power)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ---------------------------------------------------------------- workloads
+class Workload:
+    """Inputs and one step of the hot path on this rank's GPU."""
+
+    def __init__(self, args, rank, device):
+        import torch
+        from bitmask_speculation_b200 import workloads as wl
+        from bitmask_speculation_b200.kernels._extension import load_extension
+        self.args = args
+        self.device = device
+        self.native = load_extension()
+        self.kind = args.workload
+        vocab = wl.VOCAB
+        self.vocab = vocab
+        self.words = wl.words_for(vocab)
+        if self.kind == "verify":
+            self.logits, self.masks, self.proposals, self.lengths = wl.verify_batch_torch(
+                args.seqs, seed=3 + 1000 * rank, device=device)
+            self.rows = self.logits.shape[0]
+            self.batches = 1
+            self.esize = 2
+            self.dtype = "bf16"
+            from bitmask_speculation_b200.scheduling import DensityPolicy
+            self.policy = DensityPolicy().native()
+            self.name = (f"verify: {args.seqs} sequences x (K+1)=9 rows bf16 N(0,3^2) at V={vocab}; masks 40% "
+                         "enum 2-32 / 30% Bernoulli 0.05 / 30% Bernoulli 0.6; drafts geometric (0.88)")
+        elif self.kind == "argmax":
+            values, masks = wl.argmax_config_np(seed=1 + rank)
+            import numpy as np
+            reps = max(1, int(2 * L2_BYTES // values.nbytes) + 1)  # rotate > L2 of distinct batches
+            self.logits_all = torch.from_numpy(np.ascontiguousarray(np.tile(values, (reps, 1)))).to(device)
+            self.masks_all = torch.from_numpy(np.ascontiguousarray(np.tile(masks, (reps, 1)))).to(device)
+            self.rows = 6
+            self.batches = reps
+            self.esize = 4
+            self.dtype = "f32"
+            self.name = "argmax: 6 rows fp32 N(0,3^2) at V=248320 (masks .5/.5/4 valid/16 valid/.02/1 valid)"
+        elif self.kind == "sample":
+            import numpy as np
+            bits, masks, uniforms, temp = wl.sample_config_np(seed=2 + rank)
+            reps = max(1, int(2 * L2_BYTES // bits.nbytes) + 1)
+            self.logits_all = torch.from_numpy(np.tile(bits, (reps, 1)).view(np.int16)).view(torch.float16).to(device)
+            self.masks_all = torch.from_numpy(np.ascontiguousarray(np.tile(masks, (reps, 1)))).to(device)
+            self.uniforms_all = torch.from_numpy(np.tile(uniforms, reps)).to(device)
+            self.temperature = temp
+            self.rows = 8
+            self.batches = reps
+            self.esize = 2
+            self.dtype = "f16"
+            self.name = "sample: 8 rows fp16 N(0,2^2) at V=248320, T=0.7, densities {1,.5,.1,.01,1e-4,.9,.3,.05}"
+        else:
+            self.logits, self.masks = wl.scale_rows_torch(args.rows, seed=5 + 1000 * rank, device=device)
+            self.rows = args.rows
+            self.batches = 1
+            self.esize = 2
+            self.dtype = "bf16"
+            self.name = f"scale: {args.rows} rows/GPU bf16 N(0,3^2) at V=248320, log-uniform mask density"
+        self.step_index = 0
+        self._alloc_outputs()
+
+    @property
+    def bytes_per_row(self):
+        return self.vocab * self.esize + self.words * 4 + 20
+
+    def _alloc_outputs(self):
+        import torch
+        d = self.device
+        r = self.rows
+        self.row_tokens = torch.empty(r, dtype=torch.int64, device=d)
+        self.row_counts = torch.empty(r, dtype=torch.int64, device=d)
+        self.row_status = torch.empty(r, dtype=torch.int32, device=d)
+        self.row_budget = torch.empty(r, dtype=torch.int32, device=d)
+        if self.kind == "verify":
+            s = self.proposals.shape[0]
+            self.accept = torch.empty(s, dtype=torch.int32, device=d)
+            self.token = torch.empty(s, dtype=torch.int64, device=d)
+            self.kindout = torch.empty(s, dtype=torch.int32, device=d)
+            self.seq_status = torch.empty(s, dtype=torch.int32, device=d)
+
+    def _batch(self):
+        if self.batches == 1:
+            return self.logits, self.masks
+        b = self.step_index % self.batches
+        r0 = b * self.rows
+        return self.logits_all[r0:r0 + self.rows], self.masks_all[r0:r0 + self.rows]
+
+    def launches_per_step(self):
+        return 2 if self.kind == "verify" else 1
+
+    def step(self, stream_handle):
+        """One hot-path step through the C ABI on inputs resident in HBM."""
+        import ctypes
+        from bitmask_speculation_b200 import _native
+        lib = _native.library()
+        dev = self.device.index
+        logits, masks = self._batch()
+        self.step_index += 1
+        if self.kind == "verify":
+            s, k = self.proposals.shape
+            rc = lib.bms_verify_batch(
+                logits.data_ptr(), 1, masks.data_ptr(), s, k + 1, self.vocab, self.proposals.data_ptr(),
+                self.lengths.data_ptr(), ctypes.byref(self.policy), self.row_tokens.data_ptr(),
+                self.row_counts.data_ptr(), self.row_status.data_ptr(), self.row_budget.data_ptr(),
+                self.accept.data_ptr(), self.token.data_ptr(), self.kindout.data_ptr(),
+                self.seq_status.data_ptr(), dev, stream_handle)
+        elif self.kind == "sample":
+            b = (self.step_index - 1) % self.batches
+            u = self.uniforms_all[b * self.rows:(b + 1) * self.rows]
+            rc = lib.bms_masked_sample_batch(
+                logits.data_ptr(), 2, masks.data_ptr(), self.rows, self.vocab, self.temperature, u.data_ptr(),
+                self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(), dev,
+                stream_handle)
+        else:
+            code = 0 if self.kind == "argmax" else 1
+            rc = lib.bms_masked_reduce_batch(
+                logits.data_ptr(), code, masks.data_ptr(), self.rows, self.vocab, self.row_tokens.data_ptr(),
+                self.row_counts.data_ptr(), self.row_status.data_ptr(), dev, stream_handle)
+        _native.check(rc)
+
+    def kernel_only(self, stream_handle):
+        """The dominant kernel alone (fused masked argmax + count, or the sampler)."""
+        from bitmask_speculation_b200 import _native
+        lib = _native.library()
+        logits, masks = self._batch()
+        self.step_index += 1
+        if self.kind == "sample":
+            b = (self.step_index - 1) % self.batches
+            u = self.uniforms_all[b * self.rows:(b + 1) * self.rows]
+            rc = lib.bms_masked_sample_batch(
+                logits.data_ptr(), 2, masks.data_ptr(), self.rows, self.vocab, self.temperature, u.data_ptr(),
+                self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
+                self.device.index, stream_handle)
+        else:
+            code = {"f32": 0, "bf16": 1, "f16": 2}[self.dtype]
+            rc = lib.bms_masked_reduce_batch(
+                logits.data_ptr(), code, masks.data_ptr(), self.rows, self.vocab, self.row_tokens.data_ptr(),
+                self.row_counts.data_ptr(), self.row_status.data_ptr(), self.device.index, stream_handle)
+        _native.check(rc)
+
+    def check_against_oracle(self, max_rows=64):
+        """Untimed sanity check of the last step on a few rows (CPU oracle)."""
+        import numpy as np
+        import oracle
+        logits, masks = self.logits if self.batches == 1 else self.logits_all[:self.rows], \
+            self.masks if self.batches == 1 else self.masks_all[:self.rows]
+        n = min(max_rows, self.rows)
+        if self.kind in ("verify", "scale", "argmax"):
+            self.step_index = 0
+            self.kernel_only(self.stream_handle())
+            import torch
+            torch.cuda.synchronize(self.device)
+            host = logits[:n].cpu()
+            dt = {"bf16": "bfloat16", "f16": "float16", "f32": None}[self.dtype]
+            vals = host.view(torch.int16).numpy().view(np.uint16) if dt else host.numpy()
+            exp = oracle.reduce_rows(vals, masks[:n].cpu().numpy(), dtype=dt)
+            got = (self.row_tokens[:n].cpu().numpy(), self.row_counts[:n].cpu().numpy(),
+                   self.row_status[:n].cpu().numpy())
+            for g, e in zip(got, exp):
+                if not np.array_equal(g, e):
+                    raise SystemExit("benchmark output differs from the oracle")
+
+    def stream_handle(self):
+        import torch
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+
+# ---------------------------------------------------------------- e2e through the public API
+class EndToEnd:
+    """Verification through ``verification.verify_batch`` with host masks/drafts each step."""
+
+    def __init__(self, w: Workload):
+        import torch
+        self.w = w
+        if w.kind == "verify":
+            self.h_masks = w.masks.cpu().pin_memory()
+            self.h_prop = w.proposals.cpu().pin_memory()
+            self.h_len = w.lengths.cpu().pin_memory()
+            self.d_masks = torch.empty_like(w.masks)
+            self.d_prop = torch.empty_like(w.proposals)
+            self.d_len = torch.empty_like(w.lengths)
+            s = w.proposals.shape[0]
+            self.h_out = {
+                "accept_len": torch.empty(s, dtype=torch.int32).pin_memory(),
+                "token": torch.empty(s, dtype=torch.int64).pin_memory(),
+                "kind": torch.empty(s, dtype=torch.int32).pin_memory(),
+                "seq_status": torch.empty(s, dtype=torch.int32).pin_memory(),
+                "row_budget": torch.empty(w.rows, dtype=torch.int32).pin_memory(),
+            }
+            self.h2d = self.h_masks.numel() * 4 + self.h_prop.numel() * 8 + self.h_len.numel() * 4
+            self.d2h = sum(t.numel() * t.element_size() for t in self.h_out.values())
+        else:
+            logits, masks = w._batch()
+            self.h_masks = masks.cpu().pin_memory()
+            self.d_masks = torch.empty_like(masks)
+            self.h_out = {"token": torch.empty(w.rows, dtype=torch.int64).pin_memory(),
+                          "status": torch.empty(w.rows, dtype=torch.int32).pin_memory()}
+            self.h2d = self.h_masks.numel() * 4
+            self.d2h = sum(t.numel() * t.element_size() for t in self.h_out.values())
+
+    def step(self):
+        w = self.w
+        if w.kind == "verify":
+            from bitmask_speculation_b200.verification import verify_batch
+            self.d_masks.copy_(self.h_masks, non_blocking=True)
+            self.d_prop.copy_(self.h_prop, non_blocking=True)
+            self.d_len.copy_(self.h_len, non_blocking=True)
+            out = verify_batch(w.logits, self.d_masks, self.d_prop, self.d_len)
+            for k, h in self.h_out.items():
+                h.copy_(getattr(out, k), non_blocking=True)
+        else:
+            from bitmask_speculation_b200.kernels import cuda
+            logits, _ = w._batch()
+            self.d_masks.copy_(self.h_masks, non_blocking=True)
+            if w.kind == "sample":
+                import torch
+                u = torch.rand(w.rows, dtype=torch.float64, device=w.device)
+                res = cuda.batched_masked_sample(logits, self.d_masks, temperature=w.temperature, uniforms=u)
+            else:
+                res = cuda.batched_masked_reduce(logits, self.d_masks)
+            self.h_out["token"].copy_(res.token_ids, non_blocking=True)
+            self.h_out["status"].copy_(res.status, non_blocking=True)
+
+
+# ---------------------------------------------------------------- timing helpers
+def timed_loop(fn, n, device, dist=None):
+    """Device time (seconds) of n calls, events on the current stream, max over ranks."""
+    import torch
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
+    start.record(stream)
+    for _ in range(n):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    seconds = start.elapsed_time(end) / 1e3
+    if dist is not None:
+        t = torch.tensor([seconds], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        seconds = float(t.item())
+        dist.barrier()
+    return seconds
+
+
+def cpu_baseline_verify(w: Workload, budget_s=8.0):
+    """The CPU oracle (reference algorithm) on this host: reduce + verify + budgets."""
+    import numpy as np
+    import torch
+    import oracle
+    threads = oracle.max_threads()
+    host_logits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
+    host_masks = w.masks.cpu().numpy()
+    proposals = w.proposals.cpu().numpy()
+    lengths = w.lengths.cpu().numpy()
+    rows = 0
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        tok, cnt, st = oracle.reduce_rows(host_logits, host_masks, dtype="bfloat16", threads=threads)
+        oracle.verify(tok, st, proposals, lengths)
+        oracle.budget_rows(cnt, w.vocab)
+        rows += host_logits.shape[0]
+        passes += 1
+        if time.perf_counter() - t0 >= budget_s or passes >= 50:
+            break
+    elapsed = time.perf_counter() - t0
+    return rows / elapsed, threads, f"{passes} full verification rounds ({host_logits.shape[0]} rows each)"
+
+
+def cpu_baseline_rows(w: Workload, budget_s=8.0):
+    import numpy as np
+    import torch
+    import oracle
+    threads = oracle.max_threads()
+    logits, masks = w._batch()
+    if w.dtype == "f32":
+        vals, dt = logits.cpu().numpy(), None
+    else:
+        vals = logits.cpu().view(torch.int16).numpy().view(np.uint16)
+        dt = "float16" if w.dtype == "f16" else "bfloat16"
+    m = masks.cpu().numpy()
+    rows, passes = 0, 0
+    t0 = time.perf_counter()
+    while True:
+        if w.kind == "sample":
+            oracle.sample_rows(vals, m, w.temperature, np.random.default_rng(passes).random(w.rows), dtype=dt,
+                               threads=threads)
+        else:
+            oracle.reduce_rows(vals, m, dtype=dt, threads=threads)
+        rows += w.rows
+        passes += 1
+        if time.perf_counter() - t0 >= budget_s or passes >= 2000:
+            break
+    return rows / (time.perf_counter() - t0), threads, f"{passes} batches of {w.rows} rows"
+
+
+# ---------------------------------------------------------------- arms
+def run_reference_arm(args):
+    """The reference algorithm on the host cores (oracle port, all threads), rank 0 only."""
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    import torch
+    import numpy as np
+    import oracle
+    device = torch.device("cuda", local) if torch.cuda.is_available() else None
+    if device is not None:
+        torch.cuda.set_device(device)
+    threads = oracle.max_threads()
+    w = Workload(args, 0, device)
+    if args.workload == "verify":
+        host_logits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
+        host_masks = w.masks.cpu().numpy()
+        props, lens = w.proposals.cpu().numpy(), w.lengths.cpu().numpy()
+
+        def step():
+            tok, cnt, st = oracle.reduce_rows(host_logits, host_masks, dtype="bfloat16", threads=threads)
+            oracle.verify(tok, st, props, lens)
+            oracle.budget_rows(cnt, w.vocab)
+        rows_per_step = host_logits.shape[0]
+        sample = f"full verification round ({rows_per_step} rows) per step"
+    else:
+        logits, masks = w._batch()
+        dt = {"f32": None, "bf16": "bfloat16", "f16": "float16"}[w.dtype]
+        vals = logits.cpu().numpy() if dt is None else logits.cpu().view(torch.int16).numpy().view(np.uint16)
+        m = masks.cpu().numpy()
+
+        def step():
+            if w.kind == "sample":
+                oracle.sample_rows(vals, m, w.temperature, np.random.default_rng(0).random(w.rows), dtype=dt,
+                                   threads=threads)
+            else:
+                oracle.reduce_rows(vals, m, dtype=dt, threads=threads)
+        rows_per_step = w.rows
+        sample = f"{rows_per_step} rows per step"
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - t0
+    value = rows_per_step * args.steps / elapsed
+    line = {
+        "impl": "reference", "metric": "rows/s", "value": value, "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic (seeded)", "config": {"workload": w.name, "rows_per_step": rows_per_step},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200_arm(args):
+    import torch
+    rank, world, local = dist_env()
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist_mod
+        torch.cuda.set_device(local)
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        dist = dist_mod
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = Workload(args, rank, device)
+    torch.cuda.synchronize(device)
+    w.check_against_oracle()
+    stream = w.stream_handle()
+    peak, peak_kind = measured_peak()
+
+    with ClockSampler(local) as clocks:
+        for _ in range(max(3, args.warmup)):
+            w.step(stream)
+        torch.cuda.synchronize(device)
+        torch.cuda.nvtx.range_push("timed")
+        seconds = timed_loop(lambda: w.step(stream), args.steps, device, dist)
+        torch.cuda.nvtx.range_pop()
+        # Dominant kernel alone, long enough (>= roofline_seconds) for the clock samples.
+        probe = timed_loop(lambda: w.kernel_only(stream), 3, device)
+        reps = max(args.steps, int(args.roofline_seconds / max(probe / 3, 1e-6)))
+        torch.cuda.nvtx.range_push("roofline")
+        ktime = timed_loop(lambda: w.kernel_only(stream), reps, device)
+        torch.cuda.nvtx.range_pop()
+        e2e = None
+        if not args.no_e2e:
+            e = EndToEnd(w)
+            for _ in range(3):
+                e.step()
+            torch.cuda.synchronize(device)
+            if dist is not None:
+                dist.barrier()
+            t0 = time.perf_counter()
+            etime = timed_loop(e.step, args.steps, device, dist)
+            wall = time.perf_counter() - t0
+            e2e = {"value": w.rows * world * args.steps / etime, "unit": "rows/s",
+                   "h2d_bytes_per_step": e.h2d, "d2h_bytes_per_step": e.d2h,
+                   "wall_value": w.rows * world * args.steps / wall,
+                   "path": ("verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
+                            "device-resident logits, results D2H every step")}
+
+    value = w.rows * world * args.steps / seconds
+    bytes_per_launch = w.rows * w.bytes_per_row
+    kernel_s = ktime / reps
+    achieved = bytes_per_launch / kernel_s / 1e9
+    traffic = None if NCU_TRAFFIC_PER_ROW is None else NCU_TRAFFIC_PER_ROW * w.rows
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "rows/s", "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": w.name, "rows_per_gpu": w.rows, "vocab": w.vocab,
+                   "bytes_per_row": w.bytes_per_row,
+                   "l2": (f"inputs {w.rows * w.bytes_per_row * w.batches / 1e9:.2f} GB per GPU rotated "
+                          f"({w.batches} batch(es)) > 126 MB L2; no flush"),
+                   "parallelism": f"row-sharded x{world}, no collective"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "select_rows_kernel (masked argmax + count)" if w.kind != "sample"
+                     else "select_rows_kernel (masked sampler)",
+                     "kernel_us": kernel_s * 1e6, "bytes_per_launch": bytes_per_launch},
+        "gpu_launches": args.steps * w.launches_per_step(),
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if not args.no_cpu_baseline and world == 1:
+        if w.kind == "verify":
+            v, cores, sample = cpu_baseline_verify(w)
+        else:
+            v, cores, sample = cpu_baseline_rows(w)
+        line["cpu_baseline"] = {"value": v, "unit": "rows/s", "cores": cores, "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_b200_arm(args)
+
+
+if __name__ == "__main__":
+    main()

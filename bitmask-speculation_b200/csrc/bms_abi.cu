@@ -1,0 +1,535 @@
+// C-ABI entry points (include/bms_b200.h) and launch configuration.
+//
+// The library is a plain shared object built by nvcc for sm_100a; it links the
+// CUDA runtime and nothing else, takes raw device pointers and a cudaStream_t,
+// and allocates no memory.  Launch choices:
+//  * rows whose logits and masks start on 16-byte boundaries stream through the
+//    bulk-copy (TMA) pipeline; other rows use the plain-load variant of the same
+//    kernel;
+//  * the cluster size C (CTAs sharing one row) and the number of persistent
+//    clusters are chosen from the device's occupancy so that the slowest CTA
+//    streams as few chunks as possible: many rows -> C = 1 with every SM busy,
+//    few rows -> up to 16 CTAs per row merging through distributed shared memory.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/bms_b200.h"
+#include "select.cuh"
+
+namespace bms {
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_error, sizeof g_error, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    cudaGetLastError();  // clear a non-sticky error so later calls start clean
+    return fail(BMS_ERROR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define BMS_CUDA(call, what)                                  \
+    do {                                                      \
+        const cudaError_t e_ = (call);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_, (what));  \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1, want = -1;
+    cudaError_t enter(int device) {
+        want = device;
+        cudaError_t e = cudaGetDevice(&prev);
+        if (e != cudaSuccess) return e;
+        if (prev != device) return cudaSetDevice(device);
+        return cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0 && prev != want) cudaSetDevice(prev);
+    }
+};
+
+int check_device(int device) {
+    int n = 0;
+    BMS_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(BMS_ERROR_INVALID_ARGUMENT, "invalid CUDA device %d", device);
+    return BMS_SUCCESS;
+}
+
+// Every pointer the kernels touch must be device (or managed) memory of `device`.
+int check_ptr(const void* p, int device, const char* name, size_t align) {
+    if (p == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "%s must not be NULL", name);
+    if (reinterpret_cast<uintptr_t>(p) % align != 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "%s must be %zu-byte aligned", name, align);
+    cudaPointerAttributes a;
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "%s is not a CUDA pointer", name);
+    }
+    if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "%s must be CUDA device memory", name);
+    if (a.device != device)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "%s is on device %d, expected device %d", name, a.device, device);
+    return BMS_SUCCESS;
+}
+
+#define BMS_CHECK(expr)                      \
+    do {                                     \
+        const int rc_ = (expr);              \
+        if (rc_ != BMS_SUCCESS) return rc_;  \
+    } while (0)
+
+int elem_bytes(int dtype) { return dtype == BMS_FLOAT32 ? 4 : 2; }
+
+int check_dtype(int dtype) {
+    if (dtype != BMS_FLOAT32 && dtype != BMS_BFLOAT16 && dtype != BMS_FLOAT16)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "logits must be float32, bfloat16 or float16 (dtype code %d)", dtype);
+    return BMS_SUCCESS;
+}
+
+int check_vocab(int64_t vocab) {
+    if (vocab <= 0 || vocab > 2147483647LL) return fail(BMS_ERROR_INVALID_ARGUMENT, "invalid vocabulary size");
+    return BMS_SUCCESS;
+}
+
+// ---------------------------------------------------------------- launch override (tests)
+int g_force_cluster = 0;
+int g_force_clusters = 0;
+
+// ---------------------------------------------------------------- per-device kernel setup
+constexpr int kMaxDevices = 64;
+constexpr int kClusterSizes[] = {1, 2, 4, 8, 16};
+
+struct KernelInfo {
+    bool ready = false;
+    int sms = 0;
+    int max_clusters[5] = {0, 0, 0, 0, 0};  // resident clusters for each cluster size
+};
+
+std::mutex g_mutex;
+
+template <typename T, bool kSample, bool kBulk, int kStages>
+int kernel_info(int device, KernelInfo*& out) {
+    static KernelInfo table[kMaxDevices];
+    std::lock_guard<std::mutex> lock(g_mutex);
+    KernelInfo& info = table[device];
+    if (!info.ready) {
+        auto kernel = select_rows_kernel<T, kSample, kBulk, kStages>;
+        const size_t smem = select_smem_bytes<T, kSample>(kStages);
+        BMS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                 "cudaFuncSetAttribute(smem)");
+        BMS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                 "cudaFuncSetAttribute(cluster)");
+        BMS_CUDA(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+        for (int i = 0; i < 5; ++i) {
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = kClusterSizes[i];
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.gridDim = dim3(kClusterSizes[i] * info.sms);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+            info.max_clusters[i] = n;
+        }
+        if (info.max_clusters[0] <= 0) return fail(BMS_ERROR_CUDA, "selection kernel cannot be resident on device %d", device);
+        info.ready = true;
+    }
+    out = &info;
+    return BMS_SUCCESS;
+}
+
+struct Plan {
+    int cluster;
+    int clusters;
+    int64_t segment;
+};
+
+// Choose the cluster size that minimises the chunks streamed by the busiest CTA.
+Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens_per_chunk, int max_chunks) {
+    Plan best{0, 0, 0};
+    double best_cost = 0.0;
+    for (int i = 0; i < 5; ++i) {
+        const int c = kClusterSizes[i];
+        if (g_force_cluster && c != g_force_cluster) continue;
+        const int resident = info.max_clusters[i];
+        if (resident <= 0) continue;
+        const int64_t seg = ((vocab + c - 1) / c + 31) / 32 * 32;
+        const int64_t chunks = (seg + tokens_per_chunk - 1) / tokens_per_chunk;
+        if (max_chunks > 0 && chunks > max_chunks) continue;
+        int64_t clusters = rows < resident ? rows : resident;
+        if (g_force_clusters) clusters = g_force_clusters < rows ? g_force_clusters : rows;
+        const int64_t waves = (rows + clusters - 1) / clusters;
+        const double overhead = c == 1 ? 0.25 : 0.6;  // per-row merge cost, in chunk units
+        const double cost = static_cast<double>(waves) * (static_cast<double>(chunks) + overhead);
+        if (best.cluster == 0 || cost < best_cost - 1e-9) {
+            best = Plan{c, static_cast<int>(clusters), seg};
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+template <typename T, bool kSample, bool kBulk, int kStages>
+int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
+    KernelInfo* info = nullptr;
+    BMS_CHECK((kernel_info<T, kSample, kBulk, kStages>(device, info)));
+    const Plan plan = plan_launch(*info, p.rows, p.vocab, Layout<T>::kTokensPerChunk, kSample ? kMaxChunksSampler : 0);
+    if (plan.cluster == 0)
+        return fail(BMS_ERROR_UNSUPPORTED, "vocabulary of %lld tokens exceeds the %s limit", static_cast<long long>(p.vocab),
+                    kSample ? "sampler" : "selection");
+    p.segment = plan.segment;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = plan.cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.cluster * plan.clusters));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    BMS_CUDA(cudaLaunchKernelEx(&cfg, select_rows_kernel<T, kSample, kBulk, kStages>, p), "selection launch");
+    return BMS_SUCCESS;
+}
+
+constexpr int kBulkStages = 4;
+
+template <typename T, bool kSample>
+int launch_select_dtype(SelectParams p, int device, cudaStream_t stream) {
+    const int eb = sizeof(T);
+    const bool bulk = reinterpret_cast<uintptr_t>(p.logits) % 16 == 0 && reinterpret_cast<uintptr_t>(p.masks) % 16 == 0 &&
+                      (p.vocab * eb) % 16 == 0 && (p.logit_stride * eb) % 16 == 0 && p.mask_stride % 4 == 0;
+    if (bulk) return launch_select_t<T, kSample, true, kBulkStages>(p, device, stream);
+    return launch_select_t<T, kSample, false, 1>(p, device, stream);
+}
+
+template <bool kSample>
+int launch_select(int dtype, const SelectParams& p, int device, cudaStream_t stream) {
+    if (p.rows == 0) return BMS_SUCCESS;
+    switch (dtype) {
+        case BMS_FLOAT32: return launch_select_dtype<float, kSample>(p, device, stream);
+        case BMS_BFLOAT16: return launch_select_dtype<__nv_bfloat16, kSample>(p, device, stream);
+        default: return launch_select_dtype<__half, kSample>(p, device, stream);
+    }
+}
+
+// ---------------------------------------------------------------- popcount / density / budget
+__device__ int32_t policy_budget(const bms_policy& P, double d) {
+    if (P.kind == 0) {
+        if (d < P.low_density) return P.max_budget;
+        if (d < P.high_density) return (P.min_budget + P.max_budget) / 2;
+        return P.min_budget;
+    }
+    if (d < P.low_density) return P.max_budget;
+    if (d > P.high_density) return P.min_budget;
+    const double span = static_cast<double>(P.max_budget - P.min_budget);
+    const double frac = __ddiv_rn(__dsub_rn(d, P.low_density), __dsub_rn(P.high_density, P.low_density));
+    return P.max_budget - static_cast<int32_t>(floor(__dmul_rn(span, frac)));
+}
+
+// One CTA per row (grid-stride): popcount with the padding bits of the last word cleared.
+__global__ void __launch_bounds__(256) count_rows_kernel(const int32_t* __restrict__ masks, int64_t rows, int64_t vocab,
+                                                         bms_policy policy, int64_t* __restrict__ counts,
+                                                         double* __restrict__ density, int32_t* __restrict__ budget) {
+    __shared__ uint32_t part[8];
+    const int64_t words = (vocab + 31) / 32;
+    const int tail = static_cast<int>(vocab % 32);
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const int32_t* m = masks + row * words;
+        uint32_t c = 0;
+        for (int64_t w = threadIdx.x; w < words; w += blockDim.x) {
+            uint32_t bits = static_cast<uint32_t>(m[w]);
+            if (w == words - 1 && tail != 0) bits &= (1u << tail) - 1u;
+            c += __popc(bits);
+        }
+        c = __reduce_add_sync(0xFFFFFFFFu, c);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t total = 0;
+            for (int i = 0; i < 8; ++i) total += part[i];
+            if (counts) counts[row] = total;
+            const double d = __ddiv_rn(static_cast<double>(total), static_cast<double>(vocab));
+            if (density) density[row] = d;
+            if (budget) budget[row] = policy_budget(policy, d);
+        }
+        __syncthreads();
+    }
+}
+
+// Longest-prefix acceptance per sequence plus the per-row budgets.
+__global__ void __launch_bounds__(256) verify_epilogue_kernel(
+    const int64_t* __restrict__ row_tokens, const int64_t* __restrict__ row_counts, const int32_t* __restrict__ row_status,
+    int64_t seqs, int64_t rows_per_seq, int64_t vocab, const int64_t* __restrict__ proposals,
+    const int32_t* __restrict__ lengths, bms_policy policy, int32_t* __restrict__ row_budget,
+    int32_t* __restrict__ accept_len, int64_t* __restrict__ token, int32_t* __restrict__ kind,
+    int32_t* __restrict__ seq_status) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (row_budget != nullptr && row_counts != nullptr) {
+        for (int64_t r = first; r < seqs * rows_per_seq; r += stride)
+            row_budget[r] = policy_budget(policy, __ddiv_rn(static_cast<double>(row_counts[r]), static_cast<double>(vocab)));
+    }
+    const int64_t k_max = rows_per_seq - 1;
+    for (int64_t s = first; s < seqs; s += stride) {
+        const int64_t* tok = row_tokens + s * rows_per_seq;
+        const int32_t* st = row_status + s * rows_per_seq;
+        const int64_t* prop = proposals + s * k_max;
+        const int32_t len = lengths[s];
+        int32_t a = 0, kd = 0, ss = 0;
+        int64_t tk = -1;
+        if (len < 0 || len > k_max) {
+            ss = kBadLength;
+        } else {
+            for (int32_t i = 0;; ++i) {
+                if (st[i] != 0) {  // a consumed row failed: the reference raises here
+                    a = i;
+                    ss = st[i];
+                    break;
+                }
+                if (i == len) {  // every proposal matched: bonus (or fallback without proposals)
+                    a = len;
+                    tk = tok[i];
+                    kd = len > 0 ? 1 : 2;
+                    break;
+                }
+                if (tok[i] != prop[i]) {  // first mismatch: the target's token corrects it
+                    a = i;
+                    tk = tok[i];
+                    kd = 0;
+                    break;
+                }
+            }
+        }
+        accept_len[s] = a;
+        token[s] = tk;
+        kind[s] = kd;
+        seq_status[s] = ss;
+    }
+}
+
+int check_policy(const bms_policy* policy) {
+    if (policy == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "policy must not be NULL when budgets are requested");
+    const bms_policy& P = *policy;
+    if (P.kind != 0 && P.kind != 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "unknown policy kind %d", P.kind);
+    if (!(std::isfinite(P.low_density) && std::isfinite(P.high_density)) || P.low_density < 0 || P.high_density > 1 ||
+        !(P.low_density < P.high_density))
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "density thresholds must be finite, within [0, 1] and increasing");
+    if (P.min_budget < 1 || P.max_budget < P.min_budget)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "budgets must satisfy 1 <= min_budget <= max_budget");
+    return BMS_SUCCESS;
+}
+
+int sm_count(int device) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    return n;
+}
+
+int select_common(int dtype, const void* logits, const int32_t* masks, int64_t rows, int64_t vocab, int device) {
+    BMS_CHECK(check_dtype(dtype));
+    BMS_CHECK(check_vocab(vocab));
+    if (rows < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows must be nonnegative");
+    BMS_CHECK(check_device(device));
+    if (rows == 0) return BMS_SUCCESS;
+    BMS_CHECK(check_ptr(logits, device, "logits", static_cast<size_t>(elem_bytes(dtype))));
+    BMS_CHECK(check_ptr(masks, device, "masks", 4));
+    return BMS_SUCCESS;
+}
+
+SelectParams base_params(const void* logits, const int32_t* masks, int64_t rows, int64_t vocab) {
+    SelectParams p = {};
+    p.logits = logits;
+    p.masks = masks;
+    p.rows = rows;
+    p.vocab = vocab;
+    p.logit_stride = vocab;
+    p.mask_stride = (vocab + 31) / 32;
+    p.token_offset = 0;
+    return p;
+}
+
+}  // namespace
+}  // namespace bms
+
+using namespace bms;
+
+extern "C" {
+
+const char* bms_last_error(void) { return g_error; }
+
+int bms_runtime_version(int32_t* version) {
+    if (version == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "version must not be NULL");
+    int v = 0;
+    BMS_CUDA(cudaRuntimeGetVersion(&v), "cudaRuntimeGetVersion");
+    *version = v;
+    return BMS_SUCCESS;
+}
+
+int bms_set_launch_override(int32_t cluster, int32_t clusters) {
+    if (cluster != 0 && cluster != 1 && cluster != 2 && cluster != 4 && cluster != 8 && cluster != 16)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "cluster override must be 0, 1, 2, 4, 8 or 16");
+    if (clusters < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "clusters override must be nonnegative");
+    g_force_cluster = cluster;
+    g_force_clusters = clusters;
+    return BMS_SUCCESS;
+}
+
+int bms_masked_reduce_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t rows, int64_t vocab,
+                            int64_t* tokens, int64_t* counts, int32_t* status, int32_t device, void* stream) {
+    BMS_CHECK(select_common(dtype, logits, masks, rows, vocab, device));
+    if (rows == 0) return BMS_SUCCESS;
+    BMS_CHECK(check_ptr(tokens, device, "tokens", 8));
+    if (counts) BMS_CHECK(check_ptr(counts, device, "counts", 8));
+    BMS_CHECK(check_ptr(status, device, "status", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    SelectParams p = base_params(logits, masks, rows, vocab);
+    p.tokens = tokens;
+    p.counts = counts;
+    p.status = status;
+    return launch_select<false>(dtype, p, device, static_cast<cudaStream_t>(stream));
+}
+
+int bms_masked_argmax(const void* logits, int32_t dtype, const int32_t* mask, int64_t vocab, int64_t* token,
+                      int32_t* status, int32_t device, void* stream) {
+    return bms_masked_reduce_batch(logits, dtype, mask, 1, vocab, token, nullptr, status, device, stream);
+}
+
+int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t rows, int64_t vocab,
+                            double temperature, const double* uniforms, int64_t* tokens, int64_t* counts,
+                            int32_t* status, int32_t device, void* stream) {
+    if (!std::isfinite(temperature) || temperature < 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "temperature must be finite and nonnegative");
+    if (temperature == 0)  // csrc/sample.cu:120: zero temperature is the masked argmax
+        return bms_masked_reduce_batch(logits, dtype, masks, rows, vocab, tokens, counts, status, device, stream);
+    BMS_CHECK(select_common(dtype, logits, masks, rows, vocab, device));
+    if (rows == 0) return BMS_SUCCESS;
+    BMS_CHECK(check_ptr(uniforms, device, "uniforms", 8));
+    BMS_CHECK(check_ptr(tokens, device, "tokens", 8));
+    if (counts) BMS_CHECK(check_ptr(counts, device, "counts", 8));
+    BMS_CHECK(check_ptr(status, device, "status", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    SelectParams p = base_params(logits, masks, rows, vocab);
+    p.tokens = tokens;
+    p.counts = counts;
+    p.status = status;
+    p.uniforms = uniforms;
+    p.temperature = temperature;
+    // 2*log2(e)/T in float; +inf for tiny T, clamped to the smallest denormal for huge T so
+    // that -inf logits still map to zero weight.
+    const double sc = 2.0 * 1.4426950408889634 / temperature;
+    float scf = static_cast<float>(sc);
+    const float tiny = 1.40129846e-45f;
+    if (!(scf >= tiny)) scf = tiny;
+    p.scale2 = scf;
+    return launch_select<true>(dtype, p, device, static_cast<cudaStream_t>(stream));
+}
+
+int bms_masked_sample(const void* logits, int32_t dtype, const int32_t* mask, int64_t vocab, double temperature,
+                      const double* uniform, int64_t* token, int32_t* status, int32_t device, void* stream) {
+    return bms_masked_sample_batch(logits, dtype, mask, 1, vocab, temperature, uniform, token, nullptr, status, device,
+                                   stream);
+}
+
+int bms_mask_budget(const int32_t* masks, int64_t rows, int64_t vocab, const bms_policy* policy, int64_t* counts,
+                    double* density, int32_t* budget, int32_t device, void* stream) {
+    BMS_CHECK(check_vocab(vocab));
+    if (rows < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows must be nonnegative");
+    bms_policy P = {0, 1, 8, 0, 0.005, 0.02};
+    if (budget) {
+        BMS_CHECK(check_policy(policy));
+        P = *policy;
+    }
+    BMS_CHECK(check_device(device));
+    if (rows == 0) return BMS_SUCCESS;
+    BMS_CHECK(check_ptr(masks, device, "masks", 4));
+    if (counts) BMS_CHECK(check_ptr(counts, device, "counts", 8));
+    if (density) BMS_CHECK(check_ptr(density, device, "density", 8));
+    if (budget) BMS_CHECK(check_ptr(budget, device, "budget", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
+    const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+    count_rows_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(masks, rows, vocab, P, counts, density, budget);
+    BMS_CUDA(cudaGetLastError(), "popcount launch");
+    return BMS_SUCCESS;
+}
+
+int bms_mask_count(const int32_t* mask, int64_t vocab, int64_t* count, int32_t device, void* stream) {
+    if (count == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "count must not be NULL");
+    return bms_mask_budget(mask, 1, vocab, nullptr, count, nullptr, nullptr, device, stream);
+}
+
+int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t seqs, int64_t rows_per_seq,
+                     int64_t vocab, const int64_t* proposals, const int32_t* lengths, const bms_policy* policy,
+                     int64_t* row_tokens, int64_t* row_counts, int32_t* row_status, int32_t* row_budget,
+                     int32_t* accept_len, int64_t* token, int32_t* kind, int32_t* seq_status, int32_t device,
+                     void* stream) {
+    if (seqs < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "seqs must be nonnegative");
+    if (rows_per_seq < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows_per_seq must be at least 1");
+    if (seqs > INT64_MAX / rows_per_seq) return fail(BMS_ERROR_INVALID_ARGUMENT, "batch too large");
+    bms_policy P = {0, 1, 8, 0, 0.005, 0.02};
+    if (row_budget) {
+        if (row_counts == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "row_budget requires row_counts");
+        BMS_CHECK(check_policy(policy));
+        P = *policy;
+    }
+    const int64_t rows = seqs * rows_per_seq;
+    BMS_CHECK(select_common(dtype, logits, masks, rows, vocab, device));
+    if (seqs == 0) return BMS_SUCCESS;
+    if (rows_per_seq > 1) BMS_CHECK(check_ptr(proposals, device, "proposals", 8));
+    BMS_CHECK(check_ptr(lengths, device, "lengths", 4));
+    BMS_CHECK(check_ptr(row_tokens, device, "row_tokens", 8));
+    if (row_counts) BMS_CHECK(check_ptr(row_counts, device, "row_counts", 8));
+    BMS_CHECK(check_ptr(row_status, device, "row_status", 4));
+    if (row_budget) BMS_CHECK(check_ptr(row_budget, device, "row_budget", 4));
+    BMS_CHECK(check_ptr(accept_len, device, "accept_len", 4));
+    BMS_CHECK(check_ptr(token, device, "token", 8));
+    BMS_CHECK(check_ptr(kind, device, "kind", 4));
+    BMS_CHECK(check_ptr(seq_status, device, "seq_status", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    SelectParams p = base_params(logits, masks, rows, vocab);
+    p.tokens = row_tokens;
+    p.counts = row_counts;
+    p.status = row_status;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    BMS_CHECK(launch_select<false>(dtype, p, device, s));
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 4;
+    const int64_t need = (rows + 255) / 256;
+    const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+    verify_epilogue_kernel<<<grid, 256, 0, s>>>(row_tokens, row_counts, row_status, seqs, rows_per_seq, vocab,
+                                                proposals, lengths, P, row_budget, accept_len, token, kind, seq_status);
+    BMS_CUDA(cudaGetLastError(), "verification epilogue launch");
+    return BMS_SUCCESS;
+}
+
+}  // extern "C"

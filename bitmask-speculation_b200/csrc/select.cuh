@@ -1,0 +1,780 @@
+// Masked selection over packed grammar masks: one persistent streaming kernel
+// for (a) fused masked argmax + valid count + NaN status and (b) masked
+// online-softmax sampling by inverse CDF.
+//
+// Semantics follow the reference implementation of karthikeyansura/bitmask-
+// speculation: csrc/reduce.cuh:19-62 (larger value wins, ties go to the lower
+// token ID, NaN anywhere in the row fails it, padding bits of the last word are
+// ignored), csrc/argmax.cu:77-98 (status 0 ok, 1 no valid token, 2 NaN; token -1
+// on error) and csrc/sample.cu:24-112 / kernels/reference.py:10-52 (weights
+// exp((x - max) / T), first token whose running mass exceeds u * total, status
+// 3 bad uniform, 4 no finite mass, 5 valid +inf).
+//
+// Structure (B200 / sm_100a):
+//  * A cluster of C CTAs owns one row at a time; CTA rank r streams tokens
+//    [r*L, (r+1)*L) of the row.  Clusters loop over rows (persistent grid).
+//  * One producer warp moves 16 KB chunks of logits plus their mask words from
+//    HBM into a ring of shared-memory stages with 1-D bulk copies (TMA engine)
+//    completing on mbarriers; eight consumer warps reduce them.  Rows whose
+//    addresses are not 16-byte aligned use the same kernel with the consumer
+//    warps loading the chunk themselves (kBulk = false).
+//  * Consumer warp w of a chunk owns a contiguous 2 KB slice; each lane reads
+//    16-byte vectors and the mask bits covering them from shared memory.
+//  * Per-row partials are merged warp -> CTA with redux.sync and named
+//    barriers, then across the cluster by an all-gather through distributed
+//    shared memory (st.shared::cluster + remote mbarrier arrive).  Argmax keys
+//    are (order-preserving float bits << 32 | ~index), so the merge is a max.
+//  * The sampler records one (max, mass) pair per (chunk, warp) "granule" in
+//    shared memory during the single streaming pass (fp32 MUFU ex2 weights),
+//    merges ranks in fixed order in fp64, then re-reads only the granule that
+//    holds u * total and walks it with exact fp64 weights exp((x - M) / T).
+//  * Every wait is bounded (about one second, %globaltimer); on expiry the CTA
+//    stops waiting, reports status 7 for its rows and still completes the
+//    cluster protocol, so no wait can hang the GPU.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace bms {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
+constexpr int kChunkBytes = 16384;               // logits bytes per stage
+constexpr int kWarpBytes = kChunkBytes / kConsumerWarps;
+constexpr int kVecsPerLane = kWarpBytes / 16 / 32;  // 16-byte vectors per lane per chunk
+constexpr int kMaxCluster = 16;
+constexpr int kMaxChunksSampler = 128;  // granule table capacity (chunks per segment)
+constexpr uint64_t kTimeoutNs = 1000000000ull;
+
+enum Status : int32_t {
+    kOk = 0,
+    kEmpty = 1,
+    kNaN = 2,
+    kBadUniform = 3,
+    kNoMass = 4,
+    kPosInf = 5,
+    kBadLength = 6,
+    kTimeout = 7,
+};
+
+enum Flags : uint32_t { kFlagNaN = 1u, kFlagAbort = 2u };
+
+// ----------------------------------------------------------------- dtypes
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+    static constexpr int kBytes = 4;
+    static constexpr int kVec = 4;  // tokens per 16-byte vector
+    using NanAcc = float;
+    __device__ static NanAcc nan_init() { return 0.0f; }
+    __device__ static void decode(const uint4& r, float (&v)[kVec]) {
+        v[0] = __uint_as_float(r.x);
+        v[1] = __uint_as_float(r.y);
+        v[2] = __uint_as_float(r.z);
+        v[3] = __uint_as_float(r.w);
+    }
+    __device__ static void nan_update(NanAcc& a, const uint4& r) {
+        a = ptx::max_nan(a, ptx::max_nan(ptx::max_nan(__uint_as_float(r.x), __uint_as_float(r.y)),
+                                         ptx::max_nan(__uint_as_float(r.z), __uint_as_float(r.w))));
+    }
+    __device__ static bool has_nan(NanAcc a) { return a != a; }
+    __device__ static float load(const void* p, int64_t i) { return static_cast<const float*>(p)[i]; }
+    __device__ static uint32_t raw(const void* p, int64_t i) { return static_cast<const uint32_t*>(p)[i]; }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+    static constexpr int kBytes = 2;
+    static constexpr int kVec = 8;
+    using NanAcc = uint32_t;  // two packed bf16 maxima
+    __device__ static NanAcc nan_init() { return 0u; }
+    __device__ static void decode(const uint4& r, float (&v)[kVec]) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    }
+    __device__ static void nan_update(NanAcc& a, const uint4& r) {
+        a = ptx::max_nan_bf16x2(a, ptx::max_nan_bf16x2(ptx::max_nan_bf16x2(r.x, r.y), ptx::max_nan_bf16x2(r.z, r.w)));
+    }
+    __device__ static bool has_nan(NanAcc a) { return (a & 0x7FFFu) > 0x7F80u || ((a >> 16) & 0x7FFFu) > 0x7F80u; }
+    __device__ static float load(const void* p, int64_t i) {
+        return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(p)[i]) << 16);
+    }
+    __device__ static uint32_t raw(const void* p, int64_t i) { return static_cast<const uint16_t*>(p)[i]; }
+};
+
+template <>
+struct Elem<__half> {
+    static constexpr int kBytes = 2;
+    static constexpr int kVec = 8;
+    using NanAcc = uint32_t;  // two packed fp16 maxima
+    __device__ static NanAcc nan_init() { return 0u; }
+    __device__ static void decode(const uint4& r, float (&v)[kVec]) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 h;
+            memcpy(&h, &w[i], 4);
+            const float2 f = __half22float2(h);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+    __device__ static void nan_update(NanAcc& a, const uint4& r) {
+        a = ptx::max_nan_f16x2(a, ptx::max_nan_f16x2(ptx::max_nan_f16x2(r.x, r.y), ptx::max_nan_f16x2(r.z, r.w)));
+    }
+    __device__ static bool has_nan(NanAcc a) { return (a & 0x7FFFu) > 0x7C00u || ((a >> 16) & 0x7FFFu) > 0x7C00u; }
+    __device__ static float load(const void* p, int64_t i) {
+        return __half2float(static_cast<const __half*>(p)[i]);
+    }
+    __device__ static uint32_t raw(const void* p, int64_t i) { return static_cast<const uint16_t*>(p)[i]; }
+};
+
+// ----------------------------------------------------------------- params
+struct SelectParams {
+    const void* logits;      // [rows, logit_stride] elements
+    const int32_t* masks;    // [rows, mask_stride] words
+    int64_t rows;
+    int64_t vocab;           // tokens per row
+    int64_t logit_stride;    // elements between rows
+    int64_t mask_stride;     // words between rows
+    int64_t segment;         // tokens per cluster rank, multiple of 32
+    int64_t token_offset;    // added to reported token ids (vocabulary shards)
+    int64_t* tokens;         // [rows] selected token, -1 on error
+    int64_t* counts;         // [rows] valid-token count (nullable)
+    int32_t* status;         // [rows]
+    // sampler
+    const double* uniforms;  // [rows]
+    double temperature;
+    float scale2;            // 2 * log2(e) / T as float, clamped to >= the smallest denormal
+};
+
+// Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).
+__device__ __forceinline__ uint32_t ordered_bits(float v) {
+    v = v + 0.0f;  // -0.0 + 0.0 == +0.0
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float ordered_to_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// ----------------------------------------------------------------- shared memory
+template <typename T>
+struct Layout {
+    static constexpr int kTokensPerChunk = kChunkBytes / Elem<T>::kBytes;
+    static constexpr int kTokensPerWarp = kTokensPerChunk / kConsumerWarps;
+    static constexpr int kMaskWords = kTokensPerChunk / 32 + 4;  // + misalignment slack
+    static constexpr int kMaskBytes = ((kMaskWords * 4) + 15) / 16 * 16;
+    static constexpr int kStageBytes = kChunkBytes + kMaskBytes;
+};
+
+struct alignas(16) GatherSlot {
+    uint32_t a, b, c, d;  // argmax: key_hi, key_lo, count, flags | sampler: M bits, count, flags, 0
+    double s;             // sampler: segment mass relative to M
+    double pad;
+};
+
+struct alignas(16) Shared {
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t gather[2];
+    GatherSlot slots[2][kMaxCluster];
+    uint32_t warp_key_hi[kConsumerWarps];
+    uint32_t warp_key_lo[kConsumerWarps];
+    uint32_t warp_count[kConsumerWarps];
+    uint32_t warp_flags[kConsumerWarps];
+    uint32_t warp_m[kConsumerWarps];   // sampler: warp running max (ordered bits)
+    double scan[kConsumerThreads / 32 + 1];
+    double bcast_d[4];
+    int32_t bcast_i[4];
+    volatile int32_t abort;
+};
+
+constexpr int kStagesMax = 8;
+
+// Bounded mbarrier wait.  Returns false (and latches `abort`) after kTimeoutNs.
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int32_t* abort,
+                                             bool cluster_scope = false) {
+    if (cluster_scope ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = ptx::globaltimer();
+    for (;;) {
+        if (*abort) return false;
+        if (cluster_scope ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity)) return true;
+        if (ptx::globaltimer() - t0 > kTimeoutNs) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+// Bounded wait that ignores the abort latch: used only to let issued copies land.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = ptx::globaltimer();
+    while (!ptx::mbar_try_wait(bar, parity)) {
+        if (ptx::globaltimer() - t0 > kTimeoutNs) return;
+    }
+}
+
+// ----------------------------------------------------------------- block scan helpers (consumers only)
+__device__ __forceinline__ double warp_inclusive_scan(double v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (lane >= o) v += n;
+    }
+    return v;
+}
+
+// Exclusive scan of one double per consumer thread in thread order; also returns the total.
+__device__ __forceinline__ double block_exclusive_scan(Shared& sh, double v, int tid, double& total) {
+    const int lane = tid & 31, warp = tid >> 5;
+    const double inc = warp_inclusive_scan(v, lane);
+    if (lane == 31) sh.scan[warp] = inc;
+    ptx::named_sync(1, kConsumerThreads);
+    if (warp == 0) {
+        double w = lane < kConsumerWarps ? sh.scan[lane] : 0.0;
+        const double wi = warp_inclusive_scan(w, lane);
+        if (lane < kConsumerWarps) sh.scan[lane] = wi - w;  // exclusive warp prefix
+        if (lane == kConsumerWarps - 1) sh.scan[kConsumerWarps] = wi;
+    }
+    ptx::named_sync(1, kConsumerThreads);
+    total = sh.scan[kConsumerWarps];
+    const double out = sh.scan[warp] + inc - v;
+    ptx::named_sync(1, kConsumerThreads);  // scan[] reusable after this
+    return out;
+}
+
+__device__ __forceinline__ int block_min_int(Shared& sh, int v, int tid) {
+    const int lane = tid & 31, warp = tid >> 5;
+    v = __reduce_min_sync(0xFFFFFFFFu, v);
+    if (lane == 0) sh.bcast_i[0] = 0x7FFFFFFF;
+    ptx::named_sync(1, kConsumerThreads);
+    if (lane == 0) atomicMin(const_cast<int32_t*>(&sh.bcast_i[0]), v);
+    ptx::named_sync(1, kConsumerThreads);
+    const int r = sh.bcast_i[0];
+    ptx::named_sync(1, kConsumerThreads);
+    (void)warp;
+    return r;
+}
+
+__device__ __forceinline__ int block_max_int(Shared& sh, int v, int tid) {
+    const int lane = tid & 31;
+    v = __reduce_max_sync(0xFFFFFFFFu, v);
+    if (tid == 0) sh.bcast_i[1] = -0x7FFFFFFF - 1;
+    ptx::named_sync(1, kConsumerThreads);
+    if (lane == 0) atomicMax(const_cast<int32_t*>(&sh.bcast_i[1]), v);
+    ptx::named_sync(1, kConsumerThreads);
+    const int r = sh.bcast_i[1];
+    ptx::named_sync(1, kConsumerThreads);
+    return r;
+}
+
+// ----------------------------------------------------------------- the kernel
+template <typename T, bool kSample, bool kBulk, int kStages>
+__global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const SelectParams p) {
+    using E = Elem<T>;
+    using L = Layout<T>;
+    constexpr int kVec = E::kVec;
+    constexpr int kTPC = L::kTokensPerChunk;
+    constexpr int kTPW = L::kTokensPerWarp;
+    constexpr uint32_t kVecMask = (1u << kVec) - 1u;
+
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* stages = smem_raw;
+    Shared& sh = *reinterpret_cast<Shared*>(smem_raw + kStages * L::kStageBytes);
+    float2* granules = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(Shared));
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const uint32_t crank = ptx::cluster_ctarank();
+    const uint32_t csize = ptx::cluster_nctarank();
+    const uint32_t cid = ptx::cluster_id_x();
+    const uint32_t nclusters = ptx::ncluster_x();
+
+    const int64_t seg_begin_raw = static_cast<int64_t>(crank) * p.segment;
+    const int64_t seg_begin = seg_begin_raw < p.vocab ? seg_begin_raw : p.vocab;
+    const int64_t seg_end = (seg_begin_raw + p.segment) < p.vocab ? (seg_begin_raw + p.segment) : p.vocab;
+    const int nchunks = static_cast<int>((seg_end - seg_begin + kTPC - 1) / kTPC);
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            ptx::mbar_init(ptx::smem_addr(&sh.full[s]), 1);
+            ptx::mbar_init(ptx::smem_addr(&sh.empty[s]), kConsumerWarps);
+        }
+        ptx::mbar_init(ptx::smem_addr(&sh.gather[0]), csize);
+        ptx::mbar_init(ptx::smem_addr(&sh.gather[1]), csize);
+        sh.abort = 0;
+        ptx::fence_mbarrier_init();
+    }
+    __syncthreads();
+    // Every CTA of the cluster has initialised its barriers before any remote arrive.
+    ptx::cluster_arrive();
+    ptx::cluster_wait();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------------ producer warp
+        if (kBulk && lane == 0) {
+            uint32_t it = 0;
+            bool stop = false;
+            for (int64_t row = cid; row < p.rows && !stop; row += nclusters) {
+                const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                                      static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+                const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+                for (int c = 0; c < nchunks; ++c, ++it) {
+                    const int stage = static_cast<int>(it % kStages);
+                    const uint32_t use = it / kStages;
+                    if (use > 0 && !wait_bounded(ptx::smem_addr(&sh.empty[stage]), (use - 1) & 1u, &sh.abort)) {
+                        stop = true;  // consumers stopped releasing stages: issue no more copies
+                        break;
+                    }
+                    const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
+                    const int64_t t1 = (t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end;
+                    const uint32_t lbytes = static_cast<uint32_t>((t1 - t0) * E::kBytes);
+                    const int64_t w0 = t0 >> 5, w1 = (t1 + 31) >> 5;
+                    const int64_t a0 = w0 & ~int64_t(3), a1 = (w1 + 3) & ~int64_t(3);
+                    const uint32_t mbytes = static_cast<uint32_t>((a1 - a0) * 4);
+                    uint8_t* st = stages + stage * L::kStageBytes;
+                    const uint32_t full = ptx::smem_addr(&sh.full[stage]);
+                    ptx::mbar_arrive_expect_tx(full, lbytes + mbytes);
+                    ptx::bulk_load(ptx::smem_addr(st), lrow + t0 * E::kBytes, lbytes, full);
+                    ptx::bulk_load(ptx::smem_addr(st + kChunkBytes), mrow + a0, mbytes, full);
+                }
+            }
+            // Every issued copy must have landed before this CTA's shared memory can go away.
+            for (int s = 0; s < kStages; ++s) {
+                if (it > static_cast<uint32_t>(s)) {
+                    const uint32_t last = (it - 1u - static_cast<uint32_t>(s)) / kStages;
+                    drain_wait(ptx::smem_addr(&sh.full[s]), last & 1u);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ consumer warps
+        uint32_t it = 0;
+        uint32_t k = 0;  // rows processed by this cluster (gather phase)
+        for (int64_t row = cid; row < p.rows; row += nclusters, ++k) {
+            const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                                  static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+            const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+            typename E::NanAcc nan_acc = E::nan_init();
+            uint32_t count = 0;
+            // argmax state
+            float best = 0.0f;
+            int best_idx = -1;
+            // sampler state (warp-uniform running max of valid logits)
+            float run_m = -__int_as_float(0x7F800000);
+
+            for (int c = 0; c < nchunks; ++c, ++it) {
+                const int stage = kBulk ? static_cast<int>(it % kStages) : 0;
+                const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
+                const int64_t t1 = (t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end;
+                const int ntok = static_cast<int>(t1 - t0);
+                uint8_t* st = stages + stage * L::kStageBytes;
+                const uint32_t* smask;
+                if constexpr (kBulk) {
+                    wait_bounded(ptx::smem_addr(&sh.full[stage]), (it / kStages) & 1u, &sh.abort);
+                    smask = reinterpret_cast<const uint32_t*>(st + kChunkBytes) + ((t0 >> 5) & 3);
+                } else {
+                    // Cooperative plain loads for rows the bulk engine cannot address.
+                    const int nvec_pad = (ntok + kVec - 1) / kVec * kVec;
+                    for (int i = tid; i < nvec_pad; i += kConsumerThreads) {
+                        uint32_t v = 0u;
+                        if (i < ntok) v = E::raw(lrow, t0 + i);
+                        if constexpr (E::kBytes == 4) reinterpret_cast<uint32_t*>(st)[i] = v;
+                        else reinterpret_cast<uint16_t*>(st)[i] = static_cast<uint16_t>(v);
+                    }
+                    const int nwords = (ntok + 31) >> 5;
+                    for (int i = tid; i < nwords; i += kConsumerThreads) {
+                        uint32_t wv = static_cast<uint32_t>(mrow[(t0 >> 5) + i]);
+                        const int64_t last_tok = t0 + 32 * static_cast<int64_t>(i) + 31;
+                        if (last_tok >= p.vocab) {
+                            const int keep = static_cast<int>(p.vocab - (t0 + 32 * static_cast<int64_t>(i)));
+                            wv &= keep >= 32 ? 0xFFFFFFFFu : ((1u << keep) - 1u);
+                        }
+                        reinterpret_cast<uint32_t*>(st + kChunkBytes)[i] = wv;
+                    }
+                    ptx::named_sync(1, kConsumerThreads);
+                    smask = reinterpret_cast<const uint32_t*>(st + kChunkBytes);
+                }
+
+                const int nvec = (ntok + kVec - 1) / kVec;
+                const uint8_t* wl = st + warp * kWarpBytes;
+                const uint32_t* wm = smask + warp * (kTPW / 32);
+                uint4 raw[kVecsPerLane];
+                uint32_t bits[kVecsPerLane];
+#pragma unroll
+                for (int j = 0; j < kVecsPerLane; ++j) {
+                    const int vec = j * 32 + lane;
+                    const bool in = warp * (kTPW / kVec) + vec < nvec;
+                    raw[j] = in ? *reinterpret_cast<const uint4*>(wl + vec * 16) : make_uint4(0, 0, 0, 0);
+                    const uint32_t word = in ? wm[(vec * kVec) >> 5] : 0u;
+                    bits[j] = (word >> ((vec * kVec) & 31)) & kVecMask;
+                }
+                // Stage contents are in registers: release it to the producer.
+                if constexpr (kBulk) {
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.empty[stage]));
+                }
+                const int64_t wtok0 = t0 + warp * kTPW;
+
+                if constexpr (!kSample) {
+#pragma unroll
+                    for (int j = 0; j < kVecsPerLane; ++j) {
+                        E::nan_update(nan_acc, raw[j]);
+                        count += __popc(bits[j]);
+                        float v[kVec];
+                        E::decode(raw[j], v);
+                        float mv[kVec];
+#pragma unroll
+                        for (int i = 0; i < kVec; ++i)
+                            mv[i] = ((bits[j] >> i) & 1u) ? v[i] : __int_as_float(0x7FFFFFFF);
+                        float vmax = mv[0];
+#pragma unroll
+                        for (int i = 1; i < kVec; ++i) vmax = fmaxf(vmax, mv[i]);
+                        if (vmax > best || (best_idx < 0 && vmax == vmax)) {
+                            int first = 0;
+#pragma unroll
+                            for (int i = kVec - 1; i >= 0; --i)
+                                if (mv[i] == vmax) first = i;
+                            best = vmax;
+                            best_idx = static_cast<int>(wtok0 + (j * 32 + lane) * kVec + first);
+                        }
+                    }
+                } else {
+                    // Pass 1 over registers: NaN, count, masked chunk max.
+                    float lmax = __int_as_float(0x7FFFFFFF);
+#pragma unroll
+                    for (int j = 0; j < kVecsPerLane; ++j) {
+                        E::nan_update(nan_acc, raw[j]);
+                        count += __popc(bits[j]);
+                        float v[kVec];
+                        E::decode(raw[j], v);
+#pragma unroll
+                        for (int i = 0; i < kVec; ++i)
+                            if ((bits[j] >> i) & 1u) lmax = fmaxf(lmax, v[i]);
+                    }
+                    // Warp max over lanes (NaN = no valid token in the lane).
+                    const uint32_t lkey = (lmax == lmax) ? ordered_bits(lmax) : 0u;
+                    const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, lkey);
+                    if (wkey != 0u) {
+                        const float wmax = ordered_to_float(wkey);
+                        run_m = fmaxf(run_m, wmax);
+                    }
+                    // Pass 2: fp32 weights relative to the running max (all exponents <= 0).
+                    float mass = 0.0f;
+                    const bool finite_m = run_m > -__int_as_float(0x7F800000) && run_m < __int_as_float(0x7F800000);
+                    if (finite_m) {
+                        const float nhm = -0.5f * run_m;
+                        const float sc2 = p.scale2;
+                        float part[kVecsPerLane];
+#pragma unroll
+                        for (int j = 0; j < kVecsPerLane; ++j) {
+                            float v[kVec];
+                            E::decode(raw[j], v);
+                            float w[kVec];
+#pragma unroll
+                            for (int i = 0; i < kVec; ++i) {
+                                const float t = fmaf(v[i], 0.5f, nhm) * sc2;
+                                const float e = ptx::ex2(fminf(t, 0.0f));
+                                w[i] = ((bits[j] >> i) & 1u) ? e : 0.0f;
+                            }
+                            // Pairwise sum of the vector's weights.
+#pragma unroll
+                            for (int h = kVec / 2; h >= 1; h >>= 1)
+#pragma unroll
+                                for (int i = 0; i < h; ++i) w[i] += w[i + h];
+                            part[j] = w[0];
+                        }
+#pragma unroll
+                        for (int h = kVecsPerLane / 2; h >= 1; h >>= 1)
+#pragma unroll
+                            for (int i = 0; i < h; ++i) part[i] += part[i + h];
+                        mass = part[0];
+#pragma unroll
+                        for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
+                    }
+                    if (lane == 0) granules[c * kConsumerWarps + warp] = make_float2(run_m, mass);
+                }
+                if constexpr (!kBulk) ptx::named_sync(1, kConsumerThreads);  // stage 0 reusable
+            }
+
+            // ---------------------------------------------------- CTA partial
+            const bool nan_local = E::has_nan(nan_acc);
+            const uint32_t wcount = __reduce_add_sync(0xFFFFFFFFu, count);
+            const uint32_t wnan = __any_sync(0xFFFFFFFFu, nan_local) ? kFlagNaN : 0u;
+            uint32_t cta_hi = 0, cta_lo = 0, cta_count = 0, cta_flags = 0;
+            if constexpr (!kSample) {
+                const uint32_t hi = best_idx >= 0 ? ordered_bits(best) : 0u;
+                const uint32_t whi = __reduce_max_sync(0xFFFFFFFFu, hi);
+                const uint32_t lo = (best_idx >= 0 && hi == whi) ? (0xFFFFFFFFu - static_cast<uint32_t>(best_idx)) : 0u;
+                const uint32_t wlo = __reduce_max_sync(0xFFFFFFFFu, lo);
+                if (lane == 0) {
+                    sh.warp_key_hi[warp] = whi;
+                    sh.warp_key_lo[warp] = wlo;
+                }
+            } else {
+                if (lane == 0) sh.warp_m[warp] = (run_m == run_m) ? ordered_bits(run_m) : 0u;
+            }
+            if (lane == 0) {
+                sh.warp_count[warp] = wcount;
+                sh.warp_flags[warp] = wnan;
+            }
+            ptx::named_sync(1, kConsumerThreads);
+            {
+                const bool in = lane < kConsumerWarps;
+                const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, in ? sh.warp_flags[lane] : 0u);
+                cta_count = __reduce_add_sync(0xFFFFFFFFu, in ? sh.warp_count[lane] : 0u);
+                cta_flags = f | (sh.abort ? kFlagAbort : 0u);
+                if constexpr (!kSample) {
+                    const uint32_t hi = in ? sh.warp_key_hi[lane] : 0u;
+                    cta_hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+                    const uint32_t lo = (in && hi == cta_hi) ? sh.warp_key_lo[lane] : 0u;
+                    cta_lo = __reduce_max_sync(0xFFFFFFFFu, lo);
+                } else {
+                    cta_hi = __reduce_max_sync(0xFFFFFFFFu, in ? sh.warp_m[lane] : 0u);
+                }
+            }
+
+            if constexpr (!kSample) {
+                // -------------------------------------------------- argmax finish
+                uint32_t hi = cta_hi, lo = cta_lo, cnt = cta_count, flags = cta_flags;
+                if (csize > 1) {
+                    const uint32_t slot = k & 1u;
+                    if (tid == 0) {
+                        const uint32_t local = ptx::smem_addr(&sh.slots[slot][crank]);
+                        const uint32_t bar = ptx::smem_addr(&sh.gather[slot]);
+                        for (uint32_t q = 0; q < csize; ++q) {
+                            ptx::st_cluster_v4(ptx::mapa(local, q), hi, lo, cnt, flags);
+                            ptx::mbar_arrive_remote(ptx::mapa(bar, q));
+                        }
+                        wait_bounded(ptx::smem_addr(&sh.gather[slot]), (k >> 1) & 1u, &sh.abort, true);
+                    }
+                    ptx::named_sync(1, kConsumerThreads);
+                    if (crank == 0 && warp == 0) {
+                        const bool in = lane < static_cast<int>(csize);
+                        const GatherSlot g = in ? sh.slots[slot][lane] : GatherSlot{0, 0, 0, 0, 0.0, 0.0};
+                        hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
+                        lo = __reduce_max_sync(0xFFFFFFFFu, (in && g.a == hi) ? g.b : 0u);
+                        cnt = __reduce_add_sync(0xFFFFFFFFu, g.c);
+                        flags = __reduce_or_sync(0xFFFFFFFFu, g.d) | (sh.abort ? kFlagAbort : 0u);
+                    }
+                }
+                if (crank == 0 && tid == 0) {
+                    const int32_t code = (flags & kFlagAbort) ? kTimeout
+                                         : (flags & kFlagNaN) ? kNaN
+                                         : (cnt == 0u)        ? kEmpty
+                                                              : kOk;
+                    p.status[row] = code;
+                    p.tokens[row] = code == kOk ? p.token_offset + static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
+                    if (p.counts) p.counts[row] = cnt;
+                }
+            } else {
+                // -------------------------------------------------- sampler finish
+                // Segment maximum and mass relative to it, granules in (chunk, warp) order.
+                const float seg_m = cta_hi ? ordered_to_float(cta_hi) : -__int_as_float(0x7F800000);
+                const int ngran = nchunks * kConsumerWarps;
+                const bool seg_finite = seg_m > -__int_as_float(0x7F800000) && seg_m < __int_as_float(0x7F800000);
+                double term = 0.0;
+                if (seg_finite) {
+                    for (int g = tid; g < ngran; g += kConsumerThreads) {
+                        const float2 e = granules[g];
+                        if (e.y > 0.0f) term += static_cast<double>(e.y) *
+                                                exp((static_cast<double>(e.x) - static_cast<double>(seg_m)) / p.temperature);
+                    }
+                }
+                double seg_s;
+                block_exclusive_scan(sh, term, tid, seg_s);
+
+                // All-gather (M_r, S_r, count, flags) across the cluster, in rank order.
+                const uint32_t slot = k & 1u;
+                if (tid == 0) {
+                    GatherSlot mine{__float_as_uint(seg_m), cta_count, cta_flags, 0u, seg_s, 0.0};
+                    if (csize > 1) {
+                        const uint32_t local = ptx::smem_addr(&sh.slots[slot][crank]);
+                        const uint32_t bar = ptx::smem_addr(&sh.gather[slot]);
+                        uint32_t sbits[2];
+                        memcpy(sbits, &mine.s, 8);
+                        for (uint32_t q = 0; q < csize; ++q) {
+                            const uint32_t dst = ptx::mapa(local, q);
+                            ptx::st_cluster_v4(dst, mine.a, mine.b, mine.c, mine.d);
+                            ptx::st_cluster_v4(dst + 16, sbits[0], sbits[1], 0u, 0u);
+                            ptx::mbar_arrive_remote(ptx::mapa(bar, q));
+                        }
+                        wait_bounded(ptx::smem_addr(&sh.gather[slot]), (k >> 1) & 1u, &sh.abort, true);
+                    } else {
+                        sh.slots[slot][0] = mine;
+                    }
+                }
+                ptx::named_sync(1, kConsumerThreads);
+                // Row-level merge, identical on every rank.
+                float rm = -__int_as_float(0x7F800000);
+                uint32_t cnt = 0, flags = sh.abort ? kFlagAbort : 0u;
+                for (uint32_t q = 0; q < csize; ++q) {
+                    const GatherSlot& g = sh.slots[slot][q];
+                    rm = fmaxf(rm, __uint_as_float(g.a));
+                    cnt += g.b;
+                    flags |= g.c;
+                }
+                const double u = p.uniforms[row];
+                int32_t code = (flags & kFlagAbort) ? kTimeout
+                               : (flags & kFlagNaN) ? kNaN
+                               : (rm == __int_as_float(0x7F800000)) ? kPosInf
+                               : (cnt == 0u) ? kEmpty
+                               : (rm == -__int_as_float(0x7F800000)) ? kNoMass
+                               : !(u >= 0.0 && u < 1.0) ? kBadUniform
+                                                        : kOk;
+                if (code != kOk) {
+                    if (crank == 0 && tid == 0) {
+                        p.status[row] = code;
+                        p.tokens[row] = -1;
+                        if (p.counts) p.counts[row] = cnt;
+                    }
+                } else {
+                    const double M = rm;
+                    double total = 0.0;
+                    double rank_mass[kMaxCluster];
+                    for (uint32_t q = 0; q < csize; ++q) {
+                        const GatherSlot& g = sh.slots[slot][q];
+                        const float gm = __uint_as_float(g.a);
+                        rank_mass[q] = (g.s > 0.0) ? g.s * exp((static_cast<double>(gm) - M) / p.temperature) : 0.0;
+                        total += rank_mass[q];
+                    }
+                    const double cutoff = u * total;
+                    int owner = -1, last_pos = -1;
+                    double prefix = 0.0, run = 0.0, last_prefix = 0.0;
+                    for (uint32_t q = 0; q < csize; ++q) {
+                        if (rank_mass[q] <= 0.0) continue;
+                        last_pos = static_cast<int>(q);
+                        last_prefix = run;
+                        if (owner < 0 && cutoff < run + rank_mass[q]) {
+                            owner = static_cast<int>(q);
+                            prefix = run;
+                        }
+                        run += rank_mass[q];
+                    }
+                    const bool fallback = owner < 0;
+                    if (fallback) {
+                        owner = last_pos;
+                        prefix = last_prefix;
+                    }
+                    if (owner == static_cast<int>(crank)) {
+                        // Find the granule: exclusive scan of granule masses (thread-contiguous blocks).
+                        const int per = (ngran + kConsumerThreads - 1) / kConsumerThreads;
+                        const int g0 = tid * per, g1 = min(g0 + per, ngran);
+                        double local = 0.0;
+                        for (int g = g0; g < g1; ++g) {
+                            const float2 e = granules[g];
+                            if (e.y > 0.0f) local += static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / p.temperature);
+                        }
+                        double seg_total;
+                        const double excl = block_exclusive_scan(sh, local, tid, seg_total);
+                        int cand = 0x7FFFFFFF, lastg = -1;
+                        double acc = prefix + excl;
+                        for (int g = g0; g < g1; ++g) {
+                            const float2 e = granules[g];
+                            if (!(e.y > 0.0f)) continue;
+                            const double m = static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / p.temperature);
+                            if (!(m > 0.0)) continue;
+                            lastg = g;
+                            if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) cand = g;
+                            acc += m;
+                        }
+                        int gsel = fallback ? 0x7FFFFFFF : block_min_int(sh, cand, tid);
+                        const bool walk_fallback = (gsel == 0x7FFFFFFF);
+                        if (walk_fallback) gsel = block_max_int(sh, lastg, tid);
+                        // Prefix mass before the chosen granule.
+                        if (!walk_fallback && g0 <= gsel && gsel < g1) {
+                            double a = prefix + excl;
+                            for (int g = g0; g < gsel; ++g) {
+                                const float2 e = granules[g];
+                                if (e.y > 0.0f) a += static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / p.temperature);
+                            }
+                            sh.bcast_d[0] = a;
+                        }
+                        ptx::named_sync(1, kConsumerThreads);
+                        const double gprefix = walk_fallback ? 0.0 : sh.bcast_d[0];
+                        int64_t chosen = -1;
+                        if (gsel >= 0) {
+                            // Walk the granule with exact fp64 weights, in token order.
+                            const int gc = gsel / kConsumerWarps, gw = gsel % kConsumerWarps;
+                            const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
+                            const int64_t gt1 = min(gt0 + kTPW, seg_end);
+                            constexpr int kPer = kTPW / kConsumerThreads;
+                            const int64_t my0 = gt0 + tid * kPer;
+                            double w[kPer];
+                            double wsum = 0.0;
+#pragma unroll
+                            for (int i = 0; i < kPer; ++i) {
+                                const int64_t t = my0 + i;
+                                w[i] = 0.0;
+                                if (t < gt1) {
+                                    const uint32_t word = static_cast<uint32_t>(mrow[t >> 5]);
+                                    if ((word >> (t & 31)) & 1u) {
+                                        const float x = E::load(lrow, t);
+                                        if (x > -__int_as_float(0x7F800000))
+                                            w[i] = exp((static_cast<double>(x) - M) / p.temperature);
+                                    }
+                                }
+                                wsum += w[i];
+                            }
+                            double gtotal;
+                            const double wexcl = block_exclusive_scan(sh, wsum, tid, gtotal);
+                            int64_t hit = INT64_MAX, lastpos = -1;
+                            double a = gprefix + wexcl;
+#pragma unroll
+                            for (int i = 0; i < kPer; ++i) {
+                                if (!(w[i] > 0.0)) continue;
+                                lastpos = my0 + i;
+                                a += w[i];
+                                if (!walk_fallback && hit == INT64_MAX && cutoff < a) hit = my0 + i;
+                            }
+                            // Lowest hit, else the last positive-weight token of the granule.
+                            const int hit32 = hit == INT64_MAX ? 0x7FFFFFFF : static_cast<int>(hit - gt0);
+                            const int hmin = block_min_int(sh, hit32, tid);
+                            if (hmin != 0x7FFFFFFF) {
+                                chosen = gt0 + hmin;
+                            } else {
+                                const int lp = block_max_int(sh, lastpos < 0 ? -1 : static_cast<int>(lastpos - gt0), tid);
+                                chosen = lp >= 0 ? gt0 + lp : -1;
+                            }
+                        }
+                        if (tid == 0) {
+                            p.status[row] = chosen >= 0 ? kOk : kNoMass;
+                            p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
+                            if (p.counts) p.counts[row] = cnt;
+                        }
+                    }
+                }
+                // granules[] and slots are rewritten by the next row only after this point.
+                ptx::named_sync(1, kConsumerThreads);
+            }
+        }
+    }
+
+    // No CTA may exit while a peer can still write into its shared memory.
+    __syncthreads();
+    ptx::cluster_arrive();
+    ptx::cluster_wait();
+}
+
+// Shared-memory bytes the kernel needs (stages + control block + sampler granule table).
+template <typename T, bool kSample>
+constexpr size_t select_smem_bytes(int stages) {
+    return static_cast<size_t>(stages) * Layout<T>::kStageBytes + sizeof(Shared) +
+           (kSample ? static_cast<size_t>(kMaxChunksSampler) * kConsumerWarps * sizeof(float2) : 0);
+}
+
+}  // namespace bms

@@ -1,0 +1,146 @@
+/*
+ * bms_b200.h -- C ABI of the B200 (sm_100a) masked-selection library.
+ *
+ * Drop-in boundary for the native module of karthikeyansura/bitmask-speculation
+ * (csrc/bindings.cpp:10-17 exports runtime_version, mask_count, masked_argmax,
+ * masked_reduce_batch and masked_sample).  Every entry point takes plain device
+ * pointers and sizes, no framework types:
+ *
+ *   - inputs are read-only; outputs are caller-allocated device buffers that the
+ *     call overwrites (the library allocates no device or host memory);
+ *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) of CUDA device `device`; nothing synchronises with the host;
+ *   - every pointer must be device (or managed) memory of `device`, checked with
+ *     cudaPointerGetAttributes before anything is launched;
+ *   - contract violations return a nonzero BMS_ERROR_* code with a message from
+ *     bms_last_error() (thread-local) and launch nothing; row-level data errors
+ *     (empty mask, NaN, ...) are reported per row through the status outputs,
+ *     exactly like the reference's device status codes (csrc/sample.cu:24-25).
+ *
+ * Masks are packed int32 words, token t allowed iff bit (t % 32) of word t / 32
+ * is set; bits at or beyond the vocabulary are ignored.  Logits are float32,
+ * bfloat16 or float16 (the reference accepted float32 only, csrc/checks.h:21).
+ */
+#ifndef BMS_B200_H
+#define BMS_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BMS_API __attribute__((visibility("default")))
+#else
+#define BMS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Logit element types. */
+enum { BMS_FLOAT32 = 0, BMS_BFLOAT16 = 1, BMS_FLOAT16 = 2 };
+
+/* Return codes of the entry points. */
+enum {
+    BMS_SUCCESS = 0,
+    BMS_ERROR_INVALID_ARGUMENT = 1, /* the reference raised RuntimeError (TORCH_CHECK) */
+    BMS_ERROR_CUDA = 2,             /* a CUDA runtime call or launch failed */
+    BMS_ERROR_UNSUPPORTED = 3       /* valid input beyond a documented limit */
+};
+
+/* Per-row status codes written by the kernels (csrc/sample.cu:24-25, argmax.cu:77). */
+enum {
+    BMS_STATUS_OK = 0,
+    BMS_STATUS_EMPTY = 1,       /* mask has no valid token */
+    BMS_STATUS_NAN = 2,         /* a logit of the row is NaN (valid or not) */
+    BMS_STATUS_BAD_UNIFORM = 3, /* sampler uniform not in [0, 1) */
+    BMS_STATUS_NO_MASS = 4,     /* every valid logit is -inf (sampler) */
+    BMS_STATUS_POS_INF = 5,     /* a valid logit is +inf (sampler) */
+    BMS_STATUS_BAD_LENGTH = 6,  /* verification: proposal count outside [0, K] */
+    BMS_STATUS_TIMEOUT = 7      /* a bounded device wait expired; row result undefined */
+};
+
+/* Draft budget policy.  kind 0: decoding/scheduling.py:21-46 DensityPolicy
+ * (density < low -> max; < high -> (min + max) / 2; else min).  kind 1: linear
+ * (density < low -> max; > high -> min; else max - floor((max - min) *
+ * ((density - low) / (high - low))), all in IEEE double).  density is
+ * count / vocab, correctly rounded. */
+typedef struct bms_policy {
+    int32_t kind;
+    int32_t min_budget;
+    int32_t max_budget;
+    int32_t reserved;
+    double low_density;
+    double high_density;
+} bms_policy;
+
+/* Message of the last failed call on this thread ("" if none). */
+BMS_API const char *bms_last_error(void);
+
+/* Replaces csrc/runtime.cu:4-8 cuda_runtime_version. */
+BMS_API int bms_runtime_version(int32_t *version);
+
+/* Replaces csrc/popcount.cu:28-37 mask_count_cuda: *count = number of allowed
+ * tokens in one row of ceil(vocab / 32) words (count is a device int64). */
+BMS_API int bms_mask_count(const int32_t *mask, int64_t vocab, int64_t *count, int32_t device, void *stream);
+
+/* Replaces csrc/argmax.cu:117-125 masked_argmax_cuda: lowest-index valid
+ * maximum of one row; *token = -1 unless *status == BMS_STATUS_OK. */
+BMS_API int bms_masked_argmax(const void *logits, int32_t dtype, const int32_t *mask, int64_t vocab,
+                      int64_t *token, int32_t *status, int32_t device, void *stream);
+
+/* Replaces csrc/argmax.cu:127-137 masked_reduce_batch_cuda: per row of a
+ * contiguous [rows, vocab] logits / [rows, ceil(vocab/32)] mask batch, the
+ * masked argmax, the valid count and a status.  `counts` may be NULL.  No row
+ * limit (the reference stopped at 65,535 rows, csrc/checks.h:36). */
+BMS_API int bms_masked_reduce_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t rows,
+                            int64_t vocab, int64_t *tokens, int64_t *counts, int32_t *status,
+                            int32_t device, void *stream);
+
+/* Replaces csrc/sample.cu:116-132 masked_sample_cuda: inverse-CDF sample of
+ * the masked softmax at `temperature` with the device float64 scalar
+ * `uniform` in [0, 1).  temperature == 0 is the masked argmax (uniform unused). */
+BMS_API int bms_masked_sample(const void *logits, int32_t dtype, const int32_t *mask, int64_t vocab,
+                      double temperature, const double *uniform, int64_t *token, int32_t *status,
+                      int32_t device, void *stream);
+
+/* Batched form of bms_masked_sample with one uniform per row (no reference
+ * counterpart; the reference sampled one row per launch).  `counts` may be NULL. */
+BMS_API int bms_masked_sample_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t rows,
+                            int64_t vocab, double temperature, const double *uniforms,
+                            int64_t *tokens, int64_t *counts, int32_t *status, int32_t device,
+                            void *stream);
+
+/* Device form of grammar/density.py:23-53 (packed_mask_count / density) and
+ * decoding/scheduling.py:40-46 (DensityPolicy.budget) for a [rows, words]
+ * batch.  Any of counts / density / budget may be NULL; policy may be NULL when
+ * budget is NULL. */
+BMS_API int bms_mask_budget(const int32_t *masks, int64_t rows, int64_t vocab, const bms_policy *policy,
+                    int64_t *counts, double *density, int32_t *budget, int32_t device, void *stream);
+
+/* One batched verification round (decoding/verification.py:18-48 verify_prefix
+ * over the rows models/transformers.py:181-201 selects from).  Sequence s owns
+ * rows [s*rows_per_seq, (s+1)*rows_per_seq); row s*rows_per_seq + i is the
+ * target's prediction after proposals[s, :i].  proposals is [seqs,
+ * rows_per_seq - 1], lengths[s] proposals are live.  Outputs: per row the
+ * masked argmax, count, status and policy budget; per sequence the accepted
+ * prefix length, the correction / bonus / fallback token, its kind (0
+ * correction, 1 bonus, 2 fallback) and a status that is nonzero only when a
+ * row the reference would have consumed failed.  row_counts and row_budget
+ * may be NULL (then policy may be NULL). */
+BMS_API int bms_verify_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t seqs,
+                     int64_t rows_per_seq, int64_t vocab, const int64_t *proposals,
+                     const int32_t *lengths, const bms_policy *policy, int64_t *row_tokens,
+                     int64_t *row_counts, int32_t *row_status, int32_t *row_budget,
+                     int32_t *accept_len, int64_t *token, int32_t *kind, int32_t *seq_status,
+                     int32_t device, void *stream);
+
+/* Test hook: force the cluster size (1, 2, 4, 8 or 16) and the number of
+ * clusters of the selection kernels; 0 restores the automatic choice.
+ * Process-wide; not for concurrent use with other calls. */
+BMS_API int bms_set_launch_override(int32_t cluster, int32_t clusters);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BMS_B200_H */
