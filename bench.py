@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--workload", choices=["verify", "argmax", "sample", "scale"], default="verify")
     ap.add_argument("--seqs", type=int, default=256, help="verification sequences per GPU")
     ap.add_argument("--rows", type=int, default=8192, help="rows per GPU for the scale workload")
+    ap.add_argument("--sample-rows", type=int, default=8,
+                    help="rows per sampling batch (the 8 configuration rows tiled, fresh uniforms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--roofline-seconds", type=float, default=1.5)
@@ -169,16 +171,20 @@ class Workload:
         elif self.kind == "sample":
             import numpy as np
             bits, masks, uniforms, temp = wl.sample_config_np(seed=2 + rank)
+            tile = max(1, args.sample_rows // bits.shape[0])
+            bits, masks = np.tile(bits, (tile, 1)), np.tile(masks, (tile, 1))
+            uniforms = np.random.default_rng(2 + rank).random(bits.shape[0])
             reps = max(1, int(2 * L2_BYTES // bits.nbytes) + 1)
             self.logits_all = torch.from_numpy(np.tile(bits, (reps, 1)).view(np.int16)).view(torch.float16).to(device)
             self.masks_all = torch.from_numpy(np.ascontiguousarray(np.tile(masks, (reps, 1)))).to(device)
             self.uniforms_all = torch.from_numpy(np.tile(uniforms, reps)).to(device)
             self.temperature = temp
-            self.rows = 8
+            self.rows = bits.shape[0]
             self.batches = reps
             self.esize = 2
             self.dtype = "f16"
-            self.name = "sample: 8 rows fp16 N(0,2^2) at V=248320, T=0.7, densities {1,.5,.1,.01,1e-4,.9,.3,.05}"
+            self.name = (f"sample: {self.rows} rows fp16 N(0,2^2) at V=248320, T=0.7, densities "
+                         "{1,.5,.1,.01,1e-4,.9,.3,.05}")
         else:
             self.logits, self.masks = wl.scale_rows_torch(args.rows, seed=5 + 1000 * rank, device=device)
             self.rows = args.rows
@@ -209,7 +215,7 @@ class Workload:
             self.seq_status = torch.empty(s, dtype=torch.int32, device=d)
 
     def _batch(self):
-        if self.batches == 1:
+        if self.batches == 1 and hasattr(self, "logits"):
             return self.logits, self.masks
         b = self.step_index % self.batches
         r0 = b * self.rows
@@ -272,8 +278,8 @@ class Workload:
         """Untimed sanity check of the last step on a few rows (CPU oracle)."""
         import numpy as np
         import oracle
-        logits, masks = self.logits if self.batches == 1 else self.logits_all[:self.rows], \
-            self.masks if self.batches == 1 else self.masks_all[:self.rows]
+        self.step_index = 0
+        logits, masks = self._batch()
         n = min(max_rows, self.rows)
         if self.kind in ("verify", "scale", "argmax"):
             self.step_index = 0

@@ -280,54 +280,66 @@ __global__ void __launch_bounds__(256) count_rows_kernel(const int32_t* __restri
     }
 }
 
-// Longest-prefix acceptance per sequence plus the per-row budgets.
+// Longest-prefix acceptance, one warp per sequence: lane i looks at row i of a 32-row window,
+// a ballot finds the first row where the reference stops (a failed status, a draft mismatch,
+// or the bonus row), and per-row budgets follow.  Launched as a programmatic dependent of
+// the selection kernel: the wait below is the grid dependency, not a spin.
 __global__ void __launch_bounds__(256) verify_epilogue_kernel(
     const int64_t* __restrict__ row_tokens, const int64_t* __restrict__ row_counts, const int32_t* __restrict__ row_status,
     int64_t seqs, int64_t rows_per_seq, int64_t vocab, const int64_t* __restrict__ proposals,
     const int32_t* __restrict__ lengths, bms_policy policy, int32_t* __restrict__ row_budget,
     int32_t* __restrict__ accept_len, int64_t* __restrict__ token, int32_t* __restrict__ kind,
     int32_t* __restrict__ seq_status) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (row_budget != nullptr && row_counts != nullptr) {
-        for (int64_t r = first; r < seqs * rows_per_seq; r += stride)
-            row_budget[r] = policy_budget(policy, __ddiv_rn(static_cast<double>(row_counts[r]), static_cast<double>(vocab)));
-    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int lane = threadIdx.x & 31;
+    const int64_t first_thread = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t threads = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t k_max = rows_per_seq - 1;
-    for (int64_t s = first; s < seqs; s += stride) {
-        const int64_t* tok = row_tokens + s * rows_per_seq;
-        const int32_t* st = row_status + s * rows_per_seq;
-        const int64_t* prop = proposals + s * k_max;
+    for (int64_t s = first_thread >> 5; s < seqs; s += threads >> 5) {
+        const int64_t base = s * rows_per_seq;
         const int32_t len = lengths[s];
-        int32_t a = 0, kd = 0, ss = 0;
+        int32_t a = -1, ss = 0, kd = 0;
         int64_t tk = -1;
         if (len < 0 || len > k_max) {
+            a = 0;
             ss = kBadLength;
-        } else {
-            for (int32_t i = 0;; ++i) {
-                if (st[i] != 0) {  // a consumed row failed: the reference raises here
-                    a = i;
-                    ss = st[i];
-                    break;
-                }
-                if (i == len) {  // every proposal matched: bonus (or fallback without proposals)
-                    a = len;
-                    tk = tok[i];
-                    kd = len > 0 ? 1 : 2;
-                    break;
-                }
-                if (tok[i] != prop[i]) {  // first mismatch: the target's token corrects it
-                    a = i;
-                    tk = tok[i];
-                    kd = 0;
-                    break;
+        }
+        for (int64_t w0 = 0; a < 0 && w0 <= len; w0 += 32) {
+            const int64_t i = w0 + lane;
+            bool stop = false, miss = false;
+            int32_t st = 0;
+            int64_t tok = -1;
+            if (i <= len) {
+                st = row_status[base + i];
+                tok = row_tokens[base + i];
+                miss = i < len && tok != proposals[s * k_max + i];
+                stop = st != 0 || miss || i == len;
+            }
+            const uint32_t ballot = __ballot_sync(0xFFFFFFFFu, stop);
+            if (ballot) {
+                const int f = __ffs(ballot) - 1;
+                const int32_t fst = __shfl_sync(0xFFFFFFFFu, st, f);
+                const int64_t ftok = __shfl_sync(0xFFFFFFFFu, tok, f);
+                const bool fmiss = __shfl_sync(0xFFFFFFFFu, miss, f);
+                a = static_cast<int32_t>(w0 + f);
+                if (fst != 0) {
+                    ss = fst;  // a consumed row failed: the reference raises here
+                } else {
+                    tk = ftok;  // correction at the first mismatch, else bonus / fallback
+                    kd = fmiss ? 0 : (len > 0 ? 1 : 2);
                 }
             }
         }
-        accept_len[s] = a;
-        token[s] = tk;
-        kind[s] = kd;
-        seq_status[s] = ss;
+        if (lane == 0) {
+            accept_len[s] = a;
+            token[s] = tk;
+            kind[s] = kd;
+            seq_status[s] = ss;
+        }
+    }
+    if (row_budget != nullptr && row_counts != nullptr) {
+        for (int64_t r = first_thread; r < seqs * rows_per_seq; r += threads)
+            row_budget[r] = policy_budget(policy, __ddiv_rn(static_cast<double>(row_counts[r]), static_cast<double>(vocab)));
     }
 }
 
@@ -524,11 +536,23 @@ int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, in
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     BMS_CHECK(launch_select<false>(dtype, p, device, s));
     const int64_t cap = static_cast<int64_t>(sm_count(device)) * 4;
-    const int64_t need = (rows + 255) / 256;
+    const int64_t need_seq = (seqs + 7) / 8;   // one warp per sequence
+    const int64_t need_row = (rows + 255) / 256;
+    int64_t need = need_seq > need_row ? need_seq : need_row;
     const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
-    verify_epilogue_kernel<<<grid, 256, 0, s>>>(row_tokens, row_counts, row_status, seqs, rows_per_seq, vocab,
-                                                proposals, lengths, P, row_budget, accept_len, token, kind, seq_status);
-    BMS_CUDA(cudaGetLastError(), "verification epilogue launch");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    BMS_CUDA(cudaLaunchKernelEx(&cfg, verify_epilogue_kernel, row_tokens, static_cast<const int64_t*>(row_counts),
+                                static_cast<const int32_t*>(row_status), seqs, rows_per_seq, vocab, proposals, lengths,
+                                P, row_budget, accept_len, token, kind, seq_status),
+             "verification epilogue launch");
     return BMS_SUCCESS;
 }
 

@@ -157,6 +157,33 @@ __device__ __forceinline__ uint32_t max_nan_f16x2(uint32_t a, uint32_t b) {
     return r;
 }
 
+// NaN-ignoring packed maxima (a NaN operand loses to a number).
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t max_f16x2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// Byte permute; selector nibbles with bit 3 set replicate the sign bit of the chosen byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// (a & m) | (~m & c): keep a where m is set, else c.
+__device__ __forceinline__ uint32_t select_bits(uint32_t a, uint32_t m, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xE2;" : "=r"(r) : "r"(a), "r"(m), "r"(c));
+    return r;
+}
+
 // Approximate 2^x on the MUFU unit (ex2.approx, about 2 ulp; denormal results flushed to zero).
 __device__ __forceinline__ float ex2(float x) {
     float r;

@@ -111,6 +111,10 @@ struct Elem<__nv_bfloat16> {
         return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(p)[i]) << 16);
     }
     __device__ static uint32_t raw(const void* p, int64_t i) { return static_cast<const uint16_t*>(p)[i]; }
+    static constexpr uint32_t kNegInf2 = 0xFF80FF80u;
+    __device__ static uint32_t max2(uint32_t a, uint32_t b) { return ptx::max_bf16x2(a, b); }
+    __device__ static float lo(uint32_t u) { return __uint_as_float(u << 16); }
+    __device__ static float hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 };
 
 template <>
@@ -138,7 +142,56 @@ struct Elem<__half> {
         return __half2float(static_cast<const __half*>(p)[i]);
     }
     __device__ static uint32_t raw(const void* p, int64_t i) { return static_cast<const uint16_t*>(p)[i]; }
+    static constexpr uint32_t kNegInf2 = 0xFC00FC00u;
+    __device__ static uint32_t max2(uint32_t a, uint32_t b) { return ptx::max_f16x2(a, b); }
+    __device__ static float lo(uint32_t u) { return __half2float(__ushort_as_half(static_cast<unsigned short>(u & 0xFFFFu))); }
+    __device__ static float hi(uint32_t u) { return __half2float(__ushort_as_half(static_cast<unsigned short>(u >> 16))); }
 };
+
+// Invalid tokens of a 16-bit vector set to -inf, valid ones kept: the 8 mask bits are spread
+// to byte sign bits with one multiply, then sign-replicating byte permutes build the
+// per-token 16-bit masks (token 2k in the low half of pair k).
+template <typename E>
+__device__ __forceinline__ void mask_pairs(const uint4& r, uint32_t bits8, uint32_t (&q)[4]) {
+    const uint32_t slo = (bits8 & 0xFu) * 0x10204080u;  // byte k sign bit = mask bit k
+    const uint32_t shi = (bits8 >> 4) * 0x10204080u;    // byte k sign bit = mask bit 4 + k
+    q[0] = ptx::select_bits(r.x, ptx::prmt(slo, 0u, 0x9988u), E::kNegInf2);
+    q[1] = ptx::select_bits(r.y, ptx::prmt(slo, 0u, 0xBBAAu), E::kNegInf2);
+    q[2] = ptx::select_bits(r.z, ptx::prmt(shi, 0u, 0x9988u), E::kNegInf2);
+    q[3] = ptx::select_bits(r.w, ptx::prmt(shi, 0u, 0xBBAAu), E::kNegInf2);
+}
+
+// Sum over a lane's 32 (16-bit) or 16 (fp32) masked tokens of 2^((x - m) log2(e) / T),
+// pairwise per vector then across vectors.  Invalid tokens hold -inf (weight 0).
+template <typename E, bool kClamp>
+__device__ __forceinline__ float lane_mass(const uint32_t (&q16)[kVecsPerLane][4],
+                                           const float (&q32)[kVecsPerLane][E::kVec], float nhm, float sc2) {
+    constexpr int kVec = E::kVec;
+    float part[kVecsPerLane];
+#pragma unroll
+    for (int j = 0; j < kVecsPerLane; ++j) {
+        float w[kVec];
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) {
+            float x;
+            if constexpr (E::kBytes == 2) x = (i & 1) ? E::hi(q16[j][i >> 1]) : E::lo(q16[j][i >> 1]);
+            else x = q32[j][i];
+            float t = fmaf(x, 0.5f, nhm) * sc2;
+            if constexpr (kClamp) t = fminf(t, 0.0f);
+            w[i] = ptx::ex2(t);
+        }
+#pragma unroll
+        for (int h = kVec / 2; h >= 1; h >>= 1)
+#pragma unroll
+            for (int i = 0; i < h; ++i) w[i] += w[i + h];
+        part[j] = w[0];
+    }
+#pragma unroll
+    for (int h = kVecsPerLane / 2; h >= 1; h >>= 1)
+#pragma unroll
+        for (int i = 0; i < h; ++i) part[i] += part[i + h];
+    return part[0];
+}
 
 // ----------------------------------------------------------------- params
 struct SelectParams {
@@ -283,7 +336,7 @@ __device__ __forceinline__ int block_max_int(Shared& sh, int v, int tid) {
 
 // ----------------------------------------------------------------- the kernel
 template <typename T, bool kSample, bool kBulk, int kStages>
-__global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const SelectParams p) {
+__global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(const SelectParams p) {
     using E = Elem<T>;
     using L = Layout<T>;
     constexpr int kVec = E::kVec;
@@ -319,6 +372,9 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const SelectPa
         ptx::fence_mbarrier_init();
     }
     __syncthreads();
+    // A programmatic dependent (the verification epilogue) may start launching now; it waits
+    // for this grid's completion before reading any output.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Every CTA of the cluster has initialised its barriers before any remote arrive.
     ptx::cluster_arrive();
     ptx::cluster_wait();
@@ -371,9 +427,10 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const SelectPa
             const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
             typename E::NanAcc nan_acc = E::nan_init();
             uint32_t count = 0;
-            // argmax state
-            float best = 0.0f;
+            // argmax state: lane's running masked max and the chunk it came from
+            float best = -__int_as_float(0x7F800000);
             int best_idx = -1;
+            int first_valid_chunk = -1;
             // sampler state (warp-uniform running max of valid logits)
             float run_m = -__int_as_float(0x7F800000);
 
@@ -431,78 +488,93 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const SelectPa
                 const int64_t wtok0 = t0 + warp * kTPW;
 
                 if constexpr (!kSample) {
-#pragma unroll
-                    for (int j = 0; j < kVecsPerLane; ++j) {
-                        E::nan_update(nan_acc, raw[j]);
-                        count += __popc(bits[j]);
-                        float v[kVec];
-                        E::decode(raw[j], v);
-                        float mv[kVec];
-#pragma unroll
-                        for (int i = 0; i < kVec; ++i)
-                            mv[i] = ((bits[j] >> i) & 1u) ? v[i] : __int_as_float(0x7FFFFFFF);
-                        float vmax = mv[0];
-#pragma unroll
-                        for (int i = 1; i < kVec; ++i) vmax = fmaxf(vmax, mv[i]);
-                        if (vmax > best || (best_idx < 0 && vmax == vmax)) {
-                            int first = 0;
-#pragma unroll
-                            for (int i = kVec - 1; i >= 0; --i)
-                                if (mv[i] == vmax) first = i;
-                            best = vmax;
-                            best_idx = static_cast<int>(wtok0 + (j * 32 + lane) * kVec + first);
-                        }
-                    }
-                } else {
-                    // Pass 1 over registers: NaN, count, masked chunk max.
-                    float lmax = __int_as_float(0x7FFFFFFF);
-#pragma unroll
-                    for (int j = 0; j < kVecsPerLane; ++j) {
-                        E::nan_update(nan_acc, raw[j]);
-                        count += __popc(bits[j]);
-                        float v[kVec];
-                        E::decode(raw[j], v);
-#pragma unroll
-                        for (int i = 0; i < kVec; ++i)
-                            if ((bits[j] >> i) & 1u) lmax = fmaxf(lmax, v[i]);
-                    }
-                    // Warp max over lanes (NaN = no valid token in the lane).
-                    const uint32_t lkey = (lmax == lmax) ? ordered_bits(lmax) : 0u;
-                    const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, lkey);
-                    if (wkey != 0u) {
-                        const float wmax = ordered_to_float(wkey);
-                        run_m = fmaxf(run_m, wmax);
-                    }
-                    // Pass 2: fp32 weights relative to the running max (all exponents <= 0).
-                    float mass = 0.0f;
-                    const bool finite_m = run_m > -__int_as_float(0x7F800000) && run_m < __int_as_float(0x7F800000);
-                    if (finite_m) {
-                        const float nhm = -0.5f * run_m;
-                        const float sc2 = p.scale2;
-                        float part[kVecsPerLane];
+                    // Masked max of the lane's tokens in this chunk (invalid tokens = -inf).  Only
+                    // the chunk where the lane's max first reached its value is remembered; the
+                    // token index is recovered at the end of the row by the winning lane(s).
+                    float vmax;
+                    uint32_t anyb = 0u;
+                    if constexpr (E::kBytes == 2) {
+                        uint32_t t = E::kNegInf2;
 #pragma unroll
                         for (int j = 0; j < kVecsPerLane; ++j) {
+                            E::nan_update(nan_acc, raw[j]);
+                            count += __popc(bits[j]);
+                            anyb |= bits[j];
+                            uint32_t q[4];
+                            mask_pairs<E>(raw[j], bits[j], q);
+                            t = E::max2(t, E::max2(E::max2(q[0], q[1]), E::max2(q[2], q[3])));
+                        }
+                        vmax = fmaxf(E::lo(t), E::hi(t));
+                    } else {
+                        vmax = -__int_as_float(0x7F800000);
+#pragma unroll
+                        for (int j = 0; j < kVecsPerLane; ++j) {
+                            E::nan_update(nan_acc, raw[j]);
+                            count += __popc(bits[j]);
+                            anyb |= bits[j];
                             float v[kVec];
                             E::decode(raw[j], v);
-                            float w[kVec];
+#pragma unroll
+                            for (int i = 0; i < kVec; ++i)
+                                vmax = fmaxf(vmax, ((bits[j] >> i) & 1u) ? v[i] : -__int_as_float(0x7F800000));
+                        }
+                    }
+                    if (vmax > best) {
+                        best = vmax;
+                        best_idx = c;  // chunk index of the lane's running max
+                    }
+                    if (first_valid_chunk < 0 && anyb != 0u) first_valid_chunk = c;
+                } else {
+                    // Pass 1 over registers: NaN, count, masked values (-inf where invalid), chunk max.
+                    float lmax = -__int_as_float(0x7F800000);
+                    uint32_t anyb = 0u;
+                    uint32_t q16[kVecsPerLane][4];
+                    float q32[kVecsPerLane][kVec];
+#pragma unroll
+                    for (int j = 0; j < kVecsPerLane; ++j) {
+                        E::nan_update(nan_acc, raw[j]);
+                        count += __popc(bits[j]);
+                        anyb |= bits[j];
+                        if constexpr (E::kBytes == 2) {
+                            mask_pairs<E>(raw[j], bits[j], q16[j]);
+                        } else {
+                            float v[kVec];
+                            E::decode(raw[j], v);
 #pragma unroll
                             for (int i = 0; i < kVec; ++i) {
-                                const float t = fmaf(v[i], 0.5f, nhm) * sc2;
-                                const float e = ptx::ex2(fminf(t, 0.0f));
-                                w[i] = ((bits[j] >> i) & 1u) ? e : 0.0f;
+                                q32[j][i] = ((bits[j] >> i) & 1u) ? v[i] : -__int_as_float(0x7F800000);
+                                lmax = fmaxf(lmax, q32[j][i]);
                             }
-                            // Pairwise sum of the vector's weights.
-#pragma unroll
-                            for (int h = kVec / 2; h >= 1; h >>= 1)
-#pragma unroll
-                                for (int i = 0; i < h; ++i) w[i] += w[i + h];
-                            part[j] = w[0];
                         }
-#pragma unroll
-                        for (int h = kVecsPerLane / 2; h >= 1; h >>= 1)
-#pragma unroll
-                            for (int i = 0; i < h; ++i) part[i] += part[i + h];
-                        mass = part[0];
+                    }
+                    if constexpr (E::kBytes == 2) {
+                        uint32_t t = E::max2(E::max2(E::max2(q16[0][0], q16[0][1]), E::max2(q16[0][2], q16[0][3])),
+                                             E::max2(E::max2(q16[1][0], q16[1][1]), E::max2(q16[1][2], q16[1][3])));
+                        t = E::max2(t, E::max2(E::max2(E::max2(q16[2][0], q16[2][1]), E::max2(q16[2][2], q16[2][3])),
+                                               E::max2(E::max2(q16[3][0], q16[3][1]), E::max2(q16[3][2], q16[3][3]))));
+                        lmax = fmaxf(E::lo(t), E::hi(t));
+                    }
+                    // Warp-uniform running max over valid tokens (NaN valid logits are ignored here;
+                    // they fail the row through the NaN flag).
+                    const bool warp_any = __any_sync(0xFFFFFFFFu, anyb != 0u);
+                    if (warp_any) {
+                        const uint32_t lkey = (lmax == lmax) ? ordered_bits(lmax) : 0u;
+                        const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, lkey);
+                        if (wkey != 0u) run_m = fmaxf(run_m, ordered_to_float(wkey));
+                    }
+                    // Pass 2: fp32 weights 2^((x - m) * log2(e) / T) relative to the running max,
+                    // invalid tokens entering as -inf (weight 0).  scale2 = 2 log2(e) / T with
+                    // x - m formed as 0.5x - 0.5m so it cannot overflow.
+                    float mass = 0.0f;
+                    const bool finite_m = run_m > -__int_as_float(0x7F800000) && run_m < __int_as_float(0x7F800000);
+                    if (warp_any && finite_m) {
+                        const float nhm = -0.5f * run_m;
+                        const float sc2 = p.scale2;
+                        // An infinite scale (T below ~1e-38) turns x == m into 0 * inf: clamp then.
+                        if (sc2 < __int_as_float(0x7F800000))
+                            mass = lane_mass<E, false>(q16, q32, nhm, sc2);
+                        else
+                            mass = lane_mass<E, true>(q16, q32, nhm, sc2);
 #pragma unroll
                         for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
                     }
@@ -517,14 +589,33 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const SelectPa
             const uint32_t wnan = __any_sync(0xFFFFFFFFu, nan_local) ? kFlagNaN : 0u;
             uint32_t cta_hi = 0, cta_lo = 0, cta_count = 0, cta_flags = 0;
             if constexpr (!kSample) {
-                const uint32_t hi = best_idx >= 0 ? ordered_bits(best) : 0u;
-                const uint32_t whi = __reduce_max_sync(0xFFFFFFFFu, hi);
-                const uint32_t lo = (best_idx >= 0 && hi == whi) ? (0xFFFFFFFFu - static_cast<uint32_t>(best_idx)) : 0u;
-                const uint32_t wlo = __reduce_max_sync(0xFFFFFFFFu, lo);
-                if (lane == 0) {
-                    sh.warp_key_hi[warp] = whi;
-                    sh.warp_key_lo[warp] = wlo;
+                // Segment maximum first, then the lowest token holding it: only lanes whose
+                // running max equals it re-read their 16-byte slices of that one chunk.
+                const bool has = best_idx >= 0 || first_valid_chunk >= 0;
+                const uint32_t key = has ? ordered_bits(best) : 0u;
+                const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, key);
+                if (lane == 0) sh.warp_key_hi[warp] = wkey;
+                ptx::named_sync(1, kConsumerThreads);
+                uint32_t ckey = 0u;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) ckey = max(ckey, sh.warp_key_hi[w]);
+                uint32_t found = 0xFFFFFFFFu;
+                if (has && key == ckey) {
+                    const int chunk = best_idx >= 0 ? best_idx : first_valid_chunk;
+                    const int64_t base = seg_begin + static_cast<int64_t>(chunk) * kTPC + warp * kTPW;
+#pragma unroll
+                    for (int j = 0; j < kVecsPerLane; ++j) {
+#pragma unroll
+                        for (int i = 0; i < kVec; ++i) {
+                            const int64_t tok = base + (j * 32 + lane) * kVec + i;
+                            if (found == 0xFFFFFFFFu && tok < seg_end &&
+                                ((static_cast<uint32_t>(mrow[tok >> 5]) >> (tok & 31)) & 1u) && E::load(lrow, tok) == best)
+                                found = static_cast<uint32_t>(tok);
+                        }
+                    }
                 }
+                const uint32_t wfound = __reduce_min_sync(0xFFFFFFFFu, found);
+                if (lane == 0) sh.warp_key_lo[warp] = wfound == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - wfound;
             } else {
                 if (lane == 0) sh.warp_m[warp] = (run_m == run_m) ? ordered_bits(run_m) : 0u;
             }
