@@ -20,14 +20,20 @@
 //    warps loading the chunk themselves (kBulk = false).
 //  * Consumer warp w of a chunk owns a contiguous 2 KB slice; each lane reads
 //    16-byte vectors and the mask bits covering them from shared memory.
-//  * Per-row partials are merged warp -> CTA with redux.sync and named
-//    barriers, then across the cluster by an all-gather through distributed
-//    shared memory (st.shared::cluster + remote mbarrier arrive).  Argmax keys
-//    are (order-preserving float bits << 32 | ~index), so the merge is a max.
+//  * Consumer warps only stream: at the end of a row each warp reduces its own
+//    partial with redux.sync and hands it to a finalizer warp through a
+//    double-buffered shared-memory slot guarded by mbarriers, then starts the
+//    next row.  The finalizer merges the eight warp partials, recovers the
+//    argmax index by re-reading the one 2 KB warp slice that holds the first
+//    maximum, all-gathers the CTA partials across the cluster through
+//    distributed shared memory (st.shared::cluster + remote mbarrier arrive)
+//    and writes the row's outputs -- overlapped with the next row's streaming.
+//    Argmax keys are (order-preserving float bits << 32 | ~index): a max merge.
 //  * The sampler records one (max, mass) pair per (chunk, warp) "granule" in
-//    shared memory during the single streaming pass (fp32 MUFU ex2 weights),
-//    merges ranks in fixed order in fp64, then re-reads only the granule that
-//    holds u * total and walks it with exact fp64 weights exp((x - M) / T).
+//    shared memory during the single streaming pass (fp32 MUFU ex2 weights);
+//    the finalizer merges ranks in fixed order in fp64, then re-reads only the
+//    granule that holds u * total and walks it with exact fp64 weights
+//    exp((x - M) / T).
 //  * Every wait is bounded (about one second, %globaltimer); on expiry the CTA
 //    stops waiting, reports status 7 for its rows and still completes the
 //    cluster protocol, so no wait can hang the GPU.
@@ -43,7 +49,9 @@ namespace bms {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
+constexpr int kProducerWarp = kConsumerWarps;       // bulk-copy issue
+constexpr int kFinalizerWarp = kConsumerWarps + 1;  // per-row merge, index recovery, sampling walk
+constexpr int kThreads = kConsumerThreads + 64;
 constexpr int kChunkBytes = 16384;               // logits bytes per stage
 constexpr int kWarpBytes = kChunkBytes / kConsumerWarps;
 constexpr int kVecsPerLane = kWarpBytes / 16 / 32;  // 16-byte vectors per lane per chunk
@@ -239,23 +247,26 @@ struct alignas(16) GatherSlot {
     double pad;
 };
 
-struct alignas(16) Shared {
-    uint64_t full[8];
-    uint64_t empty[8];
-    uint64_t gather[2];
-    GatherSlot slots[2][kMaxCluster];
-    uint32_t warp_key_hi[kConsumerWarps];
-    uint32_t warp_key_lo[kConsumerWarps];
-    uint32_t warp_count[kConsumerWarps];
-    uint32_t warp_flags[kConsumerWarps];
-    uint32_t warp_m[kConsumerWarps];   // sampler: warp running max (ordered bits)
-    double scan[kConsumerThreads / 32 + 1];
-    double bcast_d[4];
-    int32_t bcast_i[4];
-    volatile int32_t abort;
+// One consumer warp's contribution to one row.
+struct alignas(16) WarpPartial {
+    uint32_t key;    // argmax: ordered masked max (0 = no valid token) | sampler: ordered running max
+    uint32_t chunk;  // argmax: first chunk in which a lane of this warp reached `key`
+    uint32_t count;  // valid tokens
+    uint32_t flags;  // kFlagNaN
 };
 
 constexpr int kStagesMax = 8;
+
+struct alignas(16) Shared {
+    uint64_t full[kStagesMax];
+    uint64_t empty[kStagesMax];
+    uint64_t part_full[2];   // consumers -> finalizer, one arrive per consumer warp
+    uint64_t part_empty[2];  // finalizer -> consumers, slot (and granule table) reusable
+    uint64_t gather[2];      // cluster all-gather, one arrive per rank
+    GatherSlot slots[2][kMaxCluster];
+    WarpPartial part[2][kConsumerWarps];
+    volatile int32_t abort;
+};
 
 // Bounded mbarrier wait.  Returns false (and latches `abort`) after kTimeoutNs.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int32_t* abort,
@@ -280,7 +291,7 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     }
 }
 
-// ----------------------------------------------------------------- block scan helpers (consumers only)
+// ----------------------------------------------------------------- warp helpers (finalizer)
 __device__ __forceinline__ double warp_inclusive_scan(double v, int lane) {
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -290,48 +301,51 @@ __device__ __forceinline__ double warp_inclusive_scan(double v, int lane) {
     return v;
 }
 
-// Exclusive scan of one double per consumer thread in thread order; also returns the total.
-__device__ __forceinline__ double block_exclusive_scan(Shared& sh, double v, int tid, double& total) {
-    const int lane = tid & 31, warp = tid >> 5;
-    const double inc = warp_inclusive_scan(v, lane);
-    if (lane == 31) sh.scan[warp] = inc;
-    ptx::named_sync(1, kConsumerThreads);
-    if (warp == 0) {
-        double w = lane < kConsumerWarps ? sh.scan[lane] : 0.0;
-        const double wi = warp_inclusive_scan(w, lane);
-        if (lane < kConsumerWarps) sh.scan[lane] = wi - w;  // exclusive warp prefix
-        if (lane == kConsumerWarps - 1) sh.scan[kConsumerWarps] = wi;
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// exp((x - M) / T) for a valid, finite-or(-inf) logit; the reference's weight.
+__device__ __forceinline__ double exact_weight(float x, double M, double T) {
+    return x > -__int_as_float(0x7F800000) ? exp((static_cast<double>(x) - M) / T) : 0.0;
+}
+
+__device__ __forceinline__ double granule_mass(float2 e, double M, double T) {
+    return e.y > 0.0f ? static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / T) : 0.0;
+}
+
+// Loads a lane's slice [t0, t0 + n) of a row with independent loads (tokens at or past `end`
+// read as 0 with their mask bits cleared); returns the slice's mask bits.
+template <typename E, int n>
+__device__ __forceinline__ uint32_t load_lane_slice(const uint8_t* lrow, const int32_t* mrow, int64_t t0, int64_t end,
+                                                    float (&v)[n]) {
+    static_assert(n <= 32, "slice must fit one mask word");
+    uint32_t word = t0 < end ? static_cast<uint32_t>(mrow[t0 >> 5]) >> (t0 & 31) : 0u;
+#pragma unroll
+    for (int i = 0; i < n; ++i) v[i] = (t0 + i < end) ? E::load(lrow, t0 + i) : 0.0f;
+    const int64_t avail = end - t0;
+    if (avail < n) word &= avail <= 0 ? 0u : ((1u << avail) - 1u);
+    if constexpr (n < 32) word &= (1u << n) - 1u;
+    return word;
+}
+
+// All-gather of one 32-byte slot per rank across the cluster (finalizer lane 0 issues it;
+// the caller syncs the warp before reading).  Rank q's data lands in slots[slot][q] of every CTA.
+__device__ __forceinline__ void cluster_allgather(Shared& sh, uint32_t slot, uint32_t crank, uint32_t csize,
+                                                  const GatherSlot& mine, uint32_t parity) {
+    const uint32_t local = ptx::smem_addr(&sh.slots[slot][crank]);
+    const uint32_t bar = ptx::smem_addr(&sh.gather[slot]);
+    uint32_t sbits[2];
+    memcpy(sbits, &mine.s, 8);
+    for (uint32_t q = 0; q < csize; ++q) {
+        const uint32_t dst = ptx::mapa(local, q);
+        ptx::st_cluster_v4(dst, mine.a, mine.b, mine.c, mine.d);
+        ptx::st_cluster_v4(dst + 16, sbits[0], sbits[1], 0u, 0u);
+        ptx::mbar_arrive_remote(ptx::mapa(bar, q));
     }
-    ptx::named_sync(1, kConsumerThreads);
-    total = sh.scan[kConsumerWarps];
-    const double out = sh.scan[warp] + inc - v;
-    ptx::named_sync(1, kConsumerThreads);  // scan[] reusable after this
-    return out;
-}
-
-__device__ __forceinline__ int block_min_int(Shared& sh, int v, int tid) {
-    const int lane = tid & 31, warp = tid >> 5;
-    v = __reduce_min_sync(0xFFFFFFFFu, v);
-    if (lane == 0) sh.bcast_i[0] = 0x7FFFFFFF;
-    ptx::named_sync(1, kConsumerThreads);
-    if (lane == 0) atomicMin(const_cast<int32_t*>(&sh.bcast_i[0]), v);
-    ptx::named_sync(1, kConsumerThreads);
-    const int r = sh.bcast_i[0];
-    ptx::named_sync(1, kConsumerThreads);
-    (void)warp;
-    return r;
-}
-
-__device__ __forceinline__ int block_max_int(Shared& sh, int v, int tid) {
-    const int lane = tid & 31;
-    v = __reduce_max_sync(0xFFFFFFFFu, v);
-    if (tid == 0) sh.bcast_i[1] = -0x7FFFFFFF - 1;
-    ptx::named_sync(1, kConsumerThreads);
-    if (lane == 0) atomicMax(const_cast<int32_t*>(&sh.bcast_i[1]), v);
-    ptx::named_sync(1, kConsumerThreads);
-    const int r = sh.bcast_i[1];
-    ptx::named_sync(1, kConsumerThreads);
-    return r;
+    wait_bounded(ptx::smem_addr(&sh.gather[slot]), parity, &sh.abort, true);
 }
 
 // ----------------------------------------------------------------- the kernel
@@ -343,11 +357,14 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
     constexpr int kTPC = L::kTokensPerChunk;
     constexpr int kTPW = L::kTokensPerWarp;
     constexpr uint32_t kVecMask = (1u << kVec) - 1u;
+    constexpr int kGranules = kMaxChunksSampler * kConsumerWarps;
+    constexpr int kFinPer = kTPW / 32;
+    const float kInf = __int_as_float(0x7F800000);
 
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* stages = smem_raw;
     Shared& sh = *reinterpret_cast<Shared*>(smem_raw + kStages * L::kStageBytes);
-    float2* granules = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(Shared));
+    float2* granule_base = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(Shared));
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -366,8 +383,11 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
             ptx::mbar_init(ptx::smem_addr(&sh.full[s]), 1);
             ptx::mbar_init(ptx::smem_addr(&sh.empty[s]), kConsumerWarps);
         }
-        ptx::mbar_init(ptx::smem_addr(&sh.gather[0]), csize);
-        ptx::mbar_init(ptx::smem_addr(&sh.gather[1]), csize);
+        for (int s = 0; s < 2; ++s) {
+            ptx::mbar_init(ptx::smem_addr(&sh.part_full[s]), kConsumerWarps);
+            ptx::mbar_init(ptx::smem_addr(&sh.part_empty[s]), 1);
+            ptx::mbar_init(ptx::smem_addr(&sh.gather[s]), csize);
+        }
         sh.abort = 0;
         ptx::fence_mbarrier_init();
     }
@@ -379,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
     ptx::cluster_arrive();
     ptx::cluster_wait();
 
-    if (warp == kConsumerWarps) {
+    if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer warp
         if (kBulk && lane == 0) {
             uint32_t it = 0;
@@ -417,22 +437,237 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
             }
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------------------ consumer warps
-        uint32_t it = 0;
-        uint32_t k = 0;  // rows processed by this cluster (gather phase)
+    } else if (warp == kFinalizerWarp) {
+        // ------------------------------------------------------------ finalizer warp
+        uint32_t k = 0;
         for (int64_t row = cid; row < p.rows; row += nclusters, ++k) {
+            const uint32_t slot = k & 1u;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+            wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort);
+            const bool in = lane < kConsumerWarps;
+            const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u};
+            const uint32_t cnt = __reduce_add_sync(0xFFFFFFFFu, wp.count);
+            const uint32_t flags = __reduce_or_sync(0xFFFFFFFFu, wp.flags) | (sh.abort ? kFlagAbort : 0u);
+            const uint32_t ckey = __reduce_max_sync(0xFFFFFFFFu, wp.key);
+
+            if constexpr (!kSample) {
+                // First (chunk, warp) region holding the segment maximum; its lowest valid token
+                // equal to the maximum is the segment's argmax.
+                const uint32_t region = (in && ckey != 0u && wp.key == ckey) ? (wp.chunk * kConsumerWarps + lane)
+                                                                              : 0xFFFFFFFFu;
+                const uint32_t rmin = __reduce_min_sync(0xFFFFFFFFu, region);
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
+                uint32_t found = 0xFFFFFFFFu;
+                if (rmin != 0xFFFFFFFFu) {
+                    const float target = ordered_to_float(ckey);
+                    const int64_t r0 = seg_begin + static_cast<int64_t>(rmin / kConsumerWarps) * kTPC +
+                                       static_cast<int64_t>(rmin % kConsumerWarps) * kTPW;
+                    const int64_t my0 = r0 + lane * kFinPer;
+                    float v[kFinPer];
+                    const uint32_t word = load_lane_slice<E>(lrow, mrow, my0, seg_end, v);
+#pragma unroll
+                    for (int i = kFinPer - 1; i >= 0; --i)
+                        if (((word >> i) & 1u) && v[i] == target) found = static_cast<uint32_t>(my0 + i);
+                }
+                uint32_t hi = ckey;
+                uint32_t lo = __reduce_min_sync(0xFFFFFFFFu, found);
+                lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - lo;
+                uint32_t total = cnt, fl = flags;
+                if (csize > 1) {
+                    if (lane == 0)
+                        cluster_allgather(sh, slot, crank, csize, GatherSlot{hi, lo, total, fl, 0.0, 0.0}, (k >> 1) & 1u);
+                    __syncwarp();
+                    const bool inr = lane < static_cast<int>(csize);
+                    const GatherSlot g = inr ? sh.slots[slot][lane] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
+                    hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
+                    lo = __reduce_max_sync(0xFFFFFFFFu, (inr && g.a == hi) ? g.b : 0u);
+                    total = __reduce_add_sync(0xFFFFFFFFu, g.c);
+                    fl = __reduce_or_sync(0xFFFFFFFFu, g.d) | (sh.abort ? kFlagAbort : 0u);
+                }
+                if (crank == 0 && lane == 0) {
+                    const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
+                    p.status[row] = code;
+                    p.tokens[row] = code == kOk ? p.token_offset + static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
+                    if (p.counts) p.counts[row] = total;
+                }
+            } else {
+                // Segment maximum and mass relative to it (granules in fixed (chunk, warp) order).
+                const float2* granules = granule_base + slot * kGranules;
+                const int ngran = nchunks * kConsumerWarps;
+                const float seg_m = ckey ? ordered_to_float(ckey) : -kInf;
+                const bool seg_finite = seg_m > -kInf && seg_m < kInf;
+                double term = 0.0;
+                if (seg_finite)
+                    for (int g = lane; g < ngran; g += 32) term += granule_mass(granules[g], seg_m, p.temperature);
+                const double seg_s = warp_sum(term);
+                // Rank partials, all-gathered in rank order.
+                if (lane == 0) {
+                    const GatherSlot mine{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
+                    if (csize > 1) cluster_allgather(sh, slot, crank, csize, mine, (k >> 1) & 1u);
+                    else sh.slots[slot][0] = mine;
+                }
+                __syncwarp();
+                float rm = -kInf;
+                uint32_t total = 0, fl = sh.abort ? kFlagAbort : 0u;
+                for (uint32_t q = 0; q < csize; ++q) {
+                    const GatherSlot& g = sh.slots[slot][q];
+                    rm = fmaxf(rm, __uint_as_float(g.a));
+                    total += g.b;
+                    fl |= g.c;
+                }
+                const double u = p.uniforms[row];
+                const int32_t code = (fl & kFlagAbort) ? kTimeout
+                                     : (fl & kFlagNaN) ? kNaN
+                                     : (rm == kInf) ? kPosInf
+                                     : (total == 0u) ? kEmpty
+                                     : (rm == -kInf) ? kNoMass
+                                     : !(u >= 0.0 && u < 1.0) ? kBadUniform
+                                                              : kOk;
+                if (code != kOk) {
+                    if (crank == 0 && lane == 0) {
+                        p.status[row] = code;
+                        p.tokens[row] = -1;
+                        if (p.counts) p.counts[row] = total;
+                    }
+                } else {
+                    const double M = rm;
+                    const double temp = p.temperature;
+                    // Rank masses in rank order; the owner holds the first crossing of u * total.
+                    double total_mass = 0.0;
+                    for (uint32_t q = 0; q < csize; ++q) {
+                        const GatherSlot& g = sh.slots[slot][q];
+                        if (g.s > 0.0) total_mass += g.s * exp((static_cast<double>(__uint_as_float(g.a)) - M) / temp);
+                    }
+                    const double cutoff = u * total_mass;
+                    int owner = -1, last_pos = -1;
+                    double prefix = 0.0, run = 0.0, last_prefix = 0.0;
+                    for (uint32_t q = 0; q < csize; ++q) {
+                        const GatherSlot& g = sh.slots[slot][q];
+                        const double m = g.s > 0.0 ? g.s * exp((static_cast<double>(__uint_as_float(g.a)) - M) / temp) : 0.0;
+                        if (!(m > 0.0)) continue;
+                        last_pos = static_cast<int>(q);
+                        last_prefix = run;
+                        if (owner < 0 && cutoff < run + m) {
+                            owner = static_cast<int>(q);
+                            prefix = run;
+                        }
+                        run += m;
+                    }
+                    const bool fallback = owner < 0;
+                    if (fallback) {
+                        owner = last_pos;
+                        prefix = last_prefix;
+                    }
+                    if (owner == static_cast<int>(crank)) {
+                        // Granule holding the crossing: contiguous blocks of granules per lane.
+                        const int per = (ngran + 31) / 32;
+                        const int g0 = lane * per, g1 = min(g0 + per, ngran);
+                        double local = 0.0;
+                        for (int g = g0; g < g1; ++g) local += granule_mass(granules[g], M, temp);
+                        const double incl = warp_inclusive_scan(local, lane);
+                        double acc = prefix + incl - local;
+                        int cand = 0x7FFFFFFF, lastg = -1;
+                        double cand_prefix = 0.0;
+                        for (int g = g0; g < g1; ++g) {
+                            const double m = granule_mass(granules[g], M, temp);
+                            if (!(m > 0.0)) continue;
+                            lastg = g;
+                            if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) {
+                                cand = g;
+                                cand_prefix = acc;
+                            }
+                            acc += m;
+                        }
+                        int gsel = __reduce_min_sync(0xFFFFFFFFu, cand);
+                        const bool walk_fallback = gsel == 0x7FFFFFFF;
+                        double gprefix = 0.0;
+                        if (walk_fallback) {
+                            gsel = __reduce_max_sync(0xFFFFFFFFu, lastg);
+                        } else {
+                            const uint32_t owner_lane = __ffs(__ballot_sync(0xFFFFFFFFu, cand == gsel)) - 1;
+                            gprefix = __shfl_sync(0xFFFFFFFFu, cand_prefix, owner_lane);
+                        }
+                        int64_t chosen = -1;
+                        if (gsel >= 0) {
+                            // Walk the granule in token order with exact fp64 weights.
+                            const int gc = gsel / kConsumerWarps, gw = gsel % kConsumerWarps;
+                            const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
+                            const int64_t gt1 = min(gt0 + kTPW, seg_end);
+                            const int64_t my0 = gt0 + lane * kFinPer;
+                            float v[kFinPer];
+                            const uint32_t word = load_lane_slice<E>(lrow, mrow, my0, gt1, v);
+                            double wsum = 0.0;
+                            int64_t lastpos = -1;
+#pragma unroll
+                            for (int i = 0; i < kFinPer; ++i) {
+                                if (!((word >> i) & 1u)) continue;
+                                const double w = exact_weight(v[i], M, temp);
+                                if (w > 0.0) lastpos = my0 + i;
+                                wsum += w;
+                            }
+                            const double wincl = warp_inclusive_scan(wsum, lane);
+                            int64_t hit = INT64_MAX;
+                            if (!walk_fallback) {
+                                const double before = gprefix + wincl - wsum;
+                                if (cutoff < gprefix + wincl && cutoff >= before) {
+                                    // This lane's tokens hold the crossing: walk them again in order.
+                                    double a = before;
+                                    for (int i = 0; i < kFinPer; ++i) {
+                                        if (!((word >> i) & 1u)) continue;
+                                        const double w = exact_weight(v[i], M, temp);
+                                        if (!(w > 0.0)) continue;
+                                        a += w;
+                                        if (cutoff < a) {
+                                            hit = my0 + i;
+                                            break;
+                                        }
+                                    }
+                                }
+                            }
+                            const int hit32 = hit == INT64_MAX ? 0x7FFFFFFF : static_cast<int>(hit - gt0);
+                            const int hmin = __reduce_min_sync(0xFFFFFFFFu, hit32);
+                            if (hmin != 0x7FFFFFFF) {
+                                chosen = gt0 + hmin;
+                            } else {
+                                // Rounding left the crossing past the granule's last positive weight.
+                                const int lp = __reduce_max_sync(0xFFFFFFFFu, lastpos < 0 ? -1 : static_cast<int>(lastpos - gt0));
+                                chosen = lp >= 0 ? gt0 + lp : -1;
+                            }
+                        }
+                        if (lane == 0) {
+                            p.status[row] = chosen >= 0 ? kOk : kNoMass;
+                            p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
+                            if (p.counts) p.counts[row] = total;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ consumer warps
+        uint32_t it = 0;
+        uint32_t k = 0;  // rows processed by this cluster
+        for (int64_t row = cid; row < p.rows; row += nclusters, ++k) {
+            const uint32_t slot = k & 1u;
+            const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                                  static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+            const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+            // The finalizer has released this row's partial slot (and granule table).
+            if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
+            float2* granules = granule_base + slot * kGranules;
             typename E::NanAcc nan_acc = E::nan_init();
             uint32_t count = 0;
-            // argmax state: lane's running masked max and the chunk it came from
-            float best = -__int_as_float(0x7F800000);
+            // argmax: lane's running masked max and the chunk it came from
+            float best = -kInf;
             int best_idx = -1;
             int first_valid_chunk = -1;
-            // sampler state (warp-uniform running max of valid logits)
-            float run_m = -__int_as_float(0x7F800000);
+            // sampler: warp-uniform running max of valid logits
+            float run_m = -kInf;
 
             for (int c = 0; c < nchunks; ++c, ++it) {
                 const int stage = kBulk ? static_cast<int>(it % kStages) : 0;
@@ -456,9 +691,9 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                     const int nwords = (ntok + 31) >> 5;
                     for (int i = tid; i < nwords; i += kConsumerThreads) {
                         uint32_t wv = static_cast<uint32_t>(mrow[(t0 >> 5) + i]);
-                        const int64_t last_tok = t0 + 32 * static_cast<int64_t>(i) + 31;
-                        if (last_tok >= p.vocab) {
-                            const int keep = static_cast<int>(p.vocab - (t0 + 32 * static_cast<int64_t>(i)));
+                        const int64_t first_tok = t0 + 32 * static_cast<int64_t>(i);
+                        if (first_tok + 31 >= p.vocab) {
+                            const int keep = static_cast<int>(p.vocab - first_tok);
                             wv &= keep >= 32 ? 0xFFFFFFFFu : ((1u << keep) - 1u);
                         }
                         reinterpret_cast<uint32_t*>(st + kChunkBytes)[i] = wv;
@@ -484,13 +719,14 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                 if constexpr (kBulk) {
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.empty[stage]));
+                } else {
+                    ptx::named_sync(1, kConsumerThreads);  // stage 0 reusable
                 }
-                const int64_t wtok0 = t0 + warp * kTPW;
 
                 if constexpr (!kSample) {
                     // Masked max of the lane's tokens in this chunk (invalid tokens = -inf).  Only
                     // the chunk where the lane's max first reached its value is remembered; the
-                    // token index is recovered at the end of the row by the winning lane(s).
+                    // finalizer recovers the token index from that chunk.
                     float vmax;
                     uint32_t anyb = 0u;
                     if constexpr (E::kBytes == 2) {
@@ -506,7 +742,7 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                         }
                         vmax = fmaxf(E::lo(t), E::hi(t));
                     } else {
-                        vmax = -__int_as_float(0x7F800000);
+                        vmax = -kInf;
 #pragma unroll
                         for (int j = 0; j < kVecsPerLane; ++j) {
                             E::nan_update(nan_acc, raw[j]);
@@ -515,18 +751,17 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                             float v[kVec];
                             E::decode(raw[j], v);
 #pragma unroll
-                            for (int i = 0; i < kVec; ++i)
-                                vmax = fmaxf(vmax, ((bits[j] >> i) & 1u) ? v[i] : -__int_as_float(0x7F800000));
+                            for (int i = 0; i < kVec; ++i) vmax = fmaxf(vmax, ((bits[j] >> i) & 1u) ? v[i] : -kInf);
                         }
                     }
                     if (vmax > best) {
                         best = vmax;
-                        best_idx = c;  // chunk index of the lane's running max
+                        best_idx = c;
                     }
                     if (first_valid_chunk < 0 && anyb != 0u) first_valid_chunk = c;
                 } else {
                     // Pass 1 over registers: NaN, count, masked values (-inf where invalid), chunk max.
-                    float lmax = -__int_as_float(0x7F800000);
+                    float lmax = -kInf;
                     uint32_t anyb = 0u;
                     uint32_t q16[kVecsPerLane][4];
                     float q32[kVecsPerLane][kVec];
@@ -542,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                             E::decode(raw[j], v);
 #pragma unroll
                             for (int i = 0; i < kVec; ++i) {
-                                q32[j][i] = ((bits[j] >> i) & 1u) ? v[i] : -__int_as_float(0x7F800000);
+                                q32[j][i] = ((bits[j] >> i) & 1u) ? v[i] : -kInf;
                                 lmax = fmaxf(lmax, q32[j][i]);
                             }
                         }
@@ -566,291 +801,37 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                     // invalid tokens entering as -inf (weight 0).  scale2 = 2 log2(e) / T with
                     // x - m formed as 0.5x - 0.5m so it cannot overflow.
                     float mass = 0.0f;
-                    const bool finite_m = run_m > -__int_as_float(0x7F800000) && run_m < __int_as_float(0x7F800000);
+                    const bool finite_m = run_m > -kInf && run_m < kInf;
                     if (warp_any && finite_m) {
                         const float nhm = -0.5f * run_m;
                         const float sc2 = p.scale2;
                         // An infinite scale (T below ~1e-38) turns x == m into 0 * inf: clamp then.
-                        if (sc2 < __int_as_float(0x7F800000))
-                            mass = lane_mass<E, false>(q16, q32, nhm, sc2);
-                        else
-                            mass = lane_mass<E, true>(q16, q32, nhm, sc2);
+                        if (sc2 < kInf) mass = lane_mass<E, false>(q16, q32, nhm, sc2);
+                        else mass = lane_mass<E, true>(q16, q32, nhm, sc2);
 #pragma unroll
                         for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
                     }
                     if (lane == 0) granules[c * kConsumerWarps + warp] = make_float2(run_m, mass);
                 }
-                if constexpr (!kBulk) ptx::named_sync(1, kConsumerThreads);  // stage 0 reusable
             }
 
-            // ---------------------------------------------------- CTA partial
+            // ---------------------------------------------------- warp partial -> finalizer
             const bool nan_local = E::has_nan(nan_acc);
             const uint32_t wcount = __reduce_add_sync(0xFFFFFFFFu, count);
-            const uint32_t wnan = __any_sync(0xFFFFFFFFu, nan_local) ? kFlagNaN : 0u;
-            uint32_t cta_hi = 0, cta_lo = 0, cta_count = 0, cta_flags = 0;
+            const uint32_t wflags = __any_sync(0xFFFFFFFFu, nan_local) ? kFlagNaN : 0u;
+            uint32_t wkey, wchunk = 0xFFFFFFFFu;
             if constexpr (!kSample) {
-                // Segment maximum first, then the lowest token holding it: only lanes whose
-                // running max equals it re-read their 16-byte slices of that one chunk.
                 const bool has = best_idx >= 0 || first_valid_chunk >= 0;
                 const uint32_t key = has ? ordered_bits(best) : 0u;
-                const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, key);
-                if (lane == 0) sh.warp_key_hi[warp] = wkey;
-                ptx::named_sync(1, kConsumerThreads);
-                uint32_t ckey = 0u;
-#pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) ckey = max(ckey, sh.warp_key_hi[w]);
-                uint32_t found = 0xFFFFFFFFu;
-                if (has && key == ckey) {
-                    const int chunk = best_idx >= 0 ? best_idx : first_valid_chunk;
-                    const int64_t base = seg_begin + static_cast<int64_t>(chunk) * kTPC + warp * kTPW;
-#pragma unroll
-                    for (int j = 0; j < kVecsPerLane; ++j) {
-#pragma unroll
-                        for (int i = 0; i < kVec; ++i) {
-                            const int64_t tok = base + (j * 32 + lane) * kVec + i;
-                            if (found == 0xFFFFFFFFu && tok < seg_end &&
-                                ((static_cast<uint32_t>(mrow[tok >> 5]) >> (tok & 31)) & 1u) && E::load(lrow, tok) == best)
-                                found = static_cast<uint32_t>(tok);
-                        }
-                    }
-                }
-                const uint32_t wfound = __reduce_min_sync(0xFFFFFFFFu, found);
-                if (lane == 0) sh.warp_key_lo[warp] = wfound == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - wfound;
+                wkey = __reduce_max_sync(0xFFFFFFFFu, key);
+                const uint32_t chunk = static_cast<uint32_t>(best_idx >= 0 ? best_idx : first_valid_chunk);
+                wchunk = __reduce_min_sync(0xFFFFFFFFu, (has && key == wkey) ? chunk : 0xFFFFFFFFu);
             } else {
-                if (lane == 0) sh.warp_m[warp] = (run_m == run_m) ? ordered_bits(run_m) : 0u;
+                wkey = ordered_bits(run_m);
             }
             if (lane == 0) {
-                sh.warp_count[warp] = wcount;
-                sh.warp_flags[warp] = wnan;
-            }
-            ptx::named_sync(1, kConsumerThreads);
-            {
-                const bool in = lane < kConsumerWarps;
-                const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, in ? sh.warp_flags[lane] : 0u);
-                cta_count = __reduce_add_sync(0xFFFFFFFFu, in ? sh.warp_count[lane] : 0u);
-                cta_flags = f | (sh.abort ? kFlagAbort : 0u);
-                if constexpr (!kSample) {
-                    const uint32_t hi = in ? sh.warp_key_hi[lane] : 0u;
-                    cta_hi = __reduce_max_sync(0xFFFFFFFFu, hi);
-                    const uint32_t lo = (in && hi == cta_hi) ? sh.warp_key_lo[lane] : 0u;
-                    cta_lo = __reduce_max_sync(0xFFFFFFFFu, lo);
-                } else {
-                    cta_hi = __reduce_max_sync(0xFFFFFFFFu, in ? sh.warp_m[lane] : 0u);
-                }
-            }
-
-            if constexpr (!kSample) {
-                // -------------------------------------------------- argmax finish
-                uint32_t hi = cta_hi, lo = cta_lo, cnt = cta_count, flags = cta_flags;
-                if (csize > 1) {
-                    const uint32_t slot = k & 1u;
-                    if (tid == 0) {
-                        const uint32_t local = ptx::smem_addr(&sh.slots[slot][crank]);
-                        const uint32_t bar = ptx::smem_addr(&sh.gather[slot]);
-                        for (uint32_t q = 0; q < csize; ++q) {
-                            ptx::st_cluster_v4(ptx::mapa(local, q), hi, lo, cnt, flags);
-                            ptx::mbar_arrive_remote(ptx::mapa(bar, q));
-                        }
-                        wait_bounded(ptx::smem_addr(&sh.gather[slot]), (k >> 1) & 1u, &sh.abort, true);
-                    }
-                    ptx::named_sync(1, kConsumerThreads);
-                    if (crank == 0 && warp == 0) {
-                        const bool in = lane < static_cast<int>(csize);
-                        const GatherSlot g = in ? sh.slots[slot][lane] : GatherSlot{0, 0, 0, 0, 0.0, 0.0};
-                        hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
-                        lo = __reduce_max_sync(0xFFFFFFFFu, (in && g.a == hi) ? g.b : 0u);
-                        cnt = __reduce_add_sync(0xFFFFFFFFu, g.c);
-                        flags = __reduce_or_sync(0xFFFFFFFFu, g.d) | (sh.abort ? kFlagAbort : 0u);
-                    }
-                }
-                if (crank == 0 && tid == 0) {
-                    const int32_t code = (flags & kFlagAbort) ? kTimeout
-                                         : (flags & kFlagNaN) ? kNaN
-                                         : (cnt == 0u)        ? kEmpty
-                                                              : kOk;
-                    p.status[row] = code;
-                    p.tokens[row] = code == kOk ? p.token_offset + static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
-                    if (p.counts) p.counts[row] = cnt;
-                }
-            } else {
-                // -------------------------------------------------- sampler finish
-                // Segment maximum and mass relative to it, granules in (chunk, warp) order.
-                const float seg_m = cta_hi ? ordered_to_float(cta_hi) : -__int_as_float(0x7F800000);
-                const int ngran = nchunks * kConsumerWarps;
-                const bool seg_finite = seg_m > -__int_as_float(0x7F800000) && seg_m < __int_as_float(0x7F800000);
-                double term = 0.0;
-                if (seg_finite) {
-                    for (int g = tid; g < ngran; g += kConsumerThreads) {
-                        const float2 e = granules[g];
-                        if (e.y > 0.0f) term += static_cast<double>(e.y) *
-                                                exp((static_cast<double>(e.x) - static_cast<double>(seg_m)) / p.temperature);
-                    }
-                }
-                double seg_s;
-                block_exclusive_scan(sh, term, tid, seg_s);
-
-                // All-gather (M_r, S_r, count, flags) across the cluster, in rank order.
-                const uint32_t slot = k & 1u;
-                if (tid == 0) {
-                    GatherSlot mine{__float_as_uint(seg_m), cta_count, cta_flags, 0u, seg_s, 0.0};
-                    if (csize > 1) {
-                        const uint32_t local = ptx::smem_addr(&sh.slots[slot][crank]);
-                        const uint32_t bar = ptx::smem_addr(&sh.gather[slot]);
-                        uint32_t sbits[2];
-                        memcpy(sbits, &mine.s, 8);
-                        for (uint32_t q = 0; q < csize; ++q) {
-                            const uint32_t dst = ptx::mapa(local, q);
-                            ptx::st_cluster_v4(dst, mine.a, mine.b, mine.c, mine.d);
-                            ptx::st_cluster_v4(dst + 16, sbits[0], sbits[1], 0u, 0u);
-                            ptx::mbar_arrive_remote(ptx::mapa(bar, q));
-                        }
-                        wait_bounded(ptx::smem_addr(&sh.gather[slot]), (k >> 1) & 1u, &sh.abort, true);
-                    } else {
-                        sh.slots[slot][0] = mine;
-                    }
-                }
-                ptx::named_sync(1, kConsumerThreads);
-                // Row-level merge, identical on every rank.
-                float rm = -__int_as_float(0x7F800000);
-                uint32_t cnt = 0, flags = sh.abort ? kFlagAbort : 0u;
-                for (uint32_t q = 0; q < csize; ++q) {
-                    const GatherSlot& g = sh.slots[slot][q];
-                    rm = fmaxf(rm, __uint_as_float(g.a));
-                    cnt += g.b;
-                    flags |= g.c;
-                }
-                const double u = p.uniforms[row];
-                int32_t code = (flags & kFlagAbort) ? kTimeout
-                               : (flags & kFlagNaN) ? kNaN
-                               : (rm == __int_as_float(0x7F800000)) ? kPosInf
-                               : (cnt == 0u) ? kEmpty
-                               : (rm == -__int_as_float(0x7F800000)) ? kNoMass
-                               : !(u >= 0.0 && u < 1.0) ? kBadUniform
-                                                        : kOk;
-                if (code != kOk) {
-                    if (crank == 0 && tid == 0) {
-                        p.status[row] = code;
-                        p.tokens[row] = -1;
-                        if (p.counts) p.counts[row] = cnt;
-                    }
-                } else {
-                    const double M = rm;
-                    double total = 0.0;
-                    double rank_mass[kMaxCluster];
-                    for (uint32_t q = 0; q < csize; ++q) {
-                        const GatherSlot& g = sh.slots[slot][q];
-                        const float gm = __uint_as_float(g.a);
-                        rank_mass[q] = (g.s > 0.0) ? g.s * exp((static_cast<double>(gm) - M) / p.temperature) : 0.0;
-                        total += rank_mass[q];
-                    }
-                    const double cutoff = u * total;
-                    int owner = -1, last_pos = -1;
-                    double prefix = 0.0, run = 0.0, last_prefix = 0.0;
-                    for (uint32_t q = 0; q < csize; ++q) {
-                        if (rank_mass[q] <= 0.0) continue;
-                        last_pos = static_cast<int>(q);
-                        last_prefix = run;
-                        if (owner < 0 && cutoff < run + rank_mass[q]) {
-                            owner = static_cast<int>(q);
-                            prefix = run;
-                        }
-                        run += rank_mass[q];
-                    }
-                    const bool fallback = owner < 0;
-                    if (fallback) {
-                        owner = last_pos;
-                        prefix = last_prefix;
-                    }
-                    if (owner == static_cast<int>(crank)) {
-                        // Find the granule: exclusive scan of granule masses (thread-contiguous blocks).
-                        const int per = (ngran + kConsumerThreads - 1) / kConsumerThreads;
-                        const int g0 = tid * per, g1 = min(g0 + per, ngran);
-                        double local = 0.0;
-                        for (int g = g0; g < g1; ++g) {
-                            const float2 e = granules[g];
-                            if (e.y > 0.0f) local += static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / p.temperature);
-                        }
-                        double seg_total;
-                        const double excl = block_exclusive_scan(sh, local, tid, seg_total);
-                        int cand = 0x7FFFFFFF, lastg = -1;
-                        double acc = prefix + excl;
-                        for (int g = g0; g < g1; ++g) {
-                            const float2 e = granules[g];
-                            if (!(e.y > 0.0f)) continue;
-                            const double m = static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / p.temperature);
-                            if (!(m > 0.0)) continue;
-                            lastg = g;
-                            if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) cand = g;
-                            acc += m;
-                        }
-                        int gsel = fallback ? 0x7FFFFFFF : block_min_int(sh, cand, tid);
-                        const bool walk_fallback = (gsel == 0x7FFFFFFF);
-                        if (walk_fallback) gsel = block_max_int(sh, lastg, tid);
-                        // Prefix mass before the chosen granule.
-                        if (!walk_fallback && g0 <= gsel && gsel < g1) {
-                            double a = prefix + excl;
-                            for (int g = g0; g < gsel; ++g) {
-                                const float2 e = granules[g];
-                                if (e.y > 0.0f) a += static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / p.temperature);
-                            }
-                            sh.bcast_d[0] = a;
-                        }
-                        ptx::named_sync(1, kConsumerThreads);
-                        const double gprefix = walk_fallback ? 0.0 : sh.bcast_d[0];
-                        int64_t chosen = -1;
-                        if (gsel >= 0) {
-                            // Walk the granule with exact fp64 weights, in token order.
-                            const int gc = gsel / kConsumerWarps, gw = gsel % kConsumerWarps;
-                            const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
-                            const int64_t gt1 = min(gt0 + kTPW, seg_end);
-                            constexpr int kPer = kTPW / kConsumerThreads;
-                            const int64_t my0 = gt0 + tid * kPer;
-                            double w[kPer];
-                            double wsum = 0.0;
-#pragma unroll
-                            for (int i = 0; i < kPer; ++i) {
-                                const int64_t t = my0 + i;
-                                w[i] = 0.0;
-                                if (t < gt1) {
-                                    const uint32_t word = static_cast<uint32_t>(mrow[t >> 5]);
-                                    if ((word >> (t & 31)) & 1u) {
-                                        const float x = E::load(lrow, t);
-                                        if (x > -__int_as_float(0x7F800000))
-                                            w[i] = exp((static_cast<double>(x) - M) / p.temperature);
-                                    }
-                                }
-                                wsum += w[i];
-                            }
-                            double gtotal;
-                            const double wexcl = block_exclusive_scan(sh, wsum, tid, gtotal);
-                            int64_t hit = INT64_MAX, lastpos = -1;
-                            double a = gprefix + wexcl;
-#pragma unroll
-                            for (int i = 0; i < kPer; ++i) {
-                                if (!(w[i] > 0.0)) continue;
-                                lastpos = my0 + i;
-                                a += w[i];
-                                if (!walk_fallback && hit == INT64_MAX && cutoff < a) hit = my0 + i;
-                            }
-                            // Lowest hit, else the last positive-weight token of the granule.
-                            const int hit32 = hit == INT64_MAX ? 0x7FFFFFFF : static_cast<int>(hit - gt0);
-                            const int hmin = block_min_int(sh, hit32, tid);
-                            if (hmin != 0x7FFFFFFF) {
-                                chosen = gt0 + hmin;
-                            } else {
-                                const int lp = block_max_int(sh, lastpos < 0 ? -1 : static_cast<int>(lastpos - gt0), tid);
-                                chosen = lp >= 0 ? gt0 + lp : -1;
-                            }
-                        }
-                        if (tid == 0) {
-                            p.status[row] = chosen >= 0 ? kOk : kNoMass;
-                            p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
-                            if (p.counts) p.counts[row] = cnt;
-                        }
-                    }
-                }
-                // granules[] and slots are rewritten by the next row only after this point.
-                ptx::named_sync(1, kConsumerThreads);
+                sh.part[slot][warp] = WarpPartial{wkey, wchunk, wcount, wflags};
+                ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
             }
         }
     }
@@ -861,11 +842,11 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
     ptx::cluster_wait();
 }
 
-// Shared-memory bytes the kernel needs (stages + control block + sampler granule table).
+// Shared-memory bytes the kernel needs (stages + control block + sampler granule tables).
 template <typename T, bool kSample>
 constexpr size_t select_smem_bytes(int stages) {
     return static_cast<size_t>(stages) * Layout<T>::kStageBytes + sizeof(Shared) +
-           (kSample ? static_cast<size_t>(kMaxChunksSampler) * kConsumerWarps * sizeof(float2) : 0);
+           (kSample ? 2 * static_cast<size_t>(kMaxChunksSampler) * kConsumerWarps * sizeof(float2) : 0);
 }
 
 }  // namespace bms
