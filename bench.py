@@ -37,9 +37,10 @@ sys.path.insert(0, str(ROOT))
 
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the selection kernel on the
-# verification workload (ncu capture summarised in profiles/); None until captured.
-NCU_TRAFFIC_PER_ROW = None
+# dram__bytes_read.sum + dram__bytes_write.sum per row from one ncu capture of the dominant kernel
+# on a smaller case of the same workload (profiles/select_rows_bf16_verify.md and
+# profiles/select_rows_f16_sample.md); traffic grows with the rows processed.
+NCU_TRAFFIC_PER_ROW = {"verify": 532283, "sample": 535613}
 
 
 def parse_args():
@@ -544,7 +545,8 @@ def run_b200_arm(args):
     bytes_per_launch = w.rows * w.bytes_per_row
     kernel_s = ktime / reps
     achieved = bytes_per_launch / kernel_s / 1e9
-    traffic = None if NCU_TRAFFIC_PER_ROW is None else NCU_TRAFFIC_PER_ROW * w.rows
+    per_row = NCU_TRAFFIC_PER_ROW.get(w.kind)
+    traffic = None if per_row is None else per_row * w.rows
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
