@@ -57,6 +57,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--roofline-seconds", type=float, default=1.5)
+    ap.add_argument("--cluster", type=int, default=0,
+                    help="force the selection kernel's cluster size (1/2/4/8/16; 0 = automatic)")
+    ap.add_argument("--clusters", type=int, default=0,
+                    help="force the number of persistent clusters (0 = automatic)")
     return ap.parse_args()
 
 
@@ -506,6 +510,9 @@ def run_b200_arm(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     w = Workload(args, rank, device)
+    if args.cluster or args.clusters:
+        from bitmask_speculation_b200 import _native
+        _native.set_launch_override(args.cluster, args.clusters)
     torch.cuda.synchronize(device)
     w.check_against_oracle()
     stream = w.stream_handle()
@@ -558,6 +565,7 @@ def run_b200_arm(args):
         "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
         "data": "synthetic (seeded, generated on device)",
         "config": {"workload": w.name, "rows_per_gpu": w.rows, "vocab": w.vocab,
+                   "cluster": args.cluster or "auto",
                    "bytes_per_row": w.bytes_per_row,
                    "l2": (f"inputs {w.rows * w.bytes_per_row * w.batches / 1e9:.2f} GB per GPU rotated "
                           f"({w.batches} batch(es)) > 126 MB L2; no flush"),

@@ -165,8 +165,16 @@ struct Plan {
     int64_t segment;
 };
 
-// Choose the cluster size that minimises the chunks streamed by the busiest CTA.
-Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens_per_chunk, int max_chunks) {
+// Per-row cost of the row-end work (finalizer merge, cluster all-gather, index recovery or the
+// sampling walk) in units of one streamed chunk, by cluster size; measured on B200 at
+// V = 248,320 (2,304 rows: C = 1 / 2 / 4 took 194 / 203 / 258 us for the argmax and 301 / 374 /
+// 620 us for the sampler).
+constexpr double kRowCostArgmax[5] = {1.1, 2.4, 3.6, 5.0, 7.0};
+constexpr double kRowCostSampler[5] = {5.0, 8.0, 12.0, 16.0, 20.0};
+
+// Choose the cluster size that minimises the streaming plus row-end work of the busiest CTA.
+Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens_per_chunk, int max_chunks,
+                 bool sampler) {
     Plan best{0, 0, 0};
     double best_cost = 0.0;
     for (int i = 0; i < 5; ++i) {
@@ -180,7 +188,7 @@ Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens
         int64_t clusters = rows < resident ? rows : resident;
         if (g_force_clusters) clusters = g_force_clusters < rows ? g_force_clusters : rows;
         const int64_t waves = (rows + clusters - 1) / clusters;
-        const double overhead = c == 1 ? 0.25 : 0.6;  // per-row merge cost, in chunk units
+        const double overhead = sampler ? kRowCostSampler[i] : kRowCostArgmax[i];
         const double cost = static_cast<double>(waves) * (static_cast<double>(chunks) + overhead);
         if (best.cluster == 0 || cost < best_cost - 1e-9) {
             best = Plan{c, static_cast<int>(clusters), seg};
@@ -194,7 +202,8 @@ template <typename T, bool kSample, bool kBulk, int kStages>
 int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     KernelInfo* info = nullptr;
     BMS_CHECK((kernel_info<T, kSample, kBulk, kStages>(device, info)));
-    const Plan plan = plan_launch(*info, p.rows, p.vocab, Layout<T>::kTokensPerChunk, kSample ? kMaxChunksSampler : 0);
+    const Plan plan = plan_launch(*info, p.rows, p.vocab, Layout<T>::kTokensPerChunk, kSample ? kMaxChunksSampler : 0,
+                                  kSample);
     if (plan.cluster == 0)
         return fail(BMS_ERROR_UNSUPPORTED, "vocabulary of %lld tokens exceeds the %s limit", static_cast<long long>(p.vocab),
                     kSample ? "sampler" : "selection");
@@ -215,14 +224,17 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     return BMS_SUCCESS;
 }
 
-constexpr int kBulkStages = 4;
+// Ring depth: 4 stages for the argmax (3 CTAs/SM fit), 3 for the sampler, whose granule tables
+// also live in shared memory (3 CTAs/SM as well).
+template <bool kSample>
+constexpr int bulk_stages() { return kSample ? 3 : 4; }
 
 template <typename T, bool kSample>
 int launch_select_dtype(SelectParams p, int device, cudaStream_t stream) {
     const int eb = sizeof(T);
     const bool bulk = reinterpret_cast<uintptr_t>(p.logits) % 16 == 0 && reinterpret_cast<uintptr_t>(p.masks) % 16 == 0 &&
                       (p.vocab * eb) % 16 == 0 && (p.logit_stride * eb) % 16 == 0 && p.mask_stride % 4 == 0;
-    if (bulk) return launch_select_t<T, kSample, true, kBulkStages>(p, device, stream);
+    if (bulk) return launch_select_t<T, kSample, true, bulk_stages<kSample>()>(p, device, stream);
     return launch_select_t<T, kSample, false, 1>(p, device, stream);
 }
 
@@ -462,6 +474,7 @@ int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* ma
     const float tiny = 1.40129846e-45f;
     if (!(scf >= tiny)) scf = tiny;
     p.scale2 = scf;
+    p.scale = static_cast<float>(1.4426950408889634 / temperature);
     return launch_select<true>(dtype, p, device, static_cast<cudaStream_t>(stream));
 }
 

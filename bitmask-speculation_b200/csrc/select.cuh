@@ -12,7 +12,8 @@
 //
 // Structure (B200 / sm_100a):
 //  * A cluster of C CTAs owns one row at a time; CTA rank r streams tokens
-//    [r*L, (r+1)*L) of the row.  Clusters loop over rows (persistent grid).
+//    [r*L, (r+1)*L) of the row.  Each cluster walks a contiguous block of rows
+//    (persistent grid).
 //  * One producer warp moves 16 KB chunks of logits plus their mask words from
 //    HBM into a ring of shared-memory stages with 1-D bulk copies (TMA engine)
 //    completing on mbarriers; eight consumer warps reduce them.  Rows whose
@@ -56,7 +57,7 @@ constexpr int kChunkBytes = 16384;               // logits bytes per stage
 constexpr int kWarpBytes = kChunkBytes / kConsumerWarps;
 constexpr int kVecsPerLane = kWarpBytes / 16 / 32;  // 16-byte vectors per lane per chunk
 constexpr int kMaxCluster = 16;
-constexpr int kMaxChunksSampler = 128;  // granule table capacity (chunks per segment)
+constexpr int kMaxChunksSampler = 64;  // granule table capacity (chunks per segment)
 constexpr uint64_t kTimeoutNs = 1000000000ull;
 
 enum Status : int32_t {
@@ -169,11 +170,15 @@ __device__ __forceinline__ void mask_pairs(const uint4& r, uint32_t bits8, uint3
     q[3] = ptx::select_bits(r.w, ptx::prmt(shi, 0u, 0xBBAAu), E::kNegInf2);
 }
 
-// Sum over a lane's 32 (16-bit) or 16 (fp32) masked tokens of 2^((x - m) log2(e) / T),
-// pairwise per vector then across vectors.  Invalid tokens hold -inf (weight 0).
-template <typename E, bool kClamp>
+// Sum over a lane's 32 (16-bit) or 16 (fp32) masked tokens of 2^((x - m) log2(e) / T), one MUFU
+// ex2 per token, pairwise sums per vector and across vectors.  Invalid tokens hold -inf (weight 0).
+//  kMode 0: t = fma(x, s, c) with s = log2(e)/T and c = -(m s) rounded (the caller rescales the
+//           sum by 2^(rounding error of c), which is common to every token);
+//  kMode 1: t = (0.5x - 0.5m) * 2s -- cannot overflow for any finite logits;
+//  kMode 2: as 1, clamped at 0 for an infinite scale (T below ~1e-38, where x == m gives 0 * inf).
+template <typename E, int kMode>
 __device__ __forceinline__ float lane_mass(const uint32_t (&q16)[kVecsPerLane][4],
-                                           const float (&q32)[kVecsPerLane][E::kVec], float nhm, float sc2) {
+                                           const float (&q32)[kVecsPerLane][E::kVec], float c, float scale) {
     constexpr int kVec = E::kVec;
     float part[kVecsPerLane];
 #pragma unroll
@@ -184,8 +189,13 @@ __device__ __forceinline__ float lane_mass(const uint32_t (&q16)[kVecsPerLane][4
             float x;
             if constexpr (E::kBytes == 2) x = (i & 1) ? E::hi(q16[j][i >> 1]) : E::lo(q16[j][i >> 1]);
             else x = q32[j][i];
-            float t = fmaf(x, 0.5f, nhm) * sc2;
-            if constexpr (kClamp) t = fminf(t, 0.0f);
+            float t;
+            if constexpr (kMode == 0) {
+                t = fmaf(x, scale, c);
+            } else {
+                t = fmaf(x, 0.5f, c) * scale;
+                if constexpr (kMode == 2) t = fminf(t, 0.0f);
+            }
             w[i] = ptx::ex2(t);
         }
 #pragma unroll
@@ -218,6 +228,7 @@ struct SelectParams {
     const double* uniforms;  // [rows]
     double temperature;
     float scale2;            // 2 * log2(e) / T as float, clamped to >= the smallest denormal
+    float scale;             // log2(e) / T as float (inf for tiny T)
 };
 
 // Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).
@@ -253,6 +264,8 @@ struct alignas(16) WarpPartial {
     uint32_t chunk;  // argmax: first chunk in which a lane of this warp reached `key`
     uint32_t count;  // valid tokens
     uint32_t flags;  // kFlagNaN
+    double mass;     // sampler: the warp's mass relative to its running max (fp64)
+    double pad;
 };
 
 constexpr int kStagesMax = 8;
@@ -266,6 +279,15 @@ struct alignas(16) Shared {
     GatherSlot slots[2][kMaxCluster];
     WarpPartial part[2][kConsumerWarps];
     volatile int32_t abort;
+};
+
+// Sampler-only shared memory after the control block.
+struct SamplerShared {
+    // Per row slot, one entry per (chunk, warp) granule: while streaming a float2 (running max,
+    // mass relative to it); after the row, the granule's mass relative to its warp's max (double).
+    double granules[2][kMaxChunksSampler * kConsumerWarps];
+    float walk[32][33];                                       // finalizer: the walked granule, one row per lane
+    double fac[kConsumerWarps];                               // finalizer: warp max -> row max factors
 };
 
 // Bounded mbarrier wait.  Returns false (and latches `abort`) after kTimeoutNs.
@@ -312,23 +334,40 @@ __device__ __forceinline__ double exact_weight(float x, double M, double T) {
     return x > -__int_as_float(0x7F800000) ? exp((static_cast<double>(x) - M) / T) : 0.0;
 }
 
-__device__ __forceinline__ double granule_mass(float2 e, double M, double T) {
-    return e.y > 0.0f ? static_cast<double>(e.y) * exp((static_cast<double>(e.x) - M) / T) : 0.0;
-}
 
-// Loads a lane's slice [t0, t0 + n) of a row with independent loads (tokens at or past `end`
-// read as 0 with their mask bits cleared); returns the slice's mask bits.
+// A finalizer lane's slice of n consecutive tokens: 16-bit logits kept packed two per word.
 template <typename E, int n>
-__device__ __forceinline__ uint32_t load_lane_slice(const uint8_t* lrow, const int32_t* mrow, int64_t t0, int64_t end,
-                                                    float (&v)[n]) {
-    static_assert(n <= 32, "slice must fit one mask word");
+struct Slice {
+    static constexpr int kWords = E::kBytes == 2 ? n / 2 : n;
+    uint32_t w[kWords];
+    uint32_t bits;  // mask bits of the slice (bit i = token t0 + i), 0 past the end
+    __device__ __forceinline__ float value(int i) const {
+        if constexpr (E::kBytes == 2) return (i & 1) ? E::hi(w[i >> 1]) : E::lo(w[i >> 1]);
+        else return __uint_as_float(w[i]);
+    }
+};
+
+// Loads [t0, t0 + n) of a row with independent loads (tokens at or past `end` read as 0 with
+// their mask bits cleared).  t0 is a multiple of 32, so the slice lies in one mask word.
+template <typename E, int n>
+__device__ __forceinline__ void load_slice(const uint8_t* lrow, const int32_t* mrow, int64_t t0, int64_t end,
+                                           Slice<E, n>& sl) {
+    static_assert(n <= 32 && n % 2 == 0, "slice must fit one mask word");
     uint32_t word = t0 < end ? static_cast<uint32_t>(mrow[t0 >> 5]) >> (t0 & 31) : 0u;
 #pragma unroll
-    for (int i = 0; i < n; ++i) v[i] = (t0 + i < end) ? E::load(lrow, t0 + i) : 0.0f;
+    for (int i = 0; i < Slice<E, n>::kWords; ++i) {
+        if constexpr (E::kBytes == 2) {
+            const uint32_t a = (t0 + 2 * i < end) ? E::raw(lrow, t0 + 2 * i) : 0u;
+            const uint32_t b = (t0 + 2 * i + 1 < end) ? E::raw(lrow, t0 + 2 * i + 1) : 0u;
+            sl.w[i] = a | (b << 16);
+        } else {
+            sl.w[i] = (t0 + i < end) ? E::raw(lrow, t0 + i) : 0u;
+        }
+    }
     const int64_t avail = end - t0;
     if (avail < n) word &= avail <= 0 ? 0u : ((1u << avail) - 1u);
     if constexpr (n < 32) word &= (1u << n) - 1u;
-    return word;
+    sl.bits = word;
 }
 
 // All-gather of one 32-byte slot per rank across the cluster (finalizer lane 0 issues it;
@@ -350,21 +389,20 @@ __device__ __forceinline__ void cluster_allgather(Shared& sh, uint32_t slot, uin
 
 // ----------------------------------------------------------------- the kernel
 template <typename T, bool kSample, bool kBulk, int kStages>
-__global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(const SelectParams p) {
+__global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectParams p) {
     using E = Elem<T>;
     using L = Layout<T>;
     constexpr int kVec = E::kVec;
     constexpr int kTPC = L::kTokensPerChunk;
     constexpr int kTPW = L::kTokensPerWarp;
     constexpr uint32_t kVecMask = (1u << kVec) - 1u;
-    constexpr int kGranules = kMaxChunksSampler * kConsumerWarps;
     constexpr int kFinPer = kTPW / 32;
     const float kInf = __int_as_float(0x7F800000);
 
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* stages = smem_raw;
     Shared& sh = *reinterpret_cast<Shared*>(smem_raw + kStages * L::kStageBytes);
-    float2* granule_base = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(Shared));
+    SamplerShared& ss = *reinterpret_cast<SamplerShared*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(Shared));
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -373,6 +411,11 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
     const uint32_t cid = ptx::cluster_id_x();
     const uint32_t nclusters = ptx::ncluster_x();
 
+    // Contiguous, remainder-balanced block of rows per cluster: neighbouring rows (often of
+    // different mask densities, hence cost) land on the same cluster.
+    const int64_t rows_q = p.rows / nclusters, rows_r = p.rows % nclusters;
+    const int64_t row_begin = static_cast<int64_t>(cid) * rows_q + (cid < rows_r ? cid : rows_r);
+    const int64_t row_end = row_begin + rows_q + (cid < rows_r ? 1 : 0);
     const int64_t seg_begin_raw = static_cast<int64_t>(crank) * p.segment;
     const int64_t seg_begin = seg_begin_raw < p.vocab ? seg_begin_raw : p.vocab;
     const int64_t seg_end = (seg_begin_raw + p.segment) < p.vocab ? (seg_begin_raw + p.segment) : p.vocab;
@@ -404,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
         if (kBulk && lane == 0) {
             uint32_t it = 0;
             bool stop = false;
-            for (int64_t row = cid; row < p.rows && !stop; row += nclusters) {
+            for (int64_t row = row_begin; row < row_end && !stop; ++row) {
                 const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                       static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
                 const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
@@ -440,14 +483,14 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
     } else if (warp == kFinalizerWarp) {
         // ------------------------------------------------------------ finalizer warp
         uint32_t k = 0;
-        for (int64_t row = cid; row < p.rows; row += nclusters, ++k) {
+        for (int64_t row = row_begin; row < row_end; ++row, ++k) {
             const uint32_t slot = k & 1u;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
             wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort);
             const bool in = lane < kConsumerWarps;
-            const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u};
+            const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u, 0.0, 0.0};
             const uint32_t cnt = __reduce_add_sync(0xFFFFFFFFu, wp.count);
             const uint32_t flags = __reduce_or_sync(0xFFFFFFFFu, wp.flags) | (sh.abort ? kFlagAbort : 0u);
             const uint32_t ckey = __reduce_max_sync(0xFFFFFFFFu, wp.key);
@@ -466,11 +509,11 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                     const int64_t r0 = seg_begin + static_cast<int64_t>(rmin / kConsumerWarps) * kTPC +
                                        static_cast<int64_t>(rmin % kConsumerWarps) * kTPW;
                     const int64_t my0 = r0 + lane * kFinPer;
-                    float v[kFinPer];
-                    const uint32_t word = load_lane_slice<E>(lrow, mrow, my0, seg_end, v);
+                    Slice<E, kFinPer> sl;
+                    load_slice<E, kFinPer>(lrow, mrow, my0, seg_end, sl);
 #pragma unroll
                     for (int i = kFinPer - 1; i >= 0; --i)
-                        if (((word >> i) & 1u) && v[i] == target) found = static_cast<uint32_t>(my0 + i);
+                        if (((sl.bits >> i) & 1u) && sl.value(i) == target) found = static_cast<uint32_t>(my0 + i);
                 }
                 uint32_t hi = ckey;
                 uint32_t lo = __reduce_min_sync(0xFFFFFFFFu, found);
@@ -494,14 +537,16 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                     if (p.counts) p.counts[row] = total;
                 }
             } else {
-                // Segment maximum and mass relative to it (granules in fixed (chunk, warp) order).
-                const float2* granules = granule_base + slot * kGranules;
+                // Segment maximum and mass relative to it: the consumer warps already folded their
+                // granules to their own maxima; combine the 8 warp masses in warp order.
+                const double* granules = ss.granules[slot];
                 const int ngran = nchunks * kConsumerWarps;
                 const float seg_m = ckey ? ordered_to_float(ckey) : -kInf;
                 const bool seg_finite = seg_m > -kInf && seg_m < kInf;
-                double term = 0.0;
-                if (seg_finite)
-                    for (int g = lane; g < ngran; g += 32) term += granule_mass(granules[g], seg_m, p.temperature);
+                const float wmax = in ? ordered_to_float(wp.key) : -kInf;
+                const double term = (seg_finite && in && wp.mass > 0.0)
+                                        ? wp.mass * exp((static_cast<double>(wmax) - static_cast<double>(seg_m)) / p.temperature)
+                                        : 0.0;
                 const double seg_s = warp_sum(term);
                 // Rank partials, all-gathered in rank order.
                 if (lane == 0) {
@@ -563,16 +608,22 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                     }
                     if (owner == static_cast<int>(crank)) {
                         // Granule holding the crossing: contiguous blocks of granules per lane.
+                        // Factor from each warp's max to the row max, shared by its granules.
+                        const double fac_mine = (in && wp.mass > 0.0)
+                                                    ? exp((static_cast<double>(wmax) - M) / temp) : 0.0;
+                        if (in) ss.fac[lane] = fac_mine;
+                        __syncwarp();
+                        const double* fac = ss.fac;
                         const int per = (ngran + 31) / 32;
                         const int g0 = lane * per, g1 = min(g0 + per, ngran);
                         double local = 0.0;
-                        for (int g = g0; g < g1; ++g) local += granule_mass(granules[g], M, temp);
+                        for (int g = g0; g < g1; ++g) local += granules[g] * fac[g % kConsumerWarps];
                         const double incl = warp_inclusive_scan(local, lane);
                         double acc = prefix + incl - local;
                         int cand = 0x7FFFFFFF, lastg = -1;
                         double cand_prefix = 0.0;
                         for (int g = g0; g < g1; ++g) {
-                            const double m = granule_mass(granules[g], M, temp);
+                            const double m = granules[g] * fac[g % kConsumerWarps];
                             if (!(m > 0.0)) continue;
                             lastg = g;
                             if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) {
@@ -597,44 +648,49 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                             const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
                             const int64_t gt1 = min(gt0 + kTPW, seg_end);
                             const int64_t my0 = gt0 + lane * kFinPer;
-                            float v[kFinPer];
-                            const uint32_t word = load_lane_slice<E>(lrow, mrow, my0, gt1, v);
-                            double wsum = 0.0;
-                            int64_t lastpos = -1;
+                            uint32_t bits;
+                            {
+                                Slice<E, kFinPer> sl;
+                                load_slice<E, kFinPer>(lrow, mrow, my0, gt1, sl);
 #pragma unroll
-                            for (int i = 0; i < kFinPer; ++i) {
-                                if (!((word >> i) & 1u)) continue;
-                                const double w = exact_weight(v[i], M, temp);
-                                if (w > 0.0) lastpos = my0 + i;
-                                wsum += w;
+                                for (int i = 0; i < kFinPer; ++i) ss.walk[lane][i] = sl.value(i);
+                                bits = sl.bits;
                             }
-                            const double wincl = warp_inclusive_scan(wsum, lane);
-                            int64_t hit = INT64_MAX;
-                            if (!walk_fallback) {
-                                const double before = gprefix + wincl - wsum;
-                                if (cutoff < gprefix + wincl && cutoff >= before) {
-                                    // This lane's tokens hold the crossing: walk them again in order.
-                                    double a = before;
-                                    for (int i = 0; i < kFinPer; ++i) {
-                                        if (!((word >> i) & 1u)) continue;
-                                        const double w = exact_weight(v[i], M, temp);
-                                        if (!(w > 0.0)) continue;
-                                        a += w;
-                                        if (cutoff < a) {
-                                            hit = my0 + i;
-                                            break;
-                                        }
-                                    }
+                            __syncwarp();
+                            // (1) fp32 weights relative to M locate the lane whose tokens hold the
+                            // crossing (its fp32 prefix is within ~1e-7 of the exact one).
+                            float lsum = 0.0f;
+                            {
+                                const float hm = -0.5f * static_cast<float>(M);
+                                const float sc2 = p.scale2;
+#pragma unroll
+                                for (int i = 0; i < kFinPer; ++i) {
+                                    float t = fmaf(ss.walk[lane][i], 0.5f, hm) * sc2;
+                                    t = fminf(t, 0.0f);
+                                    const float w = ptx::ex2(t);
+                                    lsum += ((bits >> i) & 1u) ? w : 0.0f;
                                 }
                             }
-                            const int hit32 = hit == INT64_MAX ? 0x7FFFFFFF : static_cast<int>(hit - gt0);
-                            const int hmin = __reduce_min_sync(0xFFFFFFFFu, hit32);
-                            if (hmin != 0x7FFFFFFF) {
-                                chosen = gt0 + hmin;
-                            } else {
-                                // Rounding left the crossing past the granule's last positive weight.
-                                const int lp = __reduce_max_sync(0xFFFFFFFFu, lastpos < 0 ? -1 : static_cast<int>(lastpos - gt0));
-                                chosen = lp >= 0 ? gt0 + lp : -1;
+                            const double lsum_d = lsum;
+                            const double lincl = warp_inclusive_scan(lsum_d, lane);
+                            const bool positive = lsum > 0.0f;
+                            const uint32_t pos_mask = __ballot_sync(0xFFFFFFFFu, positive);
+                            const uint32_t cross_mask =
+                                __ballot_sync(0xFFFFFFFFu, !walk_fallback && positive && cutoff < gprefix + lincl);
+                            const bool lane_fallback = cross_mask == 0u;
+                            const int L = lane_fallback ? (pos_mask ? 31 - __clz(pos_mask) : -1) : __ffs(cross_mask) - 1;
+                            if (L >= 0) {
+                                // (2) exact fp64 weights of lane L's tokens, one per lane, scanned in order.
+                                const uint32_t bitsL = __shfl_sync(0xFFFFFFFFu, bits, L);
+                                const double prefixL = gprefix + __shfl_sync(0xFFFFFFFFu, lincl - lsum_d, L);
+                                const bool mine = lane < kFinPer && ((bitsL >> lane) & 1u);
+                                const double w = mine ? exact_weight(ss.walk[L][lane < kFinPer ? lane : 0], M, temp) : 0.0;
+                                const double incl = warp_inclusive_scan(w, lane);
+                                const uint32_t hits = __ballot_sync(0xFFFFFFFFu, !lane_fallback && w > 0.0 && cutoff < prefixL + incl);
+                                const uint32_t pos = __ballot_sync(0xFFFFFFFFu, w > 0.0);
+                                const int64_t base = gt0 + static_cast<int64_t>(L) * kFinPer;
+                                if (hits) chosen = base + (__ffs(hits) - 1);
+                                else if (pos) chosen = base + (31 - __clz(pos));  // rounding: last positive
                             }
                         }
                         if (lane == 0) {
@@ -652,14 +708,15 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
         // ------------------------------------------------------------ consumer warps
         uint32_t it = 0;
         uint32_t k = 0;  // rows processed by this cluster
-        for (int64_t row = cid; row < p.rows; row += nclusters, ++k) {
+        for (int64_t row = row_begin; row < row_end; ++row, ++k) {
             const uint32_t slot = k & 1u;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
             // The finalizer has released this row's partial slot (and granule table).
             if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
-            float2* granules = granule_base + slot * kGranules;
+            double* granules = ss.granules[slot];
+            float2* granules_f = reinterpret_cast<float2*>(granules);
             typename E::NanAcc nan_acc = E::nan_init();
             uint32_t count = 0;
             // argmax: lane's running masked max and the chunk it came from
@@ -803,15 +860,27 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                     float mass = 0.0f;
                     const bool finite_m = run_m > -kInf && run_m < kInf;
                     if (warp_any && finite_m) {
-                        const float nhm = -0.5f * run_m;
-                        const float sc2 = p.scale2;
-                        // An infinite scale (T below ~1e-38) turns x == m into 0 * inf: clamp then.
-                        if (sc2 < kInf) mass = lane_mass<E, false>(q16, q32, nhm, sc2);
-                        else mass = lane_mass<E, true>(q16, q32, nhm, sc2);
+                        const float sc = p.scale;
+                        const float msc = run_m * sc;
+                        if (sc >= 1e-30f && fabsf(msc) < 0x1p100f) {
+                            // One FFMA per token: t = x s - (m s) rounded; the rounding error of m s
+                            // is the same for every token, folded back once per granule.
+                            const float chi = -msc;
+                            const float clo = fmaf(-run_m, sc, -chi);
+                            mass = lane_mass<E, 0>(q16, q32, chi, sc);
 #pragma unroll
-                        for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
+                            for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
+                            mass = fmaf(mass * clo, 0.6931471805599453f, mass);
+                        } else {
+                            const float nhm = -0.5f * run_m;
+                            const float sc2 = p.scale2;
+                            if (sc2 < kInf) mass = lane_mass<E, 1>(q16, q32, nhm, sc2);
+                            else mass = lane_mass<E, 2>(q16, q32, nhm, sc2);
+#pragma unroll
+                            for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
+                        }
                     }
-                    if (lane == 0) granules[c * kConsumerWarps + warp] = make_float2(run_m, mass);
+                    if (lane == 0) granules_f[c * kConsumerWarps + warp] = make_float2(run_m, mass);
                 }
             }
 
@@ -820,6 +889,22 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
             const uint32_t wcount = __reduce_add_sync(0xFFFFFFFFu, count);
             const uint32_t wflags = __any_sync(0xFFFFFFFFu, nan_local) ? kFlagNaN : 0u;
             uint32_t wkey, wchunk = 0xFFFFFFFFu;
+            double wmass = 0.0;
+            if constexpr (kSample) {
+                // Fold this warp's granules to its final max (one fp64 exp per lane per chunk); the
+                // finalizer then combines 8 warp masses instead of every granule.
+                __syncwarp();
+                double local = 0.0;
+                for (int c = lane; c < nchunks; c += 32) {
+                    const float2 e = granules_f[c * kConsumerWarps + warp];
+                    const double gm = e.y > 0.0f ? static_cast<double>(e.y) *
+                                                       exp((static_cast<double>(e.x) - static_cast<double>(run_m)) / p.temperature)
+                                                 : 0.0;
+                    granules[c * kConsumerWarps + warp] = gm;
+                    local += gm;
+                }
+                wmass = warp_sum(local);
+            }
             if constexpr (!kSample) {
                 const bool has = best_idx >= 0 || first_valid_chunk >= 0;
                 const uint32_t key = has ? ordered_bits(best) : 0u;
@@ -830,7 +915,7 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
                 wkey = ordered_bits(run_m);
             }
             if (lane == 0) {
-                sh.part[slot][warp] = WarpPartial{wkey, wchunk, wcount, wflags};
+                sh.part[slot][warp] = WarpPartial{wkey, wchunk, wcount, wflags, wmass, 0.0};
                 ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
             }
         }
@@ -842,11 +927,10 @@ __global__ void __launch_bounds__(kThreads, kSample ? 2 : 3) select_rows_kernel(
     ptx::cluster_wait();
 }
 
-// Shared-memory bytes the kernel needs (stages + control block + sampler granule tables).
+// Shared-memory bytes the kernel needs (stages + control block + sampler tables).
 template <typename T, bool kSample>
 constexpr size_t select_smem_bytes(int stages) {
-    return static_cast<size_t>(stages) * Layout<T>::kStageBytes + sizeof(Shared) +
-           (kSample ? 2 * static_cast<size_t>(kMaxChunksSampler) * kConsumerWarps * sizeof(float2) : 0);
+    return static_cast<size_t>(stages) * Layout<T>::kStageBytes + sizeof(Shared) + (kSample ? sizeof(SamplerShared) : 0);
 }
 
 }  // namespace bms

@@ -231,3 +231,30 @@ def test_chi_square_on_row_zero(cuda_module):
     f_exp *= f_obs.sum() / f_exp.sum()
     stat, pvalue = scipy_stats.chisquare(f_obs, f_exp)
     assert pvalue > 1e-3, (stat, pvalue, len(f_exp))
+
+
+@pytest.mark.parametrize("temperature", [1e-320, 1e-40, 1e-3, 0.05, 7.0, 1e30, 1e300])
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_extreme_temperatures_and_magnitudes_on_the_bulk_path(cuda_module, temperature, dtype):
+    """Huge logits, ties at the maximum, -inf valid tokens, tiny and huge temperatures (V = 8,192)."""
+    rng = np.random.default_rng(31)
+    vocab, rows = 8192, 6
+    values = rng.standard_normal((rows, vocab), dtype=np.float32) * np.float32(4)
+    values[0, :10] = 3e38          # huge logits (x - max must not overflow)
+    values[0, 10:20] = -3e38
+    values[1, 100] = values[1, 4000] = values[1].max() + 1  # tied maxima
+    values[2, rng.random(vocab) < 0.5] = -np.inf
+    values[3] = np.round(values[3])  # many ties everywhere
+    valid = rng.random((rows, vocab)) < 0.7
+    valid[:, 0] = True
+    valid[1, [100, 4000]] = True
+    masks = wl.pack_bits_np(valid)
+    bits = as_dtype_bits(values, dtype)
+    f32 = widened(bits, dtype)
+    u = np.array([0.0, 0.3, 0.5, 0.999, 0.77, 0.123456])
+    exp_tok, exp_st = oracle.sample_rows(bits, masks, temperature, u, dtype=None if dtype == "float32" else dtype)
+    tokens, _, status = cuda_module.masked_sample_batch(to_device(bits, dtype), torch.from_numpy(masks).cuda(),
+                                                        temperature, torch.from_numpy(u).cuda())
+    assert status.tolist() == exp_st.tolist()
+    for r in range(rows):
+        assert sample_matches(f32[r], masks[r], temperature, u[r], tokens[r].item(), exp_tok[r], TOL), (r, temperature)
