@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["verify", "argmax", "sample", "scale"], default="verify")
+    ap.add_argument("--workload", choices=["verify", "argmax", "sample", "scale", "vocab"], default="verify")
     ap.add_argument("--seqs", type=int, default=256, help="verification sequences per GPU")
     ap.add_argument("--rows", type=int, default=8192, help="rows per GPU for the scale workload")
     ap.add_argument("--sample-rows", type=int, default=8,
@@ -190,6 +190,22 @@ class Workload:
             self.dtype = "f16"
             self.name = (f"sample: {self.rows} rows fp16 N(0,2^2) at V=248320, T=0.7, densities "
                          "{1,.5,.1,.01,1e-4,.9,.3,.05}")
+        elif self.kind == "vocab":
+            # Every rank builds the same full rows, keeps its vocabulary slice and the full masks.
+            from bitmask_speculation_b200.sharding import shard_bounds
+            import torch.distributed as dist
+            world = dist.get_world_size() if dist.is_initialized() else 1
+            full, self.masks = wl.scale_rows_torch(args.rows, seed=5, device=device)
+            off, size = shard_bounds(vocab, world)[rank]
+            self.logits = full[:, off:off + size].contiguous()
+            del full
+            self.world = world
+            self.rows = args.rows
+            self.batches = 1
+            self.esize = 2
+            self.dtype = "bf16"
+            self.name = (f"vocab-sharded: {args.rows} rows bf16 N(0,3^2) at V=248320 split {world} ways, "
+                         "log-uniform mask density; NCCL all-gather of 32-byte partials")
         else:
             self.logits, self.masks = wl.scale_rows_torch(args.rows, seed=5 + 1000 * rank, device=device)
             self.rows = args.rows
@@ -202,6 +218,8 @@ class Workload:
 
     @property
     def bytes_per_row(self):
+        if self.kind == "vocab":  # this rank's slice of the logits and of the mask words
+            return self.logits.shape[1] * self.esize + (self.logits.shape[1] // 32) * 4 + 20
         return self.vocab * self.esize + self.words * 4 + 20
 
     def _alloc_outputs(self):
@@ -227,7 +245,7 @@ class Workload:
         return self.logits_all[r0:r0 + self.rows], self.masks_all[r0:r0 + self.rows]
 
     def launches_per_step(self):
-        return 2 if self.kind == "verify" else 1
+        return 2 if self.kind in ("verify", "vocab") else 1
 
     def step(self, stream_handle):
         """One hot-path step through the C ABI on inputs resident in HBM."""
@@ -245,6 +263,10 @@ class Workload:
                 self.row_counts.data_ptr(), self.row_status.data_ptr(), self.row_budget.data_ptr(),
                 self.accept.data_ptr(), self.token.data_ptr(), self.kindout.data_ptr(),
                 self.seq_status.data_ptr(), dev, stream_handle)
+        elif self.kind == "vocab":
+            from bitmask_speculation_b200.sharding import vocab_sharded_select
+            self.row_tokens, self.row_counts, self.row_status = vocab_sharded_select(logits, masks, self.vocab)
+            return
         elif self.kind == "sample":
             b = (self.step_index - 1) % self.batches
             u = self.uniforms_all[b * self.rows:(b + 1) * self.rows]
@@ -272,12 +294,22 @@ class Workload:
                 logits.data_ptr(), 2, masks.data_ptr(), self.rows, self.vocab, self.temperature, u.data_ptr(),
                 self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
                 self.device.index, stream_handle)
+        elif self.kind == "vocab":
+            from bitmask_speculation_b200.sharding import NativeShardBackend
+            self._parts = NativeShardBackend().partials(logits, masks, self._offset(), 0.0)
+            return
         else:
             code = {"f32": 0, "bf16": 1, "f16": 2}[self.dtype]
             rc = lib.bms_masked_reduce_batch(
                 logits.data_ptr(), code, masks.data_ptr(), self.rows, self.vocab, self.row_tokens.data_ptr(),
                 self.row_counts.data_ptr(), self.row_status.data_ptr(), self.device.index, stream_handle)
         _native.check(rc)
+
+    def _offset(self):
+        from bitmask_speculation_b200.sharding import shard_bounds
+        import torch.distributed as dist
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        return shard_bounds(self.vocab, self.world)[rank][0]
 
     def check_against_oracle(self, max_rows=64):
         """Untimed sanity check of the last step on a few rows (CPU oracle)."""
@@ -532,7 +564,7 @@ def run_b200_arm(args):
         ktime = timed_loop(lambda: w.kernel_only(stream), reps, device)
         torch.cuda.nvtx.range_pop()
         e2e = None
-        if not args.no_e2e:
+        if not args.no_e2e and w.kind != "vocab":
             e = EndToEnd(w)
             for _ in range(3):
                 e.step()
@@ -548,7 +580,8 @@ def run_b200_arm(args):
                    "path": ("verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
                             "device-resident logits, results D2H every step")}
 
-    value = w.rows * world * args.steps / seconds
+    total_rows = w.rows if w.kind == "vocab" else w.rows * world  # vocab shards split the same rows
+    value = total_rows * args.steps / seconds
     bytes_per_launch = w.rows * w.bytes_per_row
     kernel_s = ktime / reps
     achieved = bytes_per_launch / kernel_s / 1e9
@@ -562,14 +595,15 @@ def run_b200_arm(args):
     line = {
         "metric": "rows/s", "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "scaling": "strong" if w.kind == "vocab" else "weak", "vs_baseline": None, "dtype": w.dtype,
         "data": "synthetic (seeded, generated on device)",
         "config": {"workload": w.name, "rows_per_gpu": w.rows, "vocab": w.vocab,
                    "cluster": args.cluster or "auto",
                    "bytes_per_row": w.bytes_per_row,
                    "l2": (f"inputs {w.rows * w.bytes_per_row * w.batches / 1e9:.2f} GB per GPU rotated "
                           f"({w.batches} batch(es)) > 126 MB L2; no flush"),
-                   "parallelism": f"row-sharded x{world}, no collective"},
+                   "parallelism": (f"vocab-sharded x{world}, NCCL all-gather of partials" if w.kind == "vocab"
+                                   else f"row-sharded x{world}, no collective")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": "select_rows_kernel (masked argmax + count)" if w.kind != "sample"

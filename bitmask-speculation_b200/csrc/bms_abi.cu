@@ -174,12 +174,12 @@ constexpr double kRowCostSampler[5] = {5.0, 8.0, 12.0, 16.0, 20.0};
 
 // Choose the cluster size that minimises the streaming plus row-end work of the busiest CTA.
 Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens_per_chunk, int max_chunks,
-                 bool sampler) {
+                 bool sampler, bool single) {
     Plan best{0, 0, 0};
     double best_cost = 0.0;
     for (int i = 0; i < 5; ++i) {
         const int c = kClusterSizes[i];
-        if (g_force_cluster && c != g_force_cluster) continue;
+        if (single ? c != 1 : (g_force_cluster && c != g_force_cluster)) continue;
         const int resident = info.max_clusters[i];
         if (resident <= 0) continue;
         const int64_t seg = ((vocab + c - 1) / c + 31) / 32 * 32;
@@ -203,7 +203,7 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     KernelInfo* info = nullptr;
     BMS_CHECK((kernel_info<T, kSample, kBulk, kStages>(device, info)));
     const Plan plan = plan_launch(*info, p.rows, p.vocab, Layout<T>::kTokensPerChunk, kSample ? kMaxChunksSampler : 0,
-                                  kSample);
+                                  kSample, p.partials != nullptr);
     if (plan.cluster == 0)
         return fail(BMS_ERROR_UNSUPPORTED, "vocabulary of %lld tokens exceeds the %s limit", static_cast<long long>(p.vocab),
                     kSample ? "sampler" : "selection");
@@ -355,6 +355,75 @@ __global__ void __launch_bounds__(256) verify_epilogue_kernel(
     }
 }
 
+// Merge of vocabulary-shard partials, one warp per row (grid-stride).  partials is [shards, rows]
+// in shard order.  The sampler's owner walk re-reads this rank's shard (the same device functions
+// as the single-GPU cluster merge, so both produce identical bits).
+template <typename T, bool kSample>
+__global__ void __launch_bounds__(128) shard_merge_kernel(
+    const GatherSlot* __restrict__ partials, int32_t shards, int32_t shard, int64_t rows, double temperature,
+    float scale2, const double* __restrict__ uniforms, const uint8_t* __restrict__ logits,
+    const int32_t* __restrict__ masks, int64_t mask_words, int64_t vocab_shard, int64_t token_offset,
+    const uint8_t* __restrict__ granules, int64_t granule_stride, int64_t* __restrict__ tokens,
+    int64_t* __restrict__ counts, int32_t* __restrict__ status) {
+    __shared__ float walk[4][32][33];
+    __shared__ double fac[4][kConsumerWarps];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wib; row < rows; row += nwarps) {
+        if constexpr (!kSample) {
+            const bool in = lane < shards;
+            const GatherSlot g = in ? partials[lane * rows + row] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
+            const uint32_t hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
+            const uint32_t lo = __reduce_max_sync(0xFFFFFFFFu, (in && g.a == hi) ? g.b : 0u);
+            const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, g.c);
+            const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, g.d);
+            if (lane == 0) {
+                const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
+                status[row] = code;
+                tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
+                if (counts) counts[row] = total;
+            }
+        } else {
+            const SampleMerge mg = merge_sampler_ranks(partials + row, rows, static_cast<uint32_t>(shards), uniforms[row],
+                                                       temperature, 0u);
+            int64_t token = -1;
+            int32_t code = mg.code;
+            if (mg.code == kOk && mg.owner == shard) {
+                const uint8_t* rec = granules + row * granule_stride;
+                const bool has = lane < kConsumerWarps;
+                const float wmax = has ? reinterpret_cast<const float*>(rec + SamplerRecord::kWarpMaxOffset)[lane] : 0.0f;
+                const double wmass = has ? reinterpret_cast<const double*>(rec + SamplerRecord::kWarpMassOffset)[lane] : 0.0;
+                const int nchunks = static_cast<int>((vocab_shard + Layout<T>::kTokensPerChunk - 1) / Layout<T>::kTokensPerChunk);
+                const uint8_t* lrow = logits + static_cast<size_t>(row) * static_cast<size_t>(vocab_shard) * sizeof(T);
+                const int32_t* mrow = masks + static_cast<size_t>(row) * static_cast<size_t>(mask_words) + (token_offset >> 5);
+                const int64_t chosen = sampler_owner_walk<T>(
+                    reinterpret_cast<const double*>(rec + SamplerRecord::kGranuleOffset), nchunks * kConsumerWarps, wmax,
+                    wmass, has, mg, temperature, scale2, 0, vocab_shard, lrow, mrow, walk[wib], fac[wib], lane);
+                token = chosen >= 0 ? token_offset + chosen : -1;
+                if (chosen < 0) code = kNoMass;
+            }
+            if (lane == 0) {
+                // Only the owner knows the token; the others report -1 (combine ranks with a max).
+                status[row] = code;
+                tokens[row] = token;
+                if (counts) counts[row] = mg.total;
+            }
+        }
+    }
+}
+
+float sampler_scale2(double temperature) {
+    float scf = static_cast<float>(2.0 * 1.4426950408889634 / temperature);
+    const float tiny = 1.40129846e-45f;
+    if (!(scf >= tiny)) scf = tiny;
+    return scf;
+}
+
+int64_t granule_bytes(int dtype, int64_t vocab_shard) {
+    const int64_t tpc = kChunkBytes / elem_bytes(dtype);
+    return SamplerRecord::bytes(static_cast<int>((vocab_shard + tpc - 1) / tpc));
+}
+
 int check_policy(const bms_policy* policy) {
     if (policy == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "policy must not be NULL when budgets are requested");
     const bms_policy& P = *policy;
@@ -469,11 +538,7 @@ int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* ma
     p.temperature = temperature;
     // 2*log2(e)/T in float; +inf for tiny T, clamped to the smallest denormal for huge T so
     // that -inf logits still map to zero weight.
-    const double sc = 2.0 * 1.4426950408889634 / temperature;
-    float scf = static_cast<float>(sc);
-    const float tiny = 1.40129846e-45f;
-    if (!(scf >= tiny)) scf = tiny;
-    p.scale2 = scf;
+    p.scale2 = sampler_scale2(temperature);
     p.scale = static_cast<float>(1.4426950408889634 / temperature);
     return launch_select<true>(dtype, p, device, static_cast<cudaStream_t>(stream));
 }
@@ -566,6 +631,107 @@ int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, in
                                 static_cast<const int32_t*>(row_status), seqs, rows_per_seq, vocab, proposals, lengths,
                                 P, row_budget, accept_len, token, kind, seq_status),
              "verification epilogue launch");
+    return BMS_SUCCESS;
+}
+
+int64_t bms_shard_granule_bytes(int32_t dtype, int64_t vocab_shard) {
+    if (check_dtype(dtype) != BMS_SUCCESS || vocab_shard <= 0) return -1;
+    return granule_bytes(dtype, vocab_shard);
+}
+
+int bms_shard_partials(const void* logits, int32_t dtype, const int32_t* masks, int64_t mask_words, int64_t rows,
+                       int64_t vocab_shard, int64_t token_offset, double temperature, bms_partial* partials,
+                       void* granules, int64_t granule_stride, int32_t device, void* stream) {
+    if (!std::isfinite(temperature) || temperature < 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "temperature must be finite and nonnegative");
+    if (token_offset < 0 || token_offset % 32 != 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "token_offset must be a nonnegative multiple of 32");
+    BMS_CHECK(check_vocab(vocab_shard));
+    if (token_offset + vocab_shard > 2147483647LL) return fail(BMS_ERROR_INVALID_ARGUMENT, "vocabulary exceeds int32");
+    if (mask_words < (token_offset + vocab_shard + 31) / 32)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "mask_words must cover token_offset + vocab_shard");
+    BMS_CHECK(select_common(dtype, logits, masks, rows, vocab_shard, device));
+    if (rows == 0) return BMS_SUCCESS;
+    BMS_CHECK(check_ptr(partials, device, "partials", 16));
+    const bool sample = temperature != 0;
+    if (sample) {
+        BMS_CHECK(check_ptr(granules, device, "granules", 16));
+        if (granule_stride < granule_bytes(dtype, vocab_shard) || granule_stride % 16 != 0)
+            return fail(BMS_ERROR_INVALID_ARGUMENT, "granule_stride must be a multiple of 16 of at least %lld bytes",
+                        static_cast<long long>(granule_bytes(dtype, vocab_shard)));
+    }
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    SelectParams p = base_params(logits, masks, rows, vocab_shard);
+    p.mask_stride = mask_words;
+    p.mask_word_offset = token_offset / 32;
+    p.token_offset = token_offset;
+    p.partials = reinterpret_cast<GatherSlot*>(partials);
+    if (!sample) return launch_select<false>(dtype, p, device, static_cast<cudaStream_t>(stream));
+    p.granule_out = static_cast<uint8_t*>(granules);
+    p.granule_stride = granule_stride;
+    p.temperature = temperature;
+    p.scale2 = sampler_scale2(temperature);
+    p.scale = static_cast<float>(1.4426950408889634 / temperature);
+    return launch_select<true>(dtype, p, device, static_cast<cudaStream_t>(stream));
+}
+
+int bms_shard_merge(const bms_partial* partials, int32_t shards, int32_t shard, int64_t rows, double temperature,
+                    const double* uniforms, const void* logits, int32_t dtype, const int32_t* masks, int64_t mask_words,
+                    int64_t vocab_shard, int64_t token_offset, const void* granules, int64_t granule_stride,
+                    int64_t* tokens, int64_t* counts, int32_t* status, int32_t device, void* stream) {
+    if (shards < 1 || shards > 32) return fail(BMS_ERROR_INVALID_ARGUMENT, "shards must be in [1, 32]");
+    if (shard < 0 || shard >= shards) return fail(BMS_ERROR_INVALID_ARGUMENT, "shard must be in [0, shards)");
+    if (rows < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows must be nonnegative");
+    if (!std::isfinite(temperature) || temperature < 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "temperature must be finite and nonnegative");
+    BMS_CHECK(check_device(device));
+    if (rows == 0) return BMS_SUCCESS;
+    BMS_CHECK(check_ptr(partials, device, "partials", 16));
+    BMS_CHECK(check_ptr(tokens, device, "tokens", 8));
+    if (counts) BMS_CHECK(check_ptr(counts, device, "counts", 8));
+    BMS_CHECK(check_ptr(status, device, "status", 4));
+    const bool sample = temperature != 0;
+    if (sample) {
+        BMS_CHECK(check_dtype(dtype));
+        BMS_CHECK(check_vocab(vocab_shard));
+        if (token_offset < 0 || token_offset % 32 != 0 || mask_words < (token_offset + vocab_shard + 31) / 32)
+            return fail(BMS_ERROR_INVALID_ARGUMENT, "invalid shard token_offset / mask_words");
+        BMS_CHECK(check_ptr(uniforms, device, "uniforms", 8));
+        BMS_CHECK(check_ptr(logits, device, "logits", static_cast<size_t>(elem_bytes(dtype))));
+        BMS_CHECK(check_ptr(masks, device, "masks", 4));
+        BMS_CHECK(check_ptr(granules, device, "granules", 16));
+        if (granule_stride < granule_bytes(dtype, vocab_shard))
+            return fail(BMS_ERROR_INVALID_ARGUMENT, "granule_stride too small");
+    }
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
+    const int64_t need = (rows + 3) / 4;
+    const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const GatherSlot* parts = reinterpret_cast<const GatherSlot*>(partials);
+    const float sc2 = sample ? sampler_scale2(temperature) : 0.0f;
+    const uint8_t* lg = static_cast<const uint8_t*>(logits);
+    const uint8_t* gr = static_cast<const uint8_t*>(granules);
+    if (!sample) {
+        shard_merge_kernel<float, false><<<grid, 128, 0, s>>>(parts, shards, shard, rows, 0.0, 0.0f, nullptr, nullptr,
+                                                              nullptr, 0, 0, 0, nullptr, 0, tokens, counts, status);
+    } else if (dtype == BMS_FLOAT32) {
+        shard_merge_kernel<float, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, sc2, uniforms, lg,
+                                                             masks, mask_words, vocab_shard, token_offset, gr,
+                                                             granule_stride, tokens, counts, status);
+    } else if (dtype == BMS_BFLOAT16) {
+        shard_merge_kernel<__nv_bfloat16, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, sc2,
+                                                                     uniforms, lg, masks, mask_words, vocab_shard,
+                                                                     token_offset, gr, granule_stride, tokens, counts,
+                                                                     status);
+    } else {
+        shard_merge_kernel<__half, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, sc2, uniforms, lg,
+                                                              masks, mask_words, vocab_shard, token_offset, gr,
+                                                              granule_stride, tokens, counts, status);
+    }
+    BMS_CUDA(cudaGetLastError(), "shard merge launch");
     return BMS_SUCCESS;
 }
 

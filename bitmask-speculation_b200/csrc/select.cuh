@@ -212,6 +212,15 @@ __device__ __forceinline__ float lane_mass(const uint32_t (&q16)[kVecsPerLane][4
 }
 
 // ----------------------------------------------------------------- params
+// Per-row partial of one rank (cluster CTA or vocabulary shard), 32 bytes.  Argmax: a = ordered
+// max bits, b = ~(global index of the first maximum), c = valid count, d = flags.  Sampler:
+// a = max bits, b = valid count, c = flags, s = mass relative to the max.
+struct alignas(16) GatherSlot {
+    uint32_t a, b, c, d;
+    double s;
+    double pad;
+};
+
 struct SelectParams {
     const void* logits;      // [rows, logit_stride] elements
     const int32_t* masks;    // [rows, mask_stride] words
@@ -229,6 +238,11 @@ struct SelectParams {
     double temperature;
     float scale2;            // 2 * log2(e) / T as float, clamped to >= the smallest denormal
     float scale;             // log2(e) / T as float (inf for tiny T)
+    // vocabulary shards
+    int64_t mask_word_offset;  // added to every mask word index (the shard's first word in the full row)
+    GatherSlot* partials;      // non-null: write one partial record per row instead of the outputs
+    uint8_t* granule_out;      // sampler partials: per-row granule record (SamplerRecord layout)
+    int64_t granule_stride;    // bytes between granule records
 };
 
 // Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).
@@ -250,12 +264,6 @@ struct Layout {
     static constexpr int kMaskWords = kTokensPerChunk / 32 + 4;  // + misalignment slack
     static constexpr int kMaskBytes = ((kMaskWords * 4) + 15) / 16 * 16;
     static constexpr int kStageBytes = kChunkBytes + kMaskBytes;
-};
-
-struct alignas(16) GatherSlot {
-    uint32_t a, b, c, d;  // argmax: key_hi, key_lo, count, flags | sampler: M bits, count, flags, 0
-    double s;             // sampler: segment mass relative to M
-    double pad;
 };
 
 // One consumer warp's contribution to one row.
@@ -387,6 +395,171 @@ __device__ __forceinline__ void cluster_allgather(Shared& sh, uint32_t slot, uin
     wait_bounded(ptx::smem_addr(&sh.gather[slot]), parity, &sh.abort, true);
 }
 
+// ----------------------------------------------------------------- sampler merge and walk
+// One row's per-rank sampler partials merged in rank order -- the same arithmetic whether the
+// ranks are CTAs of a cluster or vocabulary shards on different GPUs.
+struct SampleMerge {
+    int32_t code;
+    uint32_t total;
+    int owner;      // rank holding the first crossing of u * total (or the last positive rank)
+    bool fallback;  // rounding left u * total past the last positive mass
+    double M, cutoff, prefix;
+};
+
+__device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, int64_t stride, uint32_t n, double u,
+                                                           double temp, uint32_t extra_flags) {
+    const float kInf = __int_as_float(0x7F800000);
+    SampleMerge r;
+    float rm = -kInf;
+    uint32_t total = 0, fl = extra_flags;
+    for (uint32_t q = 0; q < n; ++q) {
+        const GatherSlot& e = g[q * stride];
+        rm = fmaxf(rm, __uint_as_float(e.a));
+        total += e.b;
+        fl |= e.c;
+    }
+    r.total = total;
+    r.code = (fl & kFlagAbort) ? kTimeout
+             : (fl & kFlagNaN) ? kNaN
+             : (rm == kInf) ? kPosInf
+             : (total == 0u) ? kEmpty
+             : (rm == -kInf) ? kNoMass
+             : !(u >= 0.0 && u < 1.0) ? kBadUniform
+                                      : kOk;
+    r.M = rm;
+    r.owner = -1;
+    r.fallback = false;
+    r.cutoff = 0.0;
+    r.prefix = 0.0;
+    if (r.code != kOk) return r;
+    double total_mass = 0.0;
+    for (uint32_t q = 0; q < n; ++q) {
+        const GatherSlot& e = g[q * stride];
+        if (e.s > 0.0) total_mass += e.s * exp((static_cast<double>(__uint_as_float(e.a)) - r.M) / temp);
+    }
+    r.cutoff = u * total_mass;
+    int last_pos = -1;
+    double run = 0.0, last_prefix = 0.0;
+    for (uint32_t q = 0; q < n; ++q) {
+        const GatherSlot& e = g[q * stride];
+        const double m = e.s > 0.0 ? e.s * exp((static_cast<double>(__uint_as_float(e.a)) - r.M) / temp) : 0.0;
+        if (!(m > 0.0)) continue;
+        last_pos = static_cast<int>(q);
+        last_prefix = run;
+        if (r.owner < 0 && r.cutoff < run + m) {
+            r.owner = static_cast<int>(q);
+            r.prefix = run;
+        }
+        run += m;
+    }
+    if (r.owner < 0) {
+        r.fallback = true;
+        r.owner = last_pos;
+        r.prefix = last_prefix;
+    }
+    return r;
+}
+
+// The owning rank's walk (one warp): find the granule holding the crossing from the granule
+// masses (each relative to its warp's max, `fac` rescales to the row max), then the lane of that
+// granule with fp32 weights, then the token with the reference's exact fp64 weights.  Lane w < 8
+// passes its warp's (max, mass).  Returns the token's index within the row (-1 if none).
+template <typename T>
+__device__ int64_t sampler_owner_walk(const double* granules, int ngran, float wmax, double wmass, bool has_warp,
+                                      const SampleMerge& mg, double temp, float scale2, int64_t seg_begin,
+                                      int64_t seg_end, const uint8_t* lrow, const int32_t* mrow, float (*walk)[33],
+                                      double* fac, int lane) {
+    using E = Elem<T>;
+    constexpr int kTPC = Layout<T>::kTokensPerChunk;
+    constexpr int kTPW = Layout<T>::kTokensPerWarp;
+    constexpr int kFinPer = kTPW / 32;
+    const double M = mg.M, cutoff = mg.cutoff, prefix = mg.prefix;
+    const bool fallback = mg.fallback;
+    if (has_warp) fac[lane] = wmass > 0.0 ? exp((static_cast<double>(wmax) - M) / temp) : 0.0;
+    __syncwarp();
+    const int per = (ngran + 31) / 32;
+    const int g0 = lane * per, g1 = min(g0 + per, ngran);
+    double local = 0.0;
+    for (int g = g0; g < g1; ++g) local += granules[g] * fac[g % kConsumerWarps];
+    const double incl = warp_inclusive_scan(local, lane);
+    double acc = prefix + incl - local;
+    int cand = 0x7FFFFFFF, lastg = -1;
+    double cand_prefix = 0.0;
+    for (int g = g0; g < g1; ++g) {
+        const double m = granules[g] * fac[g % kConsumerWarps];
+        if (!(m > 0.0)) continue;
+        lastg = g;
+        if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) {
+            cand = g;
+            cand_prefix = acc;
+        }
+        acc += m;
+    }
+    int gsel = __reduce_min_sync(0xFFFFFFFFu, cand);
+    const bool walk_fallback = gsel == 0x7FFFFFFF;
+    double gprefix = 0.0;
+    if (walk_fallback) {
+        gsel = __reduce_max_sync(0xFFFFFFFFu, lastg);
+    } else {
+        const uint32_t owner_lane = __ffs(__ballot_sync(0xFFFFFFFFu, cand == gsel)) - 1;
+        gprefix = __shfl_sync(0xFFFFFFFFu, cand_prefix, owner_lane);
+    }
+    if (gsel < 0) return -1;
+    const int gc = gsel / kConsumerWarps, gw = gsel % kConsumerWarps;
+    const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
+    const int64_t gt1 = min(gt0 + kTPW, seg_end);
+    const int64_t my0 = gt0 + lane * kFinPer;
+    uint32_t bits;
+    {
+        Slice<E, kFinPer> sl;
+        load_slice<E, kFinPer>(lrow, mrow, my0, gt1, sl);
+#pragma unroll
+        for (int i = 0; i < kFinPer; ++i) walk[lane][i] = sl.value(i);
+        bits = sl.bits;
+    }
+    __syncwarp();
+    // (1) fp32 weights relative to M locate the lane whose tokens hold the crossing (its fp32
+    // prefix is within ~1e-7 of the exact one).
+    float lsum = 0.0f;
+    {
+        const float hm = -0.5f * static_cast<float>(M);
+#pragma unroll
+        for (int i = 0; i < kFinPer; ++i) {
+            const float t = fminf(fmaf(walk[lane][i], 0.5f, hm) * scale2, 0.0f);
+            const float w = ptx::ex2(t);
+            lsum += ((bits >> i) & 1u) ? w : 0.0f;
+        }
+    }
+    const double lsum_d = lsum;
+    const double lincl = warp_inclusive_scan(lsum_d, lane);
+    const bool positive = lsum > 0.0f;
+    const uint32_t pos_mask = __ballot_sync(0xFFFFFFFFu, positive);
+    const uint32_t cross_mask = __ballot_sync(0xFFFFFFFFu, !walk_fallback && positive && cutoff < gprefix + lincl);
+    const bool lane_fallback = cross_mask == 0u;
+    const int L = lane_fallback ? (pos_mask ? 31 - __clz(pos_mask) : -1) : __ffs(cross_mask) - 1;
+    if (L < 0) return -1;
+    // (2) exact fp64 weights of lane L's tokens, one per lane, scanned in token order.
+    const uint32_t bitsL = __shfl_sync(0xFFFFFFFFu, bits, L);
+    const double prefixL = gprefix + __shfl_sync(0xFFFFFFFFu, lincl - lsum_d, L);
+    const bool mine = lane < kFinPer && ((bitsL >> lane) & 1u);
+    const double w = mine ? exact_weight(walk[L][lane < kFinPer ? lane : 0], M, temp) : 0.0;
+    const double winc = warp_inclusive_scan(w, lane);
+    const uint32_t hits = __ballot_sync(0xFFFFFFFFu, !lane_fallback && w > 0.0 && cutoff < prefixL + winc);
+    const uint32_t pos = __ballot_sync(0xFFFFFFFFu, w > 0.0);
+    const int64_t base = gt0 + static_cast<int64_t>(L) * kFinPer;
+    if (hits) return base + (__ffs(hits) - 1);
+    if (pos) return base + (31 - __clz(pos));  // rounding: the last positive weight
+    return -1;
+}
+
+// Byte layout of a sampler partial's granule record (vocabulary shards).
+struct SamplerRecord {
+    static constexpr int64_t kWarpMaxOffset = 0;                           // float[8]
+    static constexpr int64_t kWarpMassOffset = 32;                         // double[8]
+    static constexpr int64_t kGranuleOffset = 96;                          // double[chunks * 8]
+    static constexpr int64_t bytes(int chunks) { return kGranuleOffset + 8ll * chunks * kConsumerWarps; }
+};
+
 // ----------------------------------------------------------------- the kernel
 template <typename T, bool kSample, bool kBulk, int kStages>
 __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectParams p) {
@@ -450,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             for (int64_t row = row_begin; row < row_end && !stop; ++row) {
                 const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                       static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-                const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+                const int32_t* mbase = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
                 for (int c = 0; c < nchunks; ++c, ++it) {
                     const int stage = static_cast<int>(it % kStages);
                     const uint32_t use = it / kStages;
@@ -461,14 +634,14 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
                     const int64_t t1 = (t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end;
                     const uint32_t lbytes = static_cast<uint32_t>((t1 - t0) * E::kBytes);
-                    const int64_t w0 = t0 >> 5, w1 = (t1 + 31) >> 5;
+                    const int64_t w0 = p.mask_word_offset + (t0 >> 5), w1 = p.mask_word_offset + ((t1 + 31) >> 5);
                     const int64_t a0 = w0 & ~int64_t(3), a1 = (w1 + 3) & ~int64_t(3);
                     const uint32_t mbytes = static_cast<uint32_t>((a1 - a0) * 4);
                     uint8_t* st = stages + stage * L::kStageBytes;
                     const uint32_t full = ptx::smem_addr(&sh.full[stage]);
                     ptx::mbar_arrive_expect_tx(full, lbytes + mbytes);
                     ptx::bulk_load(ptx::smem_addr(st), lrow + t0 * E::kBytes, lbytes, full);
-                    ptx::bulk_load(ptx::smem_addr(st + kChunkBytes), mrow + a0, mbytes, full);
+                    ptx::bulk_load(ptx::smem_addr(st + kChunkBytes), mbase + a0, mbytes, full);
                 }
             }
             // Every issued copy must have landed before this CTA's shared memory can go away.
@@ -487,7 +660,8 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             const uint32_t slot = k & 1u;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-            const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+            const int32_t* mrow =
+                p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
             wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort);
             const bool in = lane < kConsumerWarps;
             const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u, 0.0, 0.0};
@@ -517,8 +691,12 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 }
                 uint32_t hi = ckey;
                 uint32_t lo = __reduce_min_sync(0xFFFFFFFFu, found);
-                lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - lo;
+                lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - static_cast<uint32_t>(p.token_offset + lo);
                 uint32_t total = cnt, fl = flags;
+                if (p.partials != nullptr) {  // vocabulary shard: the row's partial is the output
+                    if (lane == 0) p.partials[row] = GatherSlot{hi, lo, total, fl, 0.0, 0.0};
+                    continue;
+                }
                 if (csize > 1) {
                     if (lane == 0)
                         cluster_allgather(sh, slot, crank, csize, GatherSlot{hi, lo, total, fl, 0.0, 0.0}, (k >> 1) & 1u);
@@ -533,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 if (crank == 0 && lane == 0) {
                     const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
                     p.status[row] = code;
-                    p.tokens[row] = code == kOk ? p.token_offset + static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
+                    p.tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
                     if (p.counts) p.counts[row] = total;
                 }
             } else {
@@ -548,155 +726,40 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                                         ? wp.mass * exp((static_cast<double>(wmax) - static_cast<double>(seg_m)) / p.temperature)
                                         : 0.0;
                 const double seg_s = warp_sum(term);
-                // Rank partials, all-gathered in rank order.
-                if (lane == 0) {
-                    const GatherSlot mine{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
-                    if (csize > 1) cluster_allgather(sh, slot, crank, csize, mine, (k >> 1) & 1u);
-                    else sh.slots[slot][0] = mine;
-                }
-                __syncwarp();
-                float rm = -kInf;
-                uint32_t total = 0, fl = sh.abort ? kFlagAbort : 0u;
-                for (uint32_t q = 0; q < csize; ++q) {
-                    const GatherSlot& g = sh.slots[slot][q];
-                    rm = fmaxf(rm, __uint_as_float(g.a));
-                    total += g.b;
-                    fl |= g.c;
-                }
-                const double u = p.uniforms[row];
-                const int32_t code = (fl & kFlagAbort) ? kTimeout
-                                     : (fl & kFlagNaN) ? kNaN
-                                     : (rm == kInf) ? kPosInf
-                                     : (total == 0u) ? kEmpty
-                                     : (rm == -kInf) ? kNoMass
-                                     : !(u >= 0.0 && u < 1.0) ? kBadUniform
-                                                              : kOk;
-                if (code != kOk) {
-                    if (crank == 0 && lane == 0) {
-                        p.status[row] = code;
-                        p.tokens[row] = -1;
-                        if (p.counts) p.counts[row] = total;
+                if (p.partials != nullptr) {
+                    // Vocabulary shard: the row's partial and granule record are the output.
+                    if (lane == 0) p.partials[row] = GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
+                    uint8_t* rec = p.granule_out + row * p.granule_stride;
+                    if (in) {
+                        reinterpret_cast<float*>(rec + SamplerRecord::kWarpMaxOffset)[lane] = wmax;
+                        reinterpret_cast<double*>(rec + SamplerRecord::kWarpMassOffset)[lane] = wp.mass;
                     }
+                    double* rg = reinterpret_cast<double*>(rec + SamplerRecord::kGranuleOffset);
+                    for (int g = lane; g < ngran; g += 32) rg[g] = granules[g];
                 } else {
-                    const double M = rm;
-                    const double temp = p.temperature;
-                    // Rank masses in rank order; the owner holds the first crossing of u * total.
-                    double total_mass = 0.0;
-                    for (uint32_t q = 0; q < csize; ++q) {
-                        const GatherSlot& g = sh.slots[slot][q];
-                        if (g.s > 0.0) total_mass += g.s * exp((static_cast<double>(__uint_as_float(g.a)) - M) / temp);
+                    // Rank partials, all-gathered in rank order, merged identically on every rank.
+                    if (lane == 0) {
+                        const GatherSlot mine{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
+                        if (csize > 1) cluster_allgather(sh, slot, crank, csize, mine, (k >> 1) & 1u);
+                        else sh.slots[slot][0] = mine;
                     }
-                    const double cutoff = u * total_mass;
-                    int owner = -1, last_pos = -1;
-                    double prefix = 0.0, run = 0.0, last_prefix = 0.0;
-                    for (uint32_t q = 0; q < csize; ++q) {
-                        const GatherSlot& g = sh.slots[slot][q];
-                        const double m = g.s > 0.0 ? g.s * exp((static_cast<double>(__uint_as_float(g.a)) - M) / temp) : 0.0;
-                        if (!(m > 0.0)) continue;
-                        last_pos = static_cast<int>(q);
-                        last_prefix = run;
-                        if (owner < 0 && cutoff < run + m) {
-                            owner = static_cast<int>(q);
-                            prefix = run;
+                    __syncwarp();
+                    const SampleMerge mg = merge_sampler_ranks(sh.slots[slot], 1, csize, p.uniforms[row], p.temperature,
+                                                               sh.abort ? kFlagAbort : 0u);
+                    if (mg.code != kOk) {
+                        if (crank == 0 && lane == 0) {
+                            p.status[row] = mg.code;
+                            p.tokens[row] = -1;
+                            if (p.counts) p.counts[row] = mg.total;
                         }
-                        run += m;
-                    }
-                    const bool fallback = owner < 0;
-                    if (fallback) {
-                        owner = last_pos;
-                        prefix = last_prefix;
-                    }
-                    if (owner == static_cast<int>(crank)) {
-                        // Granule holding the crossing: contiguous blocks of granules per lane.
-                        // Factor from each warp's max to the row max, shared by its granules.
-                        const double fac_mine = (in && wp.mass > 0.0)
-                                                    ? exp((static_cast<double>(wmax) - M) / temp) : 0.0;
-                        if (in) ss.fac[lane] = fac_mine;
-                        __syncwarp();
-                        const double* fac = ss.fac;
-                        const int per = (ngran + 31) / 32;
-                        const int g0 = lane * per, g1 = min(g0 + per, ngran);
-                        double local = 0.0;
-                        for (int g = g0; g < g1; ++g) local += granules[g] * fac[g % kConsumerWarps];
-                        const double incl = warp_inclusive_scan(local, lane);
-                        double acc = prefix + incl - local;
-                        int cand = 0x7FFFFFFF, lastg = -1;
-                        double cand_prefix = 0.0;
-                        for (int g = g0; g < g1; ++g) {
-                            const double m = granules[g] * fac[g % kConsumerWarps];
-                            if (!(m > 0.0)) continue;
-                            lastg = g;
-                            if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) {
-                                cand = g;
-                                cand_prefix = acc;
-                            }
-                            acc += m;
-                        }
-                        int gsel = __reduce_min_sync(0xFFFFFFFFu, cand);
-                        const bool walk_fallback = gsel == 0x7FFFFFFF;
-                        double gprefix = 0.0;
-                        if (walk_fallback) {
-                            gsel = __reduce_max_sync(0xFFFFFFFFu, lastg);
-                        } else {
-                            const uint32_t owner_lane = __ffs(__ballot_sync(0xFFFFFFFFu, cand == gsel)) - 1;
-                            gprefix = __shfl_sync(0xFFFFFFFFu, cand_prefix, owner_lane);
-                        }
-                        int64_t chosen = -1;
-                        if (gsel >= 0) {
-                            // Walk the granule in token order with exact fp64 weights.
-                            const int gc = gsel / kConsumerWarps, gw = gsel % kConsumerWarps;
-                            const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
-                            const int64_t gt1 = min(gt0 + kTPW, seg_end);
-                            const int64_t my0 = gt0 + lane * kFinPer;
-                            uint32_t bits;
-                            {
-                                Slice<E, kFinPer> sl;
-                                load_slice<E, kFinPer>(lrow, mrow, my0, gt1, sl);
-#pragma unroll
-                                for (int i = 0; i < kFinPer; ++i) ss.walk[lane][i] = sl.value(i);
-                                bits = sl.bits;
-                            }
-                            __syncwarp();
-                            // (1) fp32 weights relative to M locate the lane whose tokens hold the
-                            // crossing (its fp32 prefix is within ~1e-7 of the exact one).
-                            float lsum = 0.0f;
-                            {
-                                const float hm = -0.5f * static_cast<float>(M);
-                                const float sc2 = p.scale2;
-#pragma unroll
-                                for (int i = 0; i < kFinPer; ++i) {
-                                    float t = fmaf(ss.walk[lane][i], 0.5f, hm) * sc2;
-                                    t = fminf(t, 0.0f);
-                                    const float w = ptx::ex2(t);
-                                    lsum += ((bits >> i) & 1u) ? w : 0.0f;
-                                }
-                            }
-                            const double lsum_d = lsum;
-                            const double lincl = warp_inclusive_scan(lsum_d, lane);
-                            const bool positive = lsum > 0.0f;
-                            const uint32_t pos_mask = __ballot_sync(0xFFFFFFFFu, positive);
-                            const uint32_t cross_mask =
-                                __ballot_sync(0xFFFFFFFFu, !walk_fallback && positive && cutoff < gprefix + lincl);
-                            const bool lane_fallback = cross_mask == 0u;
-                            const int L = lane_fallback ? (pos_mask ? 31 - __clz(pos_mask) : -1) : __ffs(cross_mask) - 1;
-                            if (L >= 0) {
-                                // (2) exact fp64 weights of lane L's tokens, one per lane, scanned in order.
-                                const uint32_t bitsL = __shfl_sync(0xFFFFFFFFu, bits, L);
-                                const double prefixL = gprefix + __shfl_sync(0xFFFFFFFFu, lincl - lsum_d, L);
-                                const bool mine = lane < kFinPer && ((bitsL >> lane) & 1u);
-                                const double w = mine ? exact_weight(ss.walk[L][lane < kFinPer ? lane : 0], M, temp) : 0.0;
-                                const double incl = warp_inclusive_scan(w, lane);
-                                const uint32_t hits = __ballot_sync(0xFFFFFFFFu, !lane_fallback && w > 0.0 && cutoff < prefixL + incl);
-                                const uint32_t pos = __ballot_sync(0xFFFFFFFFu, w > 0.0);
-                                const int64_t base = gt0 + static_cast<int64_t>(L) * kFinPer;
-                                if (hits) chosen = base + (__ffs(hits) - 1);
-                                else if (pos) chosen = base + (31 - __clz(pos));  // rounding: last positive
-                            }
-                        }
+                    } else if (mg.owner == static_cast<int>(crank)) {
+                        const int64_t chosen =
+                            sampler_owner_walk<T>(granules, ngran, wmax, wp.mass, in, mg, p.temperature, p.scale2,
+                                                  seg_begin, seg_end, lrow, mrow, ss.walk, ss.fac, lane);
                         if (lane == 0) {
                             p.status[row] = chosen >= 0 ? kOk : kNoMass;
                             p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
-                            if (p.counts) p.counts[row] = total;
+                            if (p.counts) p.counts[row] = mg.total;
                         }
                     }
                 }
@@ -712,7 +775,8 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             const uint32_t slot = k & 1u;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-            const int32_t* mrow = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
+            const int32_t* mrow =
+                p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
             // The finalizer has released this row's partial slot (and granule table).
             if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
             double* granules = ss.granules[slot];
@@ -735,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 const uint32_t* smask;
                 if constexpr (kBulk) {
                     wait_bounded(ptx::smem_addr(&sh.full[stage]), (it / kStages) & 1u, &sh.abort);
-                    smask = reinterpret_cast<const uint32_t*>(st + kChunkBytes) + ((t0 >> 5) & 3);
+                    smask = reinterpret_cast<const uint32_t*>(st + kChunkBytes) + ((p.mask_word_offset + (t0 >> 5)) & 3);
                 } else {
                     // Cooperative plain loads for rows the bulk engine cannot address.
                     const int nvec_pad = (ntok + kVec - 1) / kVec * kVec;

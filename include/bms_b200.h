@@ -134,6 +134,44 @@ BMS_API int bms_verify_batch(const void *logits, int32_t dtype, const int32_t *m
                      int32_t *accept_len, int64_t *token, int32_t *kind, int32_t *seq_status,
                      int32_t device, void *stream);
 
+/* ---- vocabulary shards ----------------------------------------------------------------
+ * A row's vocabulary split across ranks (GPUs), each holding logits [rows, vocab_shard] of its
+ * slice and the full mask rows.  Each rank computes one 32-byte partial per row; the partials of
+ * all ranks, gathered in rank order (e.g. an NCCL all-gather), are merged on every rank.  The
+ * merge uses the same arithmetic as the single-GPU kernel's cluster merge, so a single-GPU run
+ * whose cluster ranks cover the same slices gives identical results. No reference counterpart:
+ * the reference ran one row on one device (docs/design.md:10-11). */
+typedef struct bms_partial {
+    uint32_t a, b, c, d; /* argmax: ordered max bits, ~first global index, count, flags;
+                            sampler: max bits, count, flags, 0 */
+    double s;            /* sampler: shard mass relative to its max */
+    double reserved;
+} bms_partial;
+
+/* Bytes of one row's sampler granule record for a shard of `vocab_shard` tokens (-1 if invalid). */
+BMS_API int64_t bms_shard_granule_bytes(int32_t dtype, int64_t vocab_shard);
+
+/* Partials of this rank's shard: tokens [token_offset, token_offset + vocab_shard) of every row
+ * (token_offset a multiple of 32).  `masks` are the full rows ([rows, mask_words] int32).
+ * temperature 0: argmax partials (granules may be NULL); else sampler partials plus one granule
+ * record per row at `granules + row * granule_stride` (stride >= bms_shard_granule_bytes, multiple
+ * of 16). */
+BMS_API int bms_shard_partials(const void *logits, int32_t dtype, const int32_t *masks, int64_t mask_words,
+                               int64_t rows, int64_t vocab_shard, int64_t token_offset, double temperature,
+                               bms_partial *partials, void *granules, int64_t granule_stride, int32_t device,
+                               void *stream);
+
+/* Merge `shards` ranks' partials ([shards, rows] in rank order) on rank `shard`.  temperature 0:
+ * final argmax tokens, counts and status of every row (identical on every rank).  Sampler: status
+ * and counts of every row; `tokens[row]` is the sampled token if it lies in this rank's shard and
+ * -1 otherwise (a max-reduction over ranks gives the token).  The sampler walk re-reads this rank's
+ * shard (`logits`, `masks`, `granules` as given to bms_shard_partials); uniforms are [rows]. */
+BMS_API int bms_shard_merge(const bms_partial *partials, int32_t shards, int32_t shard, int64_t rows,
+                            double temperature, const double *uniforms, const void *logits, int32_t dtype,
+                            const int32_t *masks, int64_t mask_words, int64_t vocab_shard, int64_t token_offset,
+                            const void *granules, int64_t granule_stride, int64_t *tokens, int64_t *counts,
+                            int32_t *status, int32_t device, void *stream);
+
 /* Test hook: force the cluster size (1, 2, 4, 8 or 16) and the number of
  * clusters of the selection kernels; 0 restores the automatic choice.
  * Process-wide; not for concurrent use with other calls. */
