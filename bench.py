@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--rows", type=int, default=8192, help="rows per GPU for the scale workload")
     ap.add_argument("--sample-rows", type=int, default=8,
                     help="rows per sampling batch (the 8 configuration rows tiled, fresh uniforms)")
+    ap.add_argument("--sample-density", type=float, default=None,
+                    help="override every sampling row's mask density (default: the configuration's mix)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--roofline-seconds", type=float, default=1.5)
@@ -175,7 +177,8 @@ class Workload:
             self.name = "argmax: 6 rows fp32 N(0,3^2) at V=248320 (masks .5/.5/4 valid/16 valid/.02/1 valid)"
         elif self.kind == "sample":
             import numpy as np
-            bits, masks, uniforms, temp = wl.sample_config_np(seed=2 + rank)
+            densities = wl.SAMPLE_DENSITIES if args.sample_density is None else (args.sample_density,) * 8
+            bits, masks, uniforms, temp = wl.sample_config_np(seed=2 + rank, densities=densities)
             tile = max(1, args.sample_rows // bits.shape[0])
             bits, masks = np.tile(bits, (tile, 1)), np.tile(masks, (tile, 1))
             uniforms = np.random.default_rng(2 + rank).random(bits.shape[0])

@@ -43,6 +43,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "ptx.cuh"
 
@@ -59,6 +60,8 @@ constexpr int kVecsPerLane = kWarpBytes / 16 / 32;  // 16-byte vectors per lane 
 constexpr int kMaxCluster = 16;
 constexpr int kMaxChunksSampler = 64;  // granule table capacity (chunks per segment)
 constexpr uint64_t kTimeoutNs = 1000000000ull;
+// Sampler: a chunk raises the reference max only if one of its weights would exceed 2^kSlack.
+constexpr float kSlack = 20.0f;
 
 enum Status : int32_t {
     kOk = 0,
@@ -769,8 +772,13 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
         }
     } else {
         // ------------------------------------------------------------ consumer warps
-        uint32_t it = 0;
-        uint32_t k = 0;  // rows processed by this cluster
+        uint32_t stage = 0, phase = 0;  // ring position of the next chunk (matches the producer)
+        uint32_t k = 0;                 // rows processed by this cluster
+        // Chunks holding kTPC tokens (every chunk but a ragged last one) take the unpredicated path.
+        const int nfull = static_cast<int>((seg_end - seg_begin) / kTPC);
+        // A stage's mask words start at the 16-byte boundary at or below the chunk's first word;
+        // chunks start on multiples of 128 words, so the word offset is the same for every chunk.
+        const int moff = static_cast<int>((p.mask_word_offset + (seg_begin >> 5)) & 3);
         for (int64_t row = row_begin; row < row_end; ++row, ++k) {
             const uint32_t slot = k & 1u;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
@@ -787,21 +795,29 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             float best = -kInf;
             int best_idx = -1;
             int first_valid_chunk = -1;
-            // sampler: warp-uniform running max of valid logits
-            float run_m = -kInf;
+            // sampler: a warp-uniform reference max `ref` that trails the running max of valid
+            // logits by less than 2^kSlack in weight (it is only raised when a chunk would exceed
+            // that), and the lane's exact running max.
+            float ref = -kInf, lane_max = -kInf;
+            bool fast = false;  // weights as one FFMA from `ref` (see lane_mass, mode 0)
+            float chi = 0.0f, corr = 1.0f;
+            const float sc = p.scale;
 
-            for (int c = 0; c < nchunks; ++c, ++it) {
-                const int stage = kBulk ? static_cast<int>(it % kStages) : 0;
-                const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
-                const int64_t t1 = (t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end;
-                const int ntok = static_cast<int>(t1 - t0);
-                uint8_t* st = stages + stage * L::kStageBytes;
+            auto chunk = [&](auto full_tag, int c) {
+                constexpr bool kFull = decltype(full_tag)::value;
+                uint8_t* st = stages + (kBulk ? stage : 0u) * L::kStageBytes;
                 const uint32_t* smask;
+                int ntok = kTPC;
+                if constexpr (!kFull) {
+                    const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
+                    ntok = static_cast<int>(((t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end) - t0);
+                }
                 if constexpr (kBulk) {
-                    wait_bounded(ptx::smem_addr(&sh.full[stage]), (it / kStages) & 1u, &sh.abort);
-                    smask = reinterpret_cast<const uint32_t*>(st + kChunkBytes) + ((p.mask_word_offset + (t0 >> 5)) & 3);
+                    wait_bounded(ptx::smem_addr(&sh.full[stage]), phase, &sh.abort);
+                    smask = reinterpret_cast<const uint32_t*>(st + kChunkBytes) + moff;
                 } else {
                     // Cooperative plain loads for rows the bulk engine cannot address.
+                    const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
                     const int nvec_pad = (ntok + kVec - 1) / kVec * kVec;
                     for (int i = tid; i < nvec_pad; i += kConsumerThreads) {
                         uint32_t v = 0u;
@@ -825,16 +841,22 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
 
                 const int nvec = (ntok + kVec - 1) / kVec;
                 const uint8_t* wl = st + warp * kWarpBytes;
-                const uint32_t* wm = smask + warp * (kTPW / 32);
                 uint4 raw[kVecsPerLane];
                 uint32_t bits[kVecsPerLane];
 #pragma unroll
                 for (int j = 0; j < kVecsPerLane; ++j) {
                     const int vec = j * 32 + lane;
-                    const bool in = warp * (kTPW / kVec) + vec < nvec;
+                    const bool in = kFull || warp * (kTPW / kVec) + vec < nvec;
                     raw[j] = in ? *reinterpret_cast<const uint4*>(wl + vec * 16) : make_uint4(0, 0, 0, 0);
-                    const uint32_t word = in ? wm[(vec * kVec) >> 5] : 0u;
-                    bits[j] = (word >> ((vec * kVec) & 31)) & kVecMask;
+                    if constexpr (kVec == 8) {
+                        // 8 tokens per vector: vector v's bits are byte v of the little-endian words.
+                        const uint8_t* wb = reinterpret_cast<const uint8_t*>(smask) + warp * (kTPW / 8);
+                        bits[j] = in ? wb[vec] : 0u;
+                    } else {
+                        const uint32_t* wm = smask + warp * (kTPW / 32);
+                        const uint32_t word = in ? wm[(vec * kVec) >> 5] : 0u;
+                        bits[j] = (word >> ((vec * kVec) & 31)) & kVecMask;
+                    }
                 }
                 // Stage contents are in registers: release it to the producer.
                 if constexpr (kBulk) {
@@ -910,43 +932,54 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                                                E::max2(E::max2(q16[3][0], q16[3][1]), E::max2(q16[3][2], q16[3][3]))));
                         lmax = fmaxf(E::lo(t), E::hi(t));
                     }
-                    // Warp-uniform running max over valid tokens (NaN valid logits are ignored here;
-                    // they fail the row through the NaN flag).
-                    const bool warp_any = __any_sync(0xFFFFFFFFu, anyb != 0u);
-                    if (warp_any) {
+                    lane_max = fmaxf(lane_max, lmax);  // NaN valid logits are ignored here; they fail
+                                                       // the row through the NaN flag
+                    // Raise the reference only when needed: always while it is not usable for the
+                    // one-FFMA form, otherwise when some token would weigh more than 2^kSlack.
+                    const bool need = fast ? __any_sync(0xFFFFFFFFu, fmaf(lmax, sc, chi) > kSlack)
+                                           : __any_sync(0xFFFFFFFFu, anyb != 0u);
+                    if (need) {
                         const uint32_t lkey = (lmax == lmax) ? ordered_bits(lmax) : 0u;
                         const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, lkey);
-                        if (wkey != 0u) run_m = fmaxf(run_m, ordered_to_float(wkey));
+                        if (wkey != 0u) ref = fmaxf(ref, ordered_to_float(wkey));
+                        const float msc = ref * sc;
+                        // One FFMA per token, t = x s - (ref s) rounded: the rounding error `clo` of
+                        // ref s is the same for every token and is folded back once per granule as
+                        // 2^clo ~ 1 + clo ln 2, exact to ~1e-9 for |ref s| < 2^11 (|clo| <= 2^-14).
+                        fast = ref > -kInf && ref < kInf && sc >= 1e-30f && fabsf(msc) < 0x1p11f;
+                        chi = -msc;
+                        const float clo = fmaf(-ref, sc, -chi);
+                        corr = fmaf(clo, 0.6931471805599453f, 1.0f);
                     }
-                    // Pass 2: fp32 weights 2^((x - m) * log2(e) / T) relative to the running max,
-                    // invalid tokens entering as -inf (weight 0).  scale2 = 2 log2(e) / T with
-                    // x - m formed as 0.5x - 0.5m so it cannot overflow.
+                    // Pass 2: fp32 weights 2^((x - ref) * log2(e) / T), invalid tokens entering as
+                    // -inf (weight 0).
                     float mass = 0.0f;
-                    const bool finite_m = run_m > -kInf && run_m < kInf;
-                    if (warp_any && finite_m) {
-                        const float sc = p.scale;
-                        const float msc = run_m * sc;
-                        if (sc >= 1e-30f && fabsf(msc) < 0x1p100f) {
-                            // One FFMA per token: t = x s - (m s) rounded; the rounding error of m s
-                            // is the same for every token, folded back once per granule.
-                            const float chi = -msc;
-                            const float clo = fmaf(-run_m, sc, -chi);
-                            mass = lane_mass<E, 0>(q16, q32, chi, sc);
+                    if (fast) {
+                        mass = lane_mass<E, 0>(q16, q32, chi, sc);
 #pragma unroll
-                            for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
-                            mass = fmaf(mass * clo, 0.6931471805599453f, mass);
-                        } else {
-                            const float nhm = -0.5f * run_m;
-                            const float sc2 = p.scale2;
-                            if (sc2 < kInf) mass = lane_mass<E, 1>(q16, q32, nhm, sc2);
-                            else mass = lane_mass<E, 2>(q16, q32, nhm, sc2);
+                        for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
+                        mass *= corr;
+                    } else if (need && ref > -kInf && ref < kInf) {
+                        // Here ref is the exact running max: x - ref <= 0, formed as 0.5x - 0.5ref
+                        // so that it cannot overflow, times scale2 = 2 log2(e) / T.
+                        const float nhm = -0.5f * ref;
+                        const float sc2 = p.scale2;
+                        if (sc2 < kInf) mass = lane_mass<E, 1>(q16, q32, nhm, sc2);
+                        else mass = lane_mass<E, 2>(q16, q32, nhm, sc2);
 #pragma unroll
-                            for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
-                        }
+                        for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
                     }
-                    if (lane == 0) granules_f[c * kConsumerWarps + warp] = make_float2(run_m, mass);
+                    if (lane == 0) granules_f[c * kConsumerWarps + warp] = make_float2(ref, mass);
                 }
-            }
+                if constexpr (kBulk) {
+                    if (++stage == static_cast<uint32_t>(kStages)) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            };
+            for (int c = 0; c < nfull; ++c) chunk(std::true_type{}, c);
+            if (nfull < nchunks) chunk(std::false_type{}, nfull);
 
             // ---------------------------------------------------- warp partial -> finalizer
             const bool nan_local = E::has_nan(nan_acc);
@@ -955,28 +988,26 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             uint32_t wkey, wchunk = 0xFFFFFFFFu;
             double wmass = 0.0;
             if constexpr (kSample) {
-                // Fold this warp's granules to its final max (one fp64 exp per lane per chunk); the
-                // finalizer then combines 8 warp masses instead of every granule.
+                // The warp's exact max of valid logits; fold its granules to it (one fp64 exp per
+                // lane per chunk) so that the finalizer combines 8 warp masses, not every granule.
+                wkey = __reduce_max_sync(0xFFFFFFFFu, ordered_bits(lane_max));
+                const double wm = static_cast<double>(ordered_to_float(wkey));
                 __syncwarp();
                 double local = 0.0;
                 for (int c = lane; c < nchunks; c += 32) {
                     const float2 e = granules_f[c * kConsumerWarps + warp];
-                    const double gm = e.y > 0.0f ? static_cast<double>(e.y) *
-                                                       exp((static_cast<double>(e.x) - static_cast<double>(run_m)) / p.temperature)
-                                                 : 0.0;
+                    const double gm =
+                        e.y > 0.0f ? static_cast<double>(e.y) * exp((static_cast<double>(e.x) - wm) / p.temperature) : 0.0;
                     granules[c * kConsumerWarps + warp] = gm;
                     local += gm;
                 }
                 wmass = warp_sum(local);
-            }
-            if constexpr (!kSample) {
+            } else {
                 const bool has = best_idx >= 0 || first_valid_chunk >= 0;
                 const uint32_t key = has ? ordered_bits(best) : 0u;
                 wkey = __reduce_max_sync(0xFFFFFFFFu, key);
-                const uint32_t chunk = static_cast<uint32_t>(best_idx >= 0 ? best_idx : first_valid_chunk);
-                wchunk = __reduce_min_sync(0xFFFFFFFFu, (has && key == wkey) ? chunk : 0xFFFFFFFFu);
-            } else {
-                wkey = ordered_bits(run_m);
+                const uint32_t chunk_id = static_cast<uint32_t>(best_idx >= 0 ? best_idx : first_valid_chunk);
+                wchunk = __reduce_min_sync(0xFFFFFFFFu, (has && key == wkey) ? chunk_id : 0xFFFFFFFFu);
             }
             if (lane == 0) {
                 sh.part[slot][warp] = WarpPartial{wkey, wchunk, wcount, wflags, wmass, 0.0};

@@ -258,3 +258,43 @@ def test_extreme_temperatures_and_magnitudes_on_the_bulk_path(cuda_module, tempe
     assert status.tolist() == exp_st.tolist()
     for r in range(rows):
         assert sample_matches(f32[r], masks[r], temperature, u[r], tokens[r].item(), exp_tok[r], TOL), (r, temperature)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("cluster", [0, 1, 4])
+def test_rising_maxima_and_large_offsets(cuda_module, dtype, cluster):
+    """Running maxima that rise chunk after chunk, jumps just below and above 2^20 in weight,
+    and logits far from zero (|max log2(e) / T| beyond 2^11), against the oracle."""
+    rng = np.random.default_rng(77 + cluster)
+    _native.set_launch_override(cluster, 0)
+    vocab, rows = 151936, 8
+    values = rng.standard_normal((rows, vocab), dtype=np.float32)
+    values[0] = np.linspace(-50, 50, vocab, dtype=np.float32)           # rises in every chunk
+    values[1] = np.linspace(50, -50, vocab, dtype=np.float32)           # first chunk holds the max
+    values[2, -3000:] += 9.0                                            # late jump, 2^13 in weight
+    values[3, -3000:] += 16.0                                           # late jump, 2^23 in weight
+    values[4, 70000:70010] = 40.0                                       # isolated spike mid-row
+    if dtype == "float32":
+        values[5] = values[5] * 3 + 3000.0                              # m log2(e) / T ~ 4.3e3
+        values[6] = values[6] * 2 + 1e6                                 # ~1.4e6
+        values[7] = values[7] * 500 + 1e9                               # ~1.4e7 at T = 100
+    else:
+        values[5] = values[5] * 3 + 3000.0
+        values[6] = values[6] * 64 + 1e5
+        values[7] = values[7] * 2048 + 1e7
+    valid = rng.random((rows, vocab)) < 0.6
+    valid[:, -1] = True
+    masks = wl.pack_bits_np(valid)
+    bits = as_dtype_bits(values, dtype)
+    f32 = widened(bits, dtype)
+    for temperature in (0.5, 1.0, 100.0):
+        for trial in range(3):
+            u = rng.random(rows)
+            exp_tok, exp_st = oracle.sample_rows(bits, masks, temperature, u,
+                                                 dtype=None if dtype == "float32" else dtype)
+            tokens, _, status = cuda_module.masked_sample_batch(
+                to_device(bits, dtype), torch.from_numpy(masks).cuda(), temperature, torch.from_numpy(u).cuda())
+            assert status.tolist() == exp_st.tolist()
+            for r in range(rows):
+                assert sample_matches(f32[r], masks[r], temperature, u[r], tokens[r].item(), exp_tok[r], TOL), (
+                    r, temperature, trial)
