@@ -56,6 +56,8 @@ def parse_args():
                     help="rows per sampling batch (the 8 configuration rows tiled, fresh uniforms)")
     ap.add_argument("--sample-density", type=float, default=None,
                     help="override every sampling row's mask density (default: the configuration's mix)")
+    ap.add_argument("--sample-dtype", choices=["float16", "bfloat16"], default="float16",
+                    help="logits type of the sampling workload (the configuration's rows are fp16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--roofline-seconds", type=float, default=1.5)
@@ -184,14 +186,16 @@ class Workload:
             uniforms = np.random.default_rng(2 + rank).random(bits.shape[0])
             reps = max(1, int(2 * L2_BYTES // bits.nbytes) + 1)
             self.logits_all = torch.from_numpy(np.tile(bits, (reps, 1)).view(np.int16)).view(torch.float16).to(device)
+            if args.sample_dtype == "bfloat16":
+                self.logits_all = self.logits_all.to(torch.bfloat16)
             self.masks_all = torch.from_numpy(np.ascontiguousarray(np.tile(masks, (reps, 1)))).to(device)
             self.uniforms_all = torch.from_numpy(np.tile(uniforms, reps)).to(device)
             self.temperature = temp
             self.rows = bits.shape[0]
             self.batches = reps
             self.esize = 2
-            self.dtype = "f16"
-            self.name = (f"sample: {self.rows} rows fp16 N(0,2^2) at V=248320, T=0.7, densities "
+            self.dtype = "f16" if args.sample_dtype == "float16" else "bf16"
+            self.name = (f"sample: {self.rows} rows {self.dtype} N(0,2^2) at V=248320, T=0.7, densities "
                          "{1,.5,.1,.01,1e-4,.9,.3,.05}")
         elif self.kind == "vocab":
             # Every rank builds the same full rows, keeps its vocabulary slice and the full masks.

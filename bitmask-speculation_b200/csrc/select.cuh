@@ -30,8 +30,9 @@
 //    distributed shared memory (st.shared::cluster + remote mbarrier arrive)
 //    and writes the row's outputs -- overlapped with the next row's streaming.
 //    Argmax keys are (order-preserving float bits << 32 | ~index): a max merge.
-//  * The sampler records one (max, mass) pair per (chunk, warp) "granule" in
-//    shared memory during the single streaming pass (fp32 MUFU ex2 weights);
+//  * The sampler records one (reference, mass) pair per (chunk, warp) "granule"
+//    in shared memory during the single streaming pass (fp32 MUFU ex2 weights;
+//    the warp's reference max is raised only when a weight would exceed 2^20);
 //    the finalizer merges ranks in fixed order in fp64, then re-reads only the
 //    granule that holds u * total and walks it with exact fp64 weights
 //    exp((x - M) / T).
@@ -60,8 +61,10 @@ constexpr int kVecsPerLane = kWarpBytes / 16 / 32;  // 16-byte vectors per lane 
 constexpr int kMaxCluster = 16;
 constexpr int kMaxChunksSampler = 64;  // granule table capacity (chunks per segment)
 constexpr uint64_t kTimeoutNs = 1000000000ull;
-// Sampler: a chunk raises the reference max only if one of its weights would exceed 2^kSlack.
-constexpr float kSlack = 20.0f;
+// Sampler: a lane mass above 2^20 raises the warp's reference max (no weight exceeds 2^20).
+constexpr float kRaiseMass = 0x1p20f;
+// Sampler walk: fp32 exponents are clamped here (a reference below the max gives t <= 20).
+constexpr float kWalkClamp = 64.0f;
 
 enum Status : int32_t {
     kOk = 0,
@@ -212,6 +215,36 @@ __device__ __forceinline__ float lane_mass(const uint32_t (&q16)[kVecsPerLane][4
 #pragma unroll
         for (int i = 0; i < h; ++i) part[i] += part[i + h];
     return part[0];
+}
+
+// Mode 0 of lane_mass with paired fp32 arithmetic for 16-bit logits (fma.rn.f32x2 / add.rn.f32x2):
+// the two tokens of a packed pair share one FFMA2 and their weights one FADD2.
+template <typename E>
+__device__ __forceinline__ float lane_mass_fast(const uint32_t (&q16)[kVecsPerLane][4],
+                                                const float (&q32)[kVecsPerLane][E::kVec], float c, float scale) {
+    if constexpr (E::kBytes == 4) {
+        return lane_mass<E, 0>(q16, q32, c, scale);
+    } else {
+        const uint64_t s2 = ptx::pack2(scale, scale), c2 = ptx::pack2(c, c);
+        uint64_t part[kVecsPerLane];
+#pragma unroll
+        for (int j = 0; j < kVecsPerLane; ++j) {
+            uint64_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint64_t t = ptx::fma2(ptx::pack2(E::lo(q16[j][i]), E::hi(q16[j][i])), s2, c2);
+                float t0, t1;
+                ptx::unpack2(t, t0, t1);
+                w[i] = ptx::pack2(ptx::ex2(t0), ptx::ex2(t1));
+            }
+            part[j] = ptx::add2(ptx::add2(w[0], w[1]), ptx::add2(w[2], w[3]));
+        }
+        static_assert(kVecsPerLane == 4, "pairwise tree over four vectors");
+        const uint64_t acc = ptx::add2(ptx::add2(part[0], part[1]), ptx::add2(part[2], part[3]));
+        float a, b;
+        ptx::unpack2(acc, a, b);
+        return a + b;
+    }
 }
 
 // ----------------------------------------------------------------- params
@@ -528,7 +561,7 @@ __device__ int64_t sampler_owner_walk(const double* granules, int ngran, float w
         const float hm = -0.5f * static_cast<float>(M);
 #pragma unroll
         for (int i = 0; i < kFinPer; ++i) {
-            const float t = fminf(fmaf(walk[lane][i], 0.5f, hm) * scale2, 0.0f);
+            const float t = fminf(fmaf(walk[lane][i], 0.5f, hm) * scale2, kWalkClamp);
             const float w = ptx::ex2(t);
             lsum += ((bits >> i) & 1u) ? w : 0.0f;
         }
@@ -795,10 +828,8 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             float best = -kInf;
             int best_idx = -1;
             int first_valid_chunk = -1;
-            // sampler: a warp-uniform reference max `ref` that trails the running max of valid
-            // logits by less than 2^kSlack in weight (it is only raised when a chunk would exceed
-            // that), and the lane's exact running max.
-            float ref = -kInf, lane_max = -kInf;
+            // sampler: a warp-uniform reference max `ref` of the valid logits seen so far
+            float ref = -kInf;
             bool fast = false;  // weights as one FFMA from `ref` (see lane_mass, mode 0)
             float chi = 0.0f, corr = 1.0f;
             const float sc = p.scale;
@@ -903,8 +934,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     }
                     if (first_valid_chunk < 0 && anyb != 0u) first_valid_chunk = c;
                 } else {
-                    // Pass 1 over registers: NaN, count, masked values (-inf where invalid), chunk max.
-                    float lmax = -kInf;
+                    // Pass 1 over registers: NaN, count, masked values (-inf where invalid).
                     uint32_t anyb = 0u;
                     uint32_t q16[kVecsPerLane][4];
                     float q32[kVecsPerLane][kVec];
@@ -919,26 +949,26 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                             float v[kVec];
                             E::decode(raw[j], v);
 #pragma unroll
-                            for (int i = 0; i < kVec; ++i) {
-                                q32[j][i] = ((bits[j] >> i) & 1u) ? v[i] : -kInf;
-                                lmax = fmaxf(lmax, q32[j][i]);
-                            }
+                            for (int i = 0; i < kVec; ++i) q32[j][i] = ((bits[j] >> i) & 1u) ? v[i] : -kInf;
                         }
                     }
-                    if constexpr (E::kBytes == 2) {
-                        uint32_t t = E::max2(E::max2(E::max2(q16[0][0], q16[0][1]), E::max2(q16[0][2], q16[0][3])),
-                                             E::max2(E::max2(q16[1][0], q16[1][1]), E::max2(q16[1][2], q16[1][3])));
-                        t = E::max2(t, E::max2(E::max2(E::max2(q16[2][0], q16[2][1]), E::max2(q16[2][2], q16[2][3])),
-                                               E::max2(E::max2(q16[3][0], q16[3][1]), E::max2(q16[3][2], q16[3][3]))));
-                        lmax = fmaxf(E::lo(t), E::hi(t));
-                    }
-                    lane_max = fmaxf(lane_max, lmax);  // NaN valid logits are ignored here; they fail
-                                                       // the row through the NaN flag
-                    // Raise the reference only when needed: always while it is not usable for the
-                    // one-FFMA form, otherwise when some token would weigh more than 2^kSlack.
-                    const bool need = fast ? __any_sync(0xFFFFFFFFu, fmaf(lmax, sc, chi) > kSlack)
-                                           : __any_sync(0xFFFFFFFFu, anyb != 0u);
-                    if (need) {
+                    // Raise the warp's reference to the chunk's max of valid logits (NaN ignored:
+                    // it fails the row through the NaN flag) and re-derive the exponent form.
+                    auto raise = [&]() {
+                        float lmax;
+                        if constexpr (E::kBytes == 2) {
+                            uint32_t t = E::max2(E::max2(E::max2(q16[0][0], q16[0][1]), E::max2(q16[0][2], q16[0][3])),
+                                                 E::max2(E::max2(q16[1][0], q16[1][1]), E::max2(q16[1][2], q16[1][3])));
+                            t = E::max2(t, E::max2(E::max2(E::max2(q16[2][0], q16[2][1]), E::max2(q16[2][2], q16[2][3])),
+                                                   E::max2(E::max2(q16[3][0], q16[3][1]), E::max2(q16[3][2], q16[3][3]))));
+                            lmax = fmaxf(E::lo(t), E::hi(t));
+                        } else {
+                            lmax = -kInf;
+#pragma unroll
+                            for (int j = 0; j < kVecsPerLane; ++j)
+#pragma unroll
+                                for (int i = 0; i < kVec; ++i) lmax = fmaxf(lmax, q32[j][i]);
+                        }
                         const uint32_t lkey = (lmax == lmax) ? ordered_bits(lmax) : 0u;
                         const uint32_t wkey = __reduce_max_sync(0xFFFFFFFFu, lkey);
                         if (wkey != 0u) ref = fmaxf(ref, ordered_to_float(wkey));
@@ -950,24 +980,41 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         chi = -msc;
                         const float clo = fmaf(-ref, sc, -chi);
                         corr = fmaf(clo, 0.6931471805599453f, 1.0f);
-                    }
+                    };
                     // Pass 2: fp32 weights 2^((x - ref) * log2(e) / T), invalid tokens entering as
-                    // -inf (weight 0).
+                    // -inf (weight 0).  In the one-FFMA form the reference may trail the running
+                    // max: it is raised only when a lane's mass exceeds kRaiseMass = 2^20 (or is
+                    // +inf), so no weight exceeds 2^20.  Otherwise (no valid logit yet, a
+                    // tiny temperature or huge logits) it is raised to every chunk's max.
                     float mass = 0.0f;
+                    bool done = false, any_mass = false;
                     if (fast) {
-                        mass = lane_mass<E, 0>(q16, q32, chi, sc);
+                        mass = lane_mass_fast<E>(q16, q32, chi, sc);
+                        any_mass = true;
+                        if (__any_sync(0xFFFFFFFFu, mass > kRaiseMass)) raise();
+                        else done = true;
+                    } else if (__any_sync(0xFFFFFFFFu, anyb != 0u)) {
+                        raise();
+                        any_mass = true;
+                    }
+                    if (!done && any_mass) {
+                        if (fast) {
+                            mass = lane_mass_fast<E>(q16, q32, chi, sc);
+                        } else if (ref > -kInf && ref < kInf) {
+                            // ref is this chunk's max or above: x - ref <= 0, formed as
+                            // 0.5x - 0.5ref so that it cannot overflow, times scale2 = 2 log2(e) / T.
+                            const float nhm = -0.5f * ref;
+                            const float sc2 = p.scale2;
+                            if (sc2 < kInf) mass = lane_mass<E, 1>(q16, q32, nhm, sc2);
+                            else mass = lane_mass<E, 2>(q16, q32, nhm, sc2);
+                        } else {
+                            mass = 0.0f;
+                        }
+                    }
+                    if (any_mass) {
 #pragma unroll
                         for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
-                        mass *= corr;
-                    } else if (need && ref > -kInf && ref < kInf) {
-                        // Here ref is the exact running max: x - ref <= 0, formed as 0.5x - 0.5ref
-                        // so that it cannot overflow, times scale2 = 2 log2(e) / T.
-                        const float nhm = -0.5f * ref;
-                        const float sc2 = p.scale2;
-                        if (sc2 < kInf) mass = lane_mass<E, 1>(q16, q32, nhm, sc2);
-                        else mass = lane_mass<E, 2>(q16, q32, nhm, sc2);
-#pragma unroll
-                        for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
+                        if (fast) mass *= corr;
                     }
                     if (lane == 0) granules_f[c * kConsumerWarps + warp] = make_float2(ref, mass);
                 }
@@ -988,10 +1035,10 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             uint32_t wkey, wchunk = 0xFFFFFFFFu;
             double wmass = 0.0;
             if constexpr (kSample) {
-                // The warp's exact max of valid logits; fold its granules to it (one fp64 exp per
-                // lane per chunk) so that the finalizer combines 8 warp masses, not every granule.
-                wkey = __reduce_max_sync(0xFFFFFFFFu, ordered_bits(lane_max));
-                const double wm = static_cast<double>(ordered_to_float(wkey));
+                // Fold the warp's granules to its final reference (one fp64 exp per lane per chunk)
+                // so that the finalizer combines 8 warp masses, not every granule.
+                wkey = ordered_bits(ref);
+                const double wm = static_cast<double>(ref);
                 __syncwarp();
                 double local = 0.0;
                 for (int c = lane; c < nchunks; c += 32) {
