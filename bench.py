@@ -181,8 +181,8 @@ class Workload:
             import numpy as np
             densities = wl.SAMPLE_DENSITIES if args.sample_density is None else (args.sample_density,) * 8
             bits, masks, uniforms, temp = wl.sample_config_np(seed=2 + rank, densities=densities)
-            tile = max(1, args.sample_rows // bits.shape[0])
-            bits, masks = np.tile(bits, (tile, 1)), np.tile(masks, (tile, 1))
+            tile = max(1, -(-args.sample_rows // bits.shape[0]))
+            bits, masks = np.tile(bits, (tile, 1))[:args.sample_rows], np.tile(masks, (tile, 1))[:args.sample_rows]
             uniforms = np.random.default_rng(2 + rank).random(bits.shape[0])
             reps = max(1, int(2 * L2_BYTES // bits.nbytes) + 1)
             self.logits_all = torch.from_numpy(np.tile(bits, (reps, 1)).view(np.int16)).view(torch.float16).to(device)

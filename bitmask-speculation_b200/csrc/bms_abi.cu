@@ -159,6 +159,12 @@ int kernel_info(int device, KernelInfo*& out) {
     return BMS_SUCCESS;
 }
 
+int cluster_index(int c) {
+    for (int i = 0; i < 5; ++i)
+        if (kClusterSizes[i] == c) return i;
+    return 0;
+}
+
 struct Plan {
     int cluster;
     int clusters;
@@ -209,17 +215,25 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
                     kSample ? "sampler" : "selection");
     p.segment = plan.segment;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = plan.cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    // Programmatic dependent launch: CTAs may be dispatched and initialise their barriers while
+    // the previous grid in the stream drains (the kernel waits for it before touching memory).
+    // A launch without a cluster dimension is a grid of one-CTA clusters.
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = plan.cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.gridDim = dim3(static_cast<unsigned>(plan.cluster * plan.clusters));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
     cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    // Only a grid that fills every resident slot: a smaller one, dispatched early into the slots
+    // its predecessor leaves free, would be spread unevenly over the SMs.
+    const bool full = plan.clusters >= info->max_clusters[cluster_index(plan.cluster)];
+    cfg.attrs = full ? attr : attr + 1;
+    cfg.numAttrs = (full ? 1 : 0) + (plan.cluster > 1 ? 1 : 0);
     BMS_CUDA(cudaLaunchKernelEx(&cfg, select_rows_kernel<T, kSample, kBulk, kStages>, p), "selection launch");
     return BMS_SUCCESS;
 }
@@ -361,7 +375,7 @@ __global__ void __launch_bounds__(256) verify_epilogue_kernel(
 template <typename T, bool kSample>
 __global__ void __launch_bounds__(128) shard_merge_kernel(
     const GatherSlot* __restrict__ partials, int32_t shards, int32_t shard, int64_t rows, double temperature,
-    float scale2, const double* __restrict__ uniforms, const uint8_t* __restrict__ logits,
+    double inv, float scale2, const double* __restrict__ uniforms, const uint8_t* __restrict__ logits,
     const int32_t* __restrict__ masks, int64_t mask_words, int64_t vocab_shard, int64_t token_offset,
     const uint8_t* __restrict__ granules, int64_t granule_stride, int64_t* __restrict__ tokens,
     int64_t* __restrict__ counts, int32_t* __restrict__ status) {
@@ -385,7 +399,7 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
             }
         } else {
             const SampleMerge mg = merge_sampler_ranks(partials + row, rows, static_cast<uint32_t>(shards), uniforms[row],
-                                                       temperature, 0u);
+                                                       temperature, inv, 0u, lane);
             int64_t token = -1;
             int32_t code = mg.code;
             if (mg.code == kOk && mg.owner == shard) {
@@ -393,12 +407,15 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
                 const bool has = lane < kConsumerWarps;
                 const float wmax = has ? reinterpret_cast<const float*>(rec + SamplerRecord::kWarpMaxOffset)[lane] : 0.0f;
                 const double wmass = has ? reinterpret_cast<const double*>(rec + SamplerRecord::kWarpMassOffset)[lane] : 0.0;
+                // The shard's own max, as its finalizer used it for the warp factors.
+                const float seg_m = __uint_as_float(partials[static_cast<int64_t>(shard) * rows + row].a);
+                const double wf = (has && wmass > 0.0) ? warp_factor(wmax, seg_m, temperature, inv) : 0.0;
                 const int nchunks = static_cast<int>((vocab_shard + Layout<T>::kTokensPerChunk - 1) / Layout<T>::kTokensPerChunk);
                 const uint8_t* lrow = logits + static_cast<size_t>(row) * static_cast<size_t>(vocab_shard) * sizeof(T);
                 const int32_t* mrow = masks + static_cast<size_t>(row) * static_cast<size_t>(mask_words) + (token_offset >> 5);
                 const int64_t chosen = sampler_owner_walk<T>(
-                    reinterpret_cast<const double*>(rec + SamplerRecord::kGranuleOffset), nchunks * kConsumerWarps, wmax,
-                    wmass, has, mg, temperature, scale2, 0, vocab_shard, lrow, mrow, walk[wib], fac[wib], lane);
+                    reinterpret_cast<const double*>(rec + SamplerRecord::kGranuleOffset), nchunks * kConsumerWarps, wf,
+                    wmass, has, mg, temperature, inv, scale2, 0, vocab_shard, lrow, mrow, walk[wib], fac[wib], lane);
                 token = chosen >= 0 ? token_offset + chosen : -1;
                 if (chosen < 0) code = kNoMass;
             }
@@ -410,6 +427,12 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
             }
         }
     }
+}
+
+// 1 / T for the device's exponent arguments, or 0 where it is not finite (they then divide by T).
+double inverse_temperature(double temperature) {
+    const double inv = temperature > 0.0 ? 1.0 / temperature : 0.0;
+    return std::isfinite(inv) ? inv : 0.0;
 }
 
 float sampler_scale2(double temperature) {
@@ -536,6 +559,7 @@ int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* ma
     p.status = status;
     p.uniforms = uniforms;
     p.temperature = temperature;
+    p.inv_temperature = inverse_temperature(temperature);
     // 2*log2(e)/T in float; +inf for tiny T, clamped to the smallest denormal for huge T so
     // that -inf logits still map to zero weight.
     p.scale2 = sampler_scale2(temperature);
@@ -671,6 +695,7 @@ int bms_shard_partials(const void* logits, int32_t dtype, const int32_t* masks, 
     p.granule_out = static_cast<uint8_t*>(granules);
     p.granule_stride = granule_stride;
     p.temperature = temperature;
+    p.inv_temperature = inverse_temperature(temperature);
     p.scale2 = sampler_scale2(temperature);
     p.scale = static_cast<float>(1.4426950408889634 / temperature);
     return launch_select<true>(dtype, p, device, static_cast<cudaStream_t>(stream));
@@ -712,22 +737,23 @@ int bms_shard_merge(const bms_partial* partials, int32_t shards, int32_t shard, 
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const GatherSlot* parts = reinterpret_cast<const GatherSlot*>(partials);
     const float sc2 = sample ? sampler_scale2(temperature) : 0.0f;
+    const double inv = inverse_temperature(temperature);
     const uint8_t* lg = static_cast<const uint8_t*>(logits);
     const uint8_t* gr = static_cast<const uint8_t*>(granules);
     if (!sample) {
-        shard_merge_kernel<float, false><<<grid, 128, 0, s>>>(parts, shards, shard, rows, 0.0, 0.0f, nullptr, nullptr,
+        shard_merge_kernel<float, false><<<grid, 128, 0, s>>>(parts, shards, shard, rows, 0.0, 0.0, 0.0f, nullptr, nullptr,
                                                               nullptr, 0, 0, 0, nullptr, 0, tokens, counts, status);
     } else if (dtype == BMS_FLOAT32) {
-        shard_merge_kernel<float, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, sc2, uniforms, lg,
+        shard_merge_kernel<float, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, inv, sc2, uniforms, lg,
                                                              masks, mask_words, vocab_shard, token_offset, gr,
                                                              granule_stride, tokens, counts, status);
     } else if (dtype == BMS_BFLOAT16) {
-        shard_merge_kernel<__nv_bfloat16, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, sc2,
+        shard_merge_kernel<__nv_bfloat16, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, inv, sc2,
                                                                      uniforms, lg, masks, mask_words, vocab_shard,
                                                                      token_offset, gr, granule_stride, tokens, counts,
                                                                      status);
     } else {
-        shard_merge_kernel<__half, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, sc2, uniforms, lg,
+        shard_merge_kernel<__half, true><<<grid, 128, 0, s>>>(parts, shards, shard, rows, temperature, inv, sc2, uniforms, lg,
                                                               masks, mask_words, vocab_shard, token_offset, gr,
                                                               granule_stride, tokens, counts, status);
     }

@@ -272,6 +272,7 @@ struct SelectParams {
     // sampler
     const double* uniforms;  // [rows]
     double temperature;
+    double inv_temperature;  // 1 / T where finite, else 0 (exponents then divide by T)
     float scale2;            // 2 * log2(e) / T as float, clamped to >= the smallest denormal
     float scale;             // log2(e) / T as float (inf for tiny T)
     // vocabulary shards
@@ -374,8 +375,14 @@ __device__ __forceinline__ double warp_sum(double v) {
 }
 
 // exp((x - M) / T) for a valid, finite-or(-inf) logit; the reference's weight.
-__device__ __forceinline__ double exact_weight(float x, double M, double T) {
-    return x > -__int_as_float(0x7F800000) ? exp((static_cast<double>(x) - M) / T) : 0.0;
+// exp(d / T) (d below about 14 T: references trail maxima by at most 2^20 in weight), multiplying by 1 / T where that is finite (inv > 0) and dividing
+// otherwise (denormal temperatures).
+__device__ __forceinline__ double scaled_exp(double d, double temp, double inv) {
+    return inv > 0.0 ? exp(d * inv) : exp(d / temp);
+}
+
+__device__ __forceinline__ double exact_weight(float x, double M, double T, double inv) {
+    return x > -__int_as_float(0x7F800000) ? scaled_exp(static_cast<double>(x) - M, T, inv) : 0.0;
 }
 
 
@@ -440,20 +447,23 @@ struct SampleMerge {
     int owner;      // rank holding the first crossing of u * total (or the last positive rank)
     bool fallback;  // rounding left u * total past the last positive mass
     double M, cutoff, prefix;
+    double rank_fac;  // the owner's mass factor exp((owner max - M) / T)
 };
 
+// Warp-cooperative (all 32 lanes call it, n <= 32): lane q holds rank q.  Rank masses are
+// rescaled to the row max in parallel (a rank already at the max keeps its mass exactly), then
+// located by a warp scan in rank order.
 __device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, int64_t stride, uint32_t n, double u,
-                                                           double temp, uint32_t extra_flags) {
+                                                           double temp, double inv, uint32_t extra_flags, int lane) {
     const float kInf = __int_as_float(0x7F800000);
     SampleMerge r;
-    float rm = -kInf;
-    uint32_t total = 0, fl = extra_flags;
-    for (uint32_t q = 0; q < n; ++q) {
-        const GatherSlot& e = g[q * stride];
-        rm = fmaxf(rm, __uint_as_float(e.a));
-        total += e.b;
-        fl |= e.c;
-    }
+    const bool in = static_cast<uint32_t>(lane) < n;
+    GatherSlot e{0u, 0u, 0u, 0u, 0.0, 0.0};
+    if (in) e = g[static_cast<int64_t>(lane) * stride];
+    const float a = in ? __uint_as_float(e.a) : -kInf;
+    const float rm = ordered_to_float(__reduce_max_sync(0xFFFFFFFFu, ordered_bits(a)));
+    const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, e.b);
+    const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, e.c) | extra_flags;
     r.total = total;
     r.code = (fl & kFlagAbort) ? kTimeout
              : (fl & kFlagNaN) ? kNaN
@@ -467,42 +477,48 @@ __device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, 
     r.fallback = false;
     r.cutoff = 0.0;
     r.prefix = 0.0;
+    r.rank_fac = 1.0;
     if (r.code != kOk) return r;
-    double total_mass = 0.0;
-    for (uint32_t q = 0; q < n; ++q) {
-        const GatherSlot& e = g[q * stride];
-        if (e.s > 0.0) total_mass += e.s * exp((static_cast<double>(__uint_as_float(e.a)) - r.M) / temp);
-    }
-    r.cutoff = u * total_mass;
-    int last_pos = -1;
-    double run = 0.0, last_prefix = 0.0;
-    for (uint32_t q = 0; q < n; ++q) {
-        const GatherSlot& e = g[q * stride];
-        const double m = e.s > 0.0 ? e.s * exp((static_cast<double>(__uint_as_float(e.a)) - r.M) / temp) : 0.0;
-        if (!(m > 0.0)) continue;
-        last_pos = static_cast<int>(q);
-        last_prefix = run;
-        if (r.owner < 0 && r.cutoff < run + m) {
-            r.owner = static_cast<int>(q);
-            r.prefix = run;
-        }
-        run += m;
-    }
-    if (r.owner < 0) {
+    const bool pos_in = in && e.s > 0.0;
+    const double f = pos_in ? (a == rm ? 1.0 : scaled_exp(static_cast<double>(a) - static_cast<double>(rm), temp, inv))
+                            : 0.0;
+    const double m = pos_in ? e.s * f : 0.0;
+    const double incl = warp_inclusive_scan(m, lane);
+    const double up = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+    const double before = lane > 0 ? up : 0.0;
+    r.cutoff = u * __shfl_sync(0xFFFFFFFFu, incl, 31);
+    const uint32_t positive = __ballot_sync(0xFFFFFFFFu, m > 0.0);
+    const uint32_t hits = __ballot_sync(0xFFFFFFFFu, m > 0.0 && r.cutoff < incl);
+    int owner;
+    if (hits) {
+        owner = __ffs(hits) - 1;
+    } else {
         r.fallback = true;
-        r.owner = last_pos;
-        r.prefix = last_prefix;
+        owner = positive ? 31 - __clz(positive) : -1;
+    }
+    r.owner = owner;
+    const double pre = __shfl_sync(0xFFFFFFFFu, before, owner < 0 ? 0 : owner);
+    const double rf = __shfl_sync(0xFFFFFFFFu, f, owner < 0 ? 0 : owner);
+    if (owner >= 0) {
+        r.prefix = pre;
+        r.rank_fac = rf;
     }
     return r;
 }
 
+// Factor taking a warp's mass from its reference max to its rank's max (1 when equal).
+__device__ __forceinline__ double warp_factor(float wmax, float seg_m, double temp, double inv) {
+    return wmax == seg_m ? 1.0 : scaled_exp(static_cast<double>(wmax) - static_cast<double>(seg_m), temp, inv);
+}
+
 // The owning rank's walk (one warp): find the granule holding the crossing from the granule
-// masses (each relative to its warp's max, `fac` rescales to the row max), then the lane of that
-// granule with fp32 weights, then the token with the reference's exact fp64 weights.  Lane w < 8
-// passes its warp's (max, mass).  Returns the token's index within the row (-1 if none).
+// masses (each relative to its warp's reference max; `fac` = warp factor x rank factor rescales
+// them to the row max), then the lane of that granule with fp32 weights, then the token with the
+// reference's exact fp64 weights.  Lane w < 8 passes its warp's factor to the rank max
+// (warp_factor) and mass.  Returns the token's index within the row (-1 if none).
 template <typename T>
-__device__ int64_t sampler_owner_walk(const double* granules, int ngran, float wmax, double wmass, bool has_warp,
-                                      const SampleMerge& mg, double temp, float scale2, int64_t seg_begin,
+__device__ int64_t sampler_owner_walk(const double* granules, int ngran, double wfac, double wmass, bool has_warp,
+                                      const SampleMerge& mg, double temp, double inv, float scale2, int64_t seg_begin,
                                       int64_t seg_end, const uint8_t* lrow, const int32_t* mrow, float (*walk)[33],
                                       double* fac, int lane) {
     using E = Elem<T>;
@@ -511,7 +527,7 @@ __device__ int64_t sampler_owner_walk(const double* granules, int ngran, float w
     constexpr int kFinPer = kTPW / 32;
     const double M = mg.M, cutoff = mg.cutoff, prefix = mg.prefix;
     const bool fallback = mg.fallback;
-    if (has_warp) fac[lane] = wmass > 0.0 ? exp((static_cast<double>(wmax) - M) / temp) : 0.0;
+    if (has_warp) fac[lane] = wmass > 0.0 ? wfac * mg.rank_fac : 0.0;
     __syncwarp();
     const int per = (ngran + 31) / 32;
     const int g0 = lane * per, g1 = min(g0 + per, ngran);
@@ -578,7 +594,7 @@ __device__ int64_t sampler_owner_walk(const double* granules, int ngran, float w
     const uint32_t bitsL = __shfl_sync(0xFFFFFFFFu, bits, L);
     const double prefixL = gprefix + __shfl_sync(0xFFFFFFFFu, lincl - lsum_d, L);
     const bool mine = lane < kFinPer && ((bitsL >> lane) & 1u);
-    const double w = mine ? exact_weight(walk[L][lane < kFinPer ? lane : 0], M, temp) : 0.0;
+    const double w = mine ? exact_weight(walk[L][lane < kFinPer ? lane : 0], M, temp, inv) : 0.0;
     const double winc = warp_inclusive_scan(w, lane);
     const uint32_t hits = __ballot_sync(0xFFFFFFFFu, !lane_fallback && w > 0.0 && cutoff < prefixL + winc);
     const uint32_t pos = __ballot_sync(0xFFFFFFFFu, w > 0.0);
@@ -644,12 +660,17 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
         ptx::fence_mbarrier_init();
     }
     __syncthreads();
-    // A programmatic dependent (the verification epilogue) may start launching now; it waits
-    // for this grid's completion before reading any output.
+    // Launched as a programmatic dependent, this grid may have started while the previous grid in
+    // the stream was still running: no global memory is touched before that grid completed.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // A programmatic dependent (the verification epilogue, the next selection launch) may start
+    // launching now; it waits for this grid's completion before touching global memory.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Every CTA of the cluster has initialised its barriers before any remote arrive.
-    ptx::cluster_arrive();
-    ptx::cluster_wait();
+    if (csize > 1) {
+        ptx::cluster_arrive();
+        ptx::cluster_wait();
+    }
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer warp
@@ -758,9 +779,10 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 const float seg_m = ckey ? ordered_to_float(ckey) : -kInf;
                 const bool seg_finite = seg_m > -kInf && seg_m < kInf;
                 const float wmax = in ? ordered_to_float(wp.key) : -kInf;
-                const double term = (seg_finite && in && wp.mass > 0.0)
-                                        ? wp.mass * exp((static_cast<double>(wmax) - static_cast<double>(seg_m)) / p.temperature)
-                                        : 0.0;
+                const double wf = (seg_finite && in && wp.mass > 0.0)
+                                      ? warp_factor(wmax, seg_m, p.temperature, p.inv_temperature)
+                                      : 0.0;
+                const double term = wp.mass * wf;
                 const double seg_s = warp_sum(term);
                 if (p.partials != nullptr) {
                     // Vocabulary shard: the row's partial and granule record are the output.
@@ -781,7 +803,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     }
                     __syncwarp();
                     const SampleMerge mg = merge_sampler_ranks(sh.slots[slot], 1, csize, p.uniforms[row], p.temperature,
-                                                               sh.abort ? kFlagAbort : 0u);
+                                                               p.inv_temperature, sh.abort ? kFlagAbort : 0u, lane);
                     if (mg.code != kOk) {
                         if (crank == 0 && lane == 0) {
                             p.status[row] = mg.code;
@@ -790,8 +812,9 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         }
                     } else if (mg.owner == static_cast<int>(crank)) {
                         const int64_t chosen =
-                            sampler_owner_walk<T>(granules, ngran, wmax, wp.mass, in, mg, p.temperature, p.scale2,
-                                                  seg_begin, seg_end, lrow, mrow, ss.walk, ss.fac, lane);
+                            sampler_owner_walk<T>(granules, ngran, wf, wp.mass, in, mg, p.temperature,
+                                                  p.inv_temperature, p.scale2, seg_begin, seg_end, lrow, mrow, ss.walk,
+                                                  ss.fac, lane);
                         if (lane == 0) {
                             p.status[row] = chosen >= 0 ? kOk : kNoMass;
                             p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
@@ -889,6 +912,13 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         bits[j] = (word >> ((vec * kVec) & 31)) & kVecMask;
                     }
                 }
+                // A full chunk's valid tokens are counted on whole mask words (one word per lane),
+                // a ragged last chunk's per vector.
+                uint32_t cword = 0u;
+                if constexpr (kFull) {
+                    constexpr int kWords = kTPW / 32;
+                    if (kWords >= 32 || lane < kWords) cword = smask[warp * kWords + lane];
+                }
                 // Stage contents are in registers: release it to the producer.
                 if constexpr (kBulk) {
                     __syncwarp();
@@ -896,6 +926,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 } else {
                     ptx::named_sync(1, kConsumerThreads);  // stage 0 reusable
                 }
+                if constexpr (kFull) count += __popc(cword);
 
                 if constexpr (!kSample) {
                     // Masked max of the lane's tokens in this chunk (invalid tokens = -inf).  Only
@@ -908,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
 #pragma unroll
                         for (int j = 0; j < kVecsPerLane; ++j) {
                             E::nan_update(nan_acc, raw[j]);
-                            count += __popc(bits[j]);
+                            if constexpr (!kFull) count += __popc(bits[j]);
                             anyb |= bits[j];
                             uint32_t q[4];
                             mask_pairs<E>(raw[j], bits[j], q);
@@ -920,7 +951,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
 #pragma unroll
                         for (int j = 0; j < kVecsPerLane; ++j) {
                             E::nan_update(nan_acc, raw[j]);
-                            count += __popc(bits[j]);
+                            if constexpr (!kFull) count += __popc(bits[j]);
                             anyb |= bits[j];
                             float v[kVec];
                             E::decode(raw[j], v);
@@ -941,7 +972,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
 #pragma unroll
                     for (int j = 0; j < kVecsPerLane; ++j) {
                         E::nan_update(nan_acc, raw[j]);
-                        count += __popc(bits[j]);
+                        if constexpr (!kFull) count += __popc(bits[j]);
                         anyb |= bits[j];
                         if constexpr (E::kBytes == 2) {
                             mask_pairs<E>(raw[j], bits[j], q16[j]);
@@ -1043,8 +1074,10 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 double local = 0.0;
                 for (int c = lane; c < nchunks; c += 32) {
                     const float2 e = granules_f[c * kConsumerWarps + warp];
-                    const double gm =
-                        e.y > 0.0f ? static_cast<double>(e.y) * exp((static_cast<double>(e.x) - wm) / p.temperature) : 0.0;
+                    const double gm = !(e.y > 0.0f) ? 0.0
+                                      : e.x == ref  ? static_cast<double>(e.y)
+                                                    : static_cast<double>(e.y) *
+                                                          scaled_exp(static_cast<double>(e.x) - wm, p.temperature, p.inv_temperature);
                     granules[c * kConsumerWarps + warp] = gm;
                     local += gm;
                 }
@@ -1064,9 +1097,11 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     }
 
     // No CTA may exit while a peer can still write into its shared memory.
-    __syncthreads();
-    ptx::cluster_arrive();
-    ptx::cluster_wait();
+    if (csize > 1) {
+        __syncthreads();
+        ptx::cluster_arrive();
+        ptx::cluster_wait();
+    }
 }
 
 // Shared-memory bytes the kernel needs (stages + control block + sampler tables).
