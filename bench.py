@@ -58,6 +58,8 @@ def parse_args():
                     help="override every sampling row's mask density (default: the configuration's mix)")
     ap.add_argument("--sample-dtype", choices=["float16", "bfloat16"], default="float16",
                     help="logits type of the sampling workload (the configuration's rows are fp16)")
+    ap.add_argument("--no-workspace", action="store_true",
+                    help="run the selection kernels on their fixed schedule (no dynamic-schedule workspace)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--roofline-seconds", type=float, default=1.5)
@@ -229,6 +231,21 @@ class Workload:
             return self.logits.shape[1] * self.esize + (self.logits.shape[1] // 32) * 4 + 20
         return self.vocab * self.esize + self.words * 4 + 20
 
+    @property
+    def dtype_code(self):
+        return {"f32": 0, "bf16": 1, "f16": 2}[self.dtype]
+
+    def workspace(self):
+        """(pointer, bytes) of the dynamic-schedule workspace, or (None, 0) with --no-workspace."""
+        if self.args.no_workspace:
+            return None, 0
+        if getattr(self, "_ws", None) is None:
+            import torch
+            from bitmask_speculation_b200 import _native
+            nbytes = int(_native.library().bms_workspace_bytes(self.device.index))
+            self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        return self._ws.data_ptr(), self._ws.numel()
+
     def _alloc_outputs(self):
         import torch
         d = self.device
@@ -269,7 +286,7 @@ class Workload:
                 self.lengths.data_ptr(), ctypes.byref(self.policy), self.row_tokens.data_ptr(),
                 self.row_counts.data_ptr(), self.row_status.data_ptr(), self.row_budget.data_ptr(),
                 self.accept.data_ptr(), self.token.data_ptr(), self.kindout.data_ptr(),
-                self.seq_status.data_ptr(), dev, stream_handle)
+                self.seq_status.data_ptr(), *self.workspace(), dev, stream_handle)
         elif self.kind == "vocab":
             from bitmask_speculation_b200.sharding import vocab_sharded_select
             self.row_tokens, self.row_counts, self.row_status = vocab_sharded_select(logits, masks, self.vocab)
@@ -278,14 +295,14 @@ class Workload:
             b = (self.step_index - 1) % self.batches
             u = self.uniforms_all[b * self.rows:(b + 1) * self.rows]
             rc = lib.bms_masked_sample_batch(
-                logits.data_ptr(), 2, masks.data_ptr(), self.rows, self.vocab, self.temperature, u.data_ptr(),
-                self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(), dev,
-                stream_handle)
+                logits.data_ptr(), self.dtype_code, masks.data_ptr(), self.rows, self.vocab, self.temperature,
+                u.data_ptr(), self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
+                *self.workspace(), dev, stream_handle)
         else:
-            code = 0 if self.kind == "argmax" else 1
             rc = lib.bms_masked_reduce_batch(
-                logits.data_ptr(), code, masks.data_ptr(), self.rows, self.vocab, self.row_tokens.data_ptr(),
-                self.row_counts.data_ptr(), self.row_status.data_ptr(), dev, stream_handle)
+                logits.data_ptr(), self.dtype_code, masks.data_ptr(), self.rows, self.vocab,
+                self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
+                *self.workspace(), dev, stream_handle)
         _native.check(rc)
 
     def kernel_only(self, stream_handle):
@@ -298,18 +315,18 @@ class Workload:
             b = (self.step_index - 1) % self.batches
             u = self.uniforms_all[b * self.rows:(b + 1) * self.rows]
             rc = lib.bms_masked_sample_batch(
-                logits.data_ptr(), 2, masks.data_ptr(), self.rows, self.vocab, self.temperature, u.data_ptr(),
-                self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
-                self.device.index, stream_handle)
+                logits.data_ptr(), self.dtype_code, masks.data_ptr(), self.rows, self.vocab, self.temperature,
+                u.data_ptr(), self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
+                *self.workspace(), self.device.index, stream_handle)
         elif self.kind == "vocab":
             from bitmask_speculation_b200.sharding import NativeShardBackend
             self._parts = NativeShardBackend().partials(logits, masks, self._offset(), 0.0)
             return
         else:
-            code = {"f32": 0, "bf16": 1, "f16": 2}[self.dtype]
             rc = lib.bms_masked_reduce_batch(
-                logits.data_ptr(), code, masks.data_ptr(), self.rows, self.vocab, self.row_tokens.data_ptr(),
-                self.row_counts.data_ptr(), self.row_status.data_ptr(), self.device.index, stream_handle)
+                logits.data_ptr(), self.dtype_code, masks.data_ptr(), self.rows, self.vocab,
+                self.row_tokens.data_ptr(), self.row_counts.data_ptr(), self.row_status.data_ptr(),
+                *self.workspace(), self.device.index, stream_handle)
         _native.check(rc)
 
     def _offset(self):

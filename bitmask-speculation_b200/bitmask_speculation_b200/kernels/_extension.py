@@ -113,6 +113,27 @@ class NativeModule:
 
     def __init__(self):
         self._lib = _native.library()
+        self._workspaces = {}
+        #: pass a workspace to the batched kernels (dynamic schedule); False selects the fixed one
+        self.use_workspace = True
+
+    def workspace(self, device):
+        """The zeroed workspace of (device, current stream), allocated on first use.
+
+        A workspace serves one stream: calls on one stream never overlap, and each call leaves
+        it ready for the next.  Returns (pointer, bytes), or (None, 0) when disabled.
+        """
+        if not self.use_workspace:
+            return None, 0
+        key = (device.index, _stream(device))
+        ws = self._workspaces.get(key)
+        if ws is None:
+            nbytes = int(self._lib.bms_workspace_bytes(device.index))
+            if nbytes <= 0:
+                raise RuntimeError(f"no workspace size for device {device}")
+            ws = _torch().zeros(nbytes, dtype=_torch().uint8, device=device)
+            self._workspaces[key] = ws
+        return ws.data_ptr(), ws.numel()
 
     # -- reference surface ---------------------------------------------------
     def runtime_version(self) -> int:
@@ -149,9 +170,10 @@ class NativeModule:
         counts = torch.empty(rows, dtype=torch.int64, device=dev)
         status = torch.empty(rows, dtype=torch.int32, device=dev)
         if rows:
+            ws, nbytes = self.workspace(dev)
             _native.check(self._lib.bms_masked_reduce_batch(
                 logits.data_ptr(), _dtype_code(logits), masks.data_ptr(), rows, vocab,
-                tokens.data_ptr(), counts.data_ptr(), status.data_ptr(), dev.index, _stream(dev)))
+                tokens.data_ptr(), counts.data_ptr(), status.data_ptr(), ws, nbytes, dev.index, _stream(dev)))
         return [tokens, counts, status]
 
     def masked_sample(self, logits, mask, temperature, uniform):
@@ -181,10 +203,11 @@ class NativeModule:
         if temperature != 0:
             _check_uniform(uniforms, dev, rows)
         if rows:
+            ws, nbytes = self.workspace(dev)
             _native.check(self._lib.bms_masked_sample_batch(
                 logits.data_ptr(), _dtype_code(logits), masks.data_ptr(), rows, vocab, temperature,
                 uniforms.data_ptr() if temperature != 0 else None, tokens.data_ptr(),
-                counts.data_ptr(), status.data_ptr(), dev.index, _stream(dev)))
+                counts.data_ptr(), status.data_ptr(), ws, nbytes, dev.index, _stream(dev)))
         return [tokens, counts, status]
 
     def mask_budget(self, masks, vocab: int, policy):
@@ -233,13 +256,14 @@ class NativeModule:
             seq_status=torch.empty(seqs, dtype=torch.int32, device=dev),
         )
         if seqs:
+            ws, nbytes = self.workspace(dev)
             _native.check(self._lib.bms_verify_batch(
                 logits.data_ptr(), _dtype_code(logits), masks.data_ptr(), seqs, k + 1, vocab,
                 proposals.data_ptr() if k else None, lengths.data_ptr(), ctypes.byref(policy),
                 out["row_tokens"].data_ptr(), out["row_counts"].data_ptr(),
                 out["row_status"].data_ptr(), out["row_budget"].data_ptr(),
                 out["accept_len"].data_ptr(), out["token"].data_ptr(), out["kind"].data_ptr(),
-                out["seq_status"].data_ptr(), dev.index, _stream(dev)))
+                out["seq_status"].data_ptr(), ws, nbytes, dev.index, _stream(dev)))
         return out
 
 

@@ -12,6 +12,7 @@
 //    few rows -> up to 16 CTAs per row merging through distributed shared memory.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -204,10 +205,68 @@ Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens
     return best;
 }
 
+std::atomic<uint32_t> g_epoch{0};
+
+// Dynamic schedule (a workspace is given, at least 1.5x as many rows as resident one-CTA
+// clusters, rows of at most kWsChunks chunks, no forced cluster size): one-CTA clusters fill
+// every resident slot and take tickets -- whole rows first, then quarter-row blocks of the last
+// rows (half as many as CTAs), whose pieces are merged through the workspace; the blocks absorb
+// the spread of the CTAs' finishing times.  Smaller batches keep the fixed schedule: measured on
+// B200 at V = 248,320 (256 to 1,500 rows), splitting them gained no bandwidth for the argmax and
+// less than the merges cost for the sampler, while 2,304 rows gained 1-3%.  With a forced CTA
+// count (test hook) every batch takes this path, split rows included.
+template <typename T, bool kSample, bool kBulk, int kStages>
+bool launch_dynamic(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t& cfg) {
+    constexpr int kTPC = Layout<T>::kTokensPerChunk;
+    const int64_t n = (p.vocab + kTPC - 1) / kTPC;
+    if (p.ws == nullptr || p.partials != nullptr || g_force_cluster != 0 || n > kWsChunks) return false;
+    int64_t grid = info.max_clusters[0];
+    if (g_force_clusters > 0 && g_force_clusters < grid) grid = g_force_clusters;
+    else if (2 * p.rows < 3 * grid) return false;
+    int64_t split, block;
+    if (p.rows <= grid) {
+        split = p.rows;
+        block = (split * n + grid - 1) / grid;
+    } else {
+        split = grid / 2 > 1 ? grid / 2 : 1;
+        block = (n + 3) / 4;
+    }
+    if (split > p.ws_rows) split = p.ws_rows;
+    block = block < 4 ? 4 : block > kWsChunks ? kWsChunks : block;
+    const int64_t split_chunks = split * n;
+    p.whole_rows = p.rows - split;
+    p.block = static_cast<int32_t>(block);
+    p.tickets = p.whole_rows + (split_chunks + block - 1) / block;
+    p.segment = (p.vocab + 31) / 32 * 32;
+    uint32_t e = ++g_epoch;
+    if (e == 0) e = ++g_epoch;
+    p.epoch = e;
+    const int64_t ctas = p.tickets < grid ? p.tickets : grid;
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+    return true;
+}
+
 template <typename T, bool kSample, bool kBulk, int kStages>
 int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     KernelInfo* info = nullptr;
     BMS_CHECK((kernel_info<T, kSample, kBulk, kStages>(device, info)));
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    {
+        cudaLaunchConfig_t cfg = {};
+        if (launch_dynamic<T, kSample, kBulk, kStages>(p, *info, cfg)) {
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
+            cfg.stream = stream;
+            const bool full = static_cast<int>(cfg.gridDim.x) >= info->max_clusters[0];
+            cfg.attrs = pdl;
+            cfg.numAttrs = full ? 1 : 0;
+            BMS_CUDA(cudaLaunchKernelEx(&cfg, select_rows_kernel<T, kSample, kBulk, kStages>, p), "selection launch");
+            return BMS_SUCCESS;
+        }
+        p.ws = nullptr;
+    }
     const Plan plan = plan_launch(*info, p.rows, p.vocab, Layout<T>::kTokensPerChunk, kSample ? kMaxChunksSampler : 0,
                                   kSample, p.partials != nullptr);
     if (plan.cluster == 0)
@@ -479,6 +538,23 @@ int select_common(int dtype, const void* logits, const int32_t* masks, int64_t r
     return BMS_SUCCESS;
 }
 
+// Split-row capacity of a device's workspace: one split row per resident CTA at most.
+int64_t workspace_rows(int device) { return 4ll * sm_count(device); }
+
+int attach_workspace(SelectParams& p, void* ws, int64_t bytes, int device) {
+    if (ws == nullptr) return BMS_SUCCESS;
+    const int64_t need = ws_bytes(workspace_rows(device));
+    if (bytes < need)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "workspace of %lld bytes is smaller than bms_workspace_bytes() = %lld",
+                    static_cast<long long>(bytes), static_cast<long long>(need));
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+    BMS_CHECK(check_ptr(ws, device, "workspace", 256));
+    p.ws = static_cast<uint8_t*>(ws);
+    p.ws_rows = workspace_rows(device);
+    return BMS_SUCCESS;
+}
+
 SelectParams base_params(const void* logits, const int32_t* masks, int64_t rows, int64_t vocab) {
     SelectParams p = {};
     p.logits = logits;
@@ -517,8 +593,14 @@ int bms_set_launch_override(int32_t cluster, int32_t clusters) {
     return BMS_SUCCESS;
 }
 
+int64_t bms_workspace_bytes(int32_t device) {
+    if (check_device(device) != BMS_SUCCESS) return -1;
+    return ws_bytes(workspace_rows(device));
+}
+
 int bms_masked_reduce_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t rows, int64_t vocab,
-                            int64_t* tokens, int64_t* counts, int32_t* status, int32_t device, void* stream) {
+                            int64_t* tokens, int64_t* counts, int32_t* status, void* workspace,
+                            int64_t workspace_bytes, int32_t device, void* stream) {
     BMS_CHECK(select_common(dtype, logits, masks, rows, vocab, device));
     if (rows == 0) return BMS_SUCCESS;
     BMS_CHECK(check_ptr(tokens, device, "tokens", 8));
@@ -527,6 +609,7 @@ int bms_masked_reduce_batch(const void* logits, int32_t dtype, const int32_t* ma
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
     SelectParams p = base_params(logits, masks, rows, vocab);
+    BMS_CHECK(attach_workspace(p, workspace, workspace_bytes, device));
     p.tokens = tokens;
     p.counts = counts;
     p.status = status;
@@ -535,16 +618,17 @@ int bms_masked_reduce_batch(const void* logits, int32_t dtype, const int32_t* ma
 
 int bms_masked_argmax(const void* logits, int32_t dtype, const int32_t* mask, int64_t vocab, int64_t* token,
                       int32_t* status, int32_t device, void* stream) {
-    return bms_masked_reduce_batch(logits, dtype, mask, 1, vocab, token, nullptr, status, device, stream);
+    return bms_masked_reduce_batch(logits, dtype, mask, 1, vocab, token, nullptr, status, nullptr, 0, device, stream);
 }
 
 int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t rows, int64_t vocab,
                             double temperature, const double* uniforms, int64_t* tokens, int64_t* counts,
-                            int32_t* status, int32_t device, void* stream) {
+                            int32_t* status, void* workspace, int64_t workspace_bytes, int32_t device, void* stream) {
     if (!std::isfinite(temperature) || temperature < 0)
         return fail(BMS_ERROR_INVALID_ARGUMENT, "temperature must be finite and nonnegative");
     if (temperature == 0)  // csrc/sample.cu:120: zero temperature is the masked argmax
-        return bms_masked_reduce_batch(logits, dtype, masks, rows, vocab, tokens, counts, status, device, stream);
+        return bms_masked_reduce_batch(logits, dtype, masks, rows, vocab, tokens, counts, status, workspace,
+                                       workspace_bytes, device, stream);
     BMS_CHECK(select_common(dtype, logits, masks, rows, vocab, device));
     if (rows == 0) return BMS_SUCCESS;
     BMS_CHECK(check_ptr(uniforms, device, "uniforms", 8));
@@ -554,6 +638,7 @@ int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* ma
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
     SelectParams p = base_params(logits, masks, rows, vocab);
+    BMS_CHECK(attach_workspace(p, workspace, workspace_bytes, device));
     p.tokens = tokens;
     p.counts = counts;
     p.status = status;
@@ -569,8 +654,8 @@ int bms_masked_sample_batch(const void* logits, int32_t dtype, const int32_t* ma
 
 int bms_masked_sample(const void* logits, int32_t dtype, const int32_t* mask, int64_t vocab, double temperature,
                       const double* uniform, int64_t* token, int32_t* status, int32_t device, void* stream) {
-    return bms_masked_sample_batch(logits, dtype, mask, 1, vocab, temperature, uniform, token, nullptr, status, device,
-                                   stream);
+    return bms_masked_sample_batch(logits, dtype, mask, 1, vocab, temperature, uniform, token, nullptr, status, nullptr,
+                                   0, device, stream);
 }
 
 int bms_mask_budget(const int32_t* masks, int64_t rows, int64_t vocab, const bms_policy* policy, int64_t* counts,
@@ -605,8 +690,8 @@ int bms_mask_count(const int32_t* mask, int64_t vocab, int64_t* count, int32_t d
 int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t seqs, int64_t rows_per_seq,
                      int64_t vocab, const int64_t* proposals, const int32_t* lengths, const bms_policy* policy,
                      int64_t* row_tokens, int64_t* row_counts, int32_t* row_status, int32_t* row_budget,
-                     int32_t* accept_len, int64_t* token, int32_t* kind, int32_t* seq_status, int32_t device,
-                     void* stream) {
+                     int32_t* accept_len, int64_t* token, int32_t* kind, int32_t* seq_status, void* workspace,
+                     int64_t workspace_bytes, int32_t device, void* stream) {
     if (seqs < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "seqs must be nonnegative");
     if (rows_per_seq < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows_per_seq must be at least 1");
     if (seqs > INT64_MAX / rows_per_seq) return fail(BMS_ERROR_INVALID_ARGUMENT, "batch too large");
@@ -632,6 +717,7 @@ int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, in
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
     SelectParams p = base_params(logits, masks, rows, vocab);
+    BMS_CHECK(attach_workspace(p, workspace, workspace_bytes, device));
     p.tokens = row_tokens;
     p.counts = row_counts;
     p.status = row_status;

@@ -18,6 +18,23 @@ __device__ __forceinline__ uint64_t globaltimer() {
     return t;
 }
 
+// Device-scope fetch-and-add with acquire-release ordering: writes that happen before it (in
+// this thread, or in threads that synchronised with it) are visible to whoever observes its
+// result, and what the observer reads afterwards sees theirs.
+__device__ __forceinline__ uint64_t atom_add_acq_rel_gpu(unsigned long long* p, uint64_t v) {
+    uint64_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+
+// 16-byte global -> shared copy through L2 (no registers); cp_async_wait_all completes this
+// thread's copies.
+__device__ __forceinline__ void cp_async_16(uint32_t smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---- mbarrier ---------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

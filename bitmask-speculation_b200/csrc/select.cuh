@@ -280,6 +280,13 @@ struct SelectParams {
     GatherSlot* partials;      // non-null: write one partial record per row instead of the outputs
     uint8_t* granule_out;      // sampler partials: per-row granule record (SamplerRecord layout)
     int64_t granule_stride;    // bytes between granule records
+    // dynamic schedule (one-CTA clusters; ws == nullptr: each cluster owns a fixed block of rows)
+    uint8_t* ws;               // workspace (layout above)
+    int64_t ws_rows;           // its split-row capacity
+    int64_t whole_rows;        // tickets [0, whole_rows) are rows 0.. handed out whole
+    int64_t tickets;           // then ceil((rows - whole_rows) * row_chunks / block) blocks of chunks
+    int32_t block;             // chunks per block of the split rows
+    uint32_t epoch;            // this launch's tag, never 0
 };
 
 // Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).
@@ -315,16 +322,71 @@ struct alignas(16) WarpPartial {
 
 constexpr int kStagesMax = 8;
 
+// A unit of work: chunks [c0, c1) of one row's segment.  A whole unit is finished in this CTA
+// (or cluster); a split unit is one piece of a row whose pieces are merged through the
+// workspace by the CTA that completes the row; the end unit stops the CTA.
+enum UnitKind : int32_t { kUnitWhole = 0, kUnitSplit = 1, kUnitEnd = 2 };
+
+struct alignas(16) Unit {
+    int64_t row;
+    int32_t c0, c1;
+    int32_t kind;
+    int32_t pad[3];
+};
+
+constexpr int kUnitSlots = 4;  // producer -> consumers descriptor ring
+
 struct alignas(16) Shared {
     uint64_t full[kStagesMax];
     uint64_t empty[kStagesMax];
     uint64_t part_full[2];   // consumers -> finalizer, one arrive per consumer warp
     uint64_t part_empty[2];  // finalizer -> consumers, slot (and granule table) reusable
     uint64_t gather[2];      // cluster all-gather, one arrive per rank
+    uint64_t unit_full[kUnitSlots];   // producer -> consumers, descriptor written
+    uint64_t unit_empty[kUnitSlots];  // consumers -> producer, one arrive per consumer warp
+    Unit units[kUnitSlots];
+    Unit part_unit[2];                // the unit of each partial slot (consumers -> finalizer)
     GatherSlot slots[2][kMaxCluster];
     WarpPartial part[2][kConsumerWarps];
+    int32_t piece_c0[32];             // finalizer: first chunks of a split row's pieces, in order
+    GatherSlot piece_part[32];        // finalizer: their partials
     volatile int32_t abort;
 };
+
+// ----------------------------------------------------------------- dynamic-schedule workspace
+// Sampler pieces publish their granules already scaled to the piece's max, so that the merge
+// needs only the pieces' partials and the row's granules.  Caller-owned device memory, zeroed
+// once.  Every launch returns its ticket, done and row
+// counters to zero (after a timed-out wait, its last CTA clears every row counter) and tags its
+// pieces with its epoch (never 0), so that consecutive launches and graph replays need no
+// clearing and pieces of an earlier launch are never merged.  Layout: WsHeader | row counters [rows_cap] | pieces [rows_cap][kWsChunks] |
+// granules [rows_cap][kWsChunks][kConsumerWarps] doubles.
+constexpr int kWsChunks = 64;  // chunks per split row (longer rows are not split)
+
+struct alignas(64) WsHeader {
+    unsigned long long tickets;  // next ticket
+    unsigned long long done;     // CTAs finished (low word) and timed out (high word): after a
+                                 // timeout the last CTA clears every row counter
+    unsigned long long pad[6];
+};
+
+struct alignas(16) WsPiece {     // one per (split row, first chunk of a piece)
+    uint32_t epoch;              // launch that wrote it
+    int32_t c1;                  // end chunk of the piece
+    uint32_t pad[2];
+    GatherSlot part;             // the piece's partial (argmax or sampler form)
+};
+
+__host__ __device__ constexpr int64_t ws_counters_offset() { return sizeof(WsHeader); }
+__host__ __device__ constexpr int64_t ws_pieces_offset(int64_t rows_cap) {
+    return (ws_counters_offset() + 8 * rows_cap + 255) / 256 * 256;
+}
+__host__ __device__ constexpr int64_t ws_granules_offset(int64_t rows_cap) {
+    return ws_pieces_offset(rows_cap) + static_cast<int64_t>(sizeof(WsPiece)) * kWsChunks * rows_cap;
+}
+__host__ __device__ constexpr int64_t ws_bytes(int64_t rows_cap) {
+    return ws_granules_offset(rows_cap) + 8ll * kConsumerWarps * kWsChunks * rows_cap;
+}
 
 // Sampler-only shared memory after the control block.
 struct SamplerShared {
@@ -450,20 +512,17 @@ struct SampleMerge {
     double rank_fac;  // the owner's mass factor exp((owner max - M) / T)
 };
 
-// Warp-cooperative (all 32 lanes call it, n <= 32): lane q holds rank q.  Rank masses are
+// Warp-cooperative (all 32 lanes call it, at most 32 ranks): lane q holds rank q (`in`).  Rank masses are
 // rescaled to the row max in parallel (a rank already at the max keeps its mass exactly), then
 // located by a warp scan in rank order.
-__device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, int64_t stride, uint32_t n, double u,
-                                                           double temp, double inv, uint32_t extra_flags, int lane) {
+__device__ __forceinline__ SampleMerge merge_sampler_lanes(const GatherSlot& e, bool in, double u, double temp,
+                                                           double inv, uint32_t extra_flags, int lane) {
     const float kInf = __int_as_float(0x7F800000);
     SampleMerge r;
-    const bool in = static_cast<uint32_t>(lane) < n;
-    GatherSlot e{0u, 0u, 0u, 0u, 0.0, 0.0};
-    if (in) e = g[static_cast<int64_t>(lane) * stride];
     const float a = in ? __uint_as_float(e.a) : -kInf;
     const float rm = ordered_to_float(__reduce_max_sync(0xFFFFFFFFu, ordered_bits(a)));
-    const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, e.b);
-    const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, e.c) | extra_flags;
+    const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, in ? e.b : 0u);
+    const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, in ? e.c : 0u) | extra_flags;
     r.total = total;
     r.code = (fl & kFlagAbort) ? kTimeout
              : (fl & kFlagNaN) ? kNaN
@@ -504,6 +563,14 @@ __device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, 
         r.rank_fac = rf;
     }
     return r;
+}
+
+__device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, int64_t stride, uint32_t n, double u,
+                                                           double temp, double inv, uint32_t extra_flags, int lane) {
+    const bool in = static_cast<uint32_t>(lane) < n;
+    GatherSlot e{0u, 0u, 0u, 0u, 0.0, 0.0};
+    if (in) e = g[static_cast<int64_t>(lane) * stride];
+    return merge_sampler_lanes(e, in, u, temp, inv, extra_flags, lane);
 }
 
 // Factor taking a warp's mass from its reference max to its rank's max (1 when equal).
@@ -612,7 +679,150 @@ struct SamplerRecord {
     static constexpr int64_t bytes(int chunks) { return kGranuleOffset + 8ll * chunks * kConsumerWarps; }
 };
 
+// ----------------------------------------------------------------- workspace access
+__device__ __forceinline__ WsHeader* ws_header(const SelectParams& p) { return reinterpret_cast<WsHeader*>(p.ws); }
+__device__ __forceinline__ unsigned long long* ws_row_counter(const SelectParams& p, int64_t t) {
+    return reinterpret_cast<unsigned long long*>(p.ws + ws_counters_offset()) + t;
+}
+__device__ __forceinline__ WsPiece* ws_piece(const SelectParams& p, int64_t t, int c) {
+    return reinterpret_cast<WsPiece*>(p.ws + ws_pieces_offset(p.ws_rows)) + (t * kWsChunks + c);
+}
+__device__ __forceinline__ double* ws_granules(const SelectParams& p, int64_t t, int c) {
+    return reinterpret_cast<double*>(p.ws + ws_granules_offset(p.ws_rows)) + (t * kWsChunks + c) * kConsumerWarps;
+}
+
 // ----------------------------------------------------------------- the kernel
+// Finalizer (one warp) of a split unit: the piece's partial (argmax: key, first region holding
+// it, count, flags; sampler: max, count, flags, mass) and, for the sampler, its granules scaled
+// to the piece's max go to the workspace.  The CTA whose piece completes the row's chunk count
+// merges the row's pieces in chunk order -- the same merge as cluster ranks and vocabulary
+// shards -- and writes the row's outputs: the argmax index is recovered from the winning region
+// only, the sampler walks the owning piece.  Sampler: `granules` (shared memory) holds the
+// piece's granules, lanes w < 8 pass warp w's factor to the piece max; the buffer is then reused
+// for the row's granules.
+template <typename T, bool kSample>
+__device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row_chunks, const GatherSlot& part, double wf,
+                                   double* granules, Shared& sh, SamplerShared& ss, const uint8_t* lrow,
+                                   const int32_t* mrow, int lane) {
+    using E = Elem<T>;
+    constexpr int kTPC = Layout<T>::kTokensPerChunk;
+    constexpr int kTPW = Layout<T>::kTokensPerWarp;
+    constexpr int kFinPer = kTPW / 32;
+    const int64_t t = d.row - p.whole_rows;
+    const int nch = d.c1 - d.c0;
+    WsPiece* pc = ws_piece(p, t, d.c0);
+    if (lane == 0) {
+        pc->epoch = p.epoch;
+        pc->c1 = d.c1;
+        pc->part = part;
+    }
+    if constexpr (kSample) {
+        if (lane < kConsumerWarps) ss.fac[lane] = wf;
+        __syncwarp();
+        double* g = ws_granules(p, t, d.c0);
+        for (int i = lane; i < nch * kConsumerWarps; i += 32) g[i] = granules[i] * ss.fac[i % kConsumerWarps];
+    }
+    // Publish the piece and count its chunks in with one acquire-release add: the add that
+    // reaches the row's total identifies the merging CTA, which then sees every piece.
+    __syncwarp();
+    unsigned long long before = 0;
+    if (lane == 0) before = ptx::atom_add_acq_rel_gpu(ws_row_counter(p, t), static_cast<uint64_t>(nch));
+    before = __shfl_sync(0xFFFFFFFFu, before, 0);
+    if (before + static_cast<unsigned long long>(nch) != static_cast<unsigned long long>(row_chunks)) return;
+    __syncwarp();
+
+    // One round trip: the sampler's row granules stream into shared memory (no registers) while
+    // the piece records at chunks c = lane and lane + 32 load; records of this launch (epoch) are
+    // compacted in chunk order (at most 32 pieces: rows of <= 64 chunks in blocks of >= 4 chunks,
+    // split at most once more at a row boundary).
+    if constexpr (kSample) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(ws_granules(p, t, 0));
+        const uint32_t dst = ptx::smem_addr(granules);
+        const int copies = row_chunks * kConsumerWarps * 8 / 16;
+        for (int i = lane; i < copies; i += 32) ptx::cp_async_16(dst + 16 * i, src + 16 * i);
+    }
+    auto head = [&](int c, uint32_t& epoch, GatherSlot& g) {
+        const uint4* src = reinterpret_cast<const uint4*>(ws_piece(p, t, c));
+        const uint4 h = __ldcg(src), x = __ldcg(src + 1), y = __ldcg(src + 2);
+        epoch = h.x;
+        memcpy(&g, &x, 16);
+        memcpy(reinterpret_cast<uint8_t*>(&g) + 16, &y, 16);
+    };
+    uint32_t ea = 0, eb = 0;
+    GatherSlot ga{0u, 0u, 0u, 0u, 0.0, 0.0}, gb{0u, 0u, 0u, 0u, 0.0, 0.0};
+    if (lane < row_chunks) head(lane, ea, ga);
+    if (lane + 32 < row_chunks) head(lane + 32, eb, gb);
+    const bool va = lane < row_chunks && ea == p.epoch;
+    const bool vb = lane + 32 < row_chunks && eb == p.epoch;
+    const uint32_t ba = __ballot_sync(0xFFFFFFFFu, va), bb = __ballot_sync(0xFFFFFFFFu, vb);
+    const uint32_t below = (1u << lane) - 1u;
+    const int na = __popc(ba);
+    if (va) {
+        sh.piece_c0[__popc(ba & below)] = lane;
+        sh.piece_part[__popc(ba & below)] = ga;
+    }
+    if (vb && na + __popc(bb & below) < 32) {
+        sh.piece_c0[na + __popc(bb & below)] = lane + 32;
+        sh.piece_part[na + __popc(bb & below)] = gb;
+    }
+    const int npieces = min(na + __popc(bb), 32);
+    if constexpr (kSample) ptx::cp_async_wait_all();
+    __syncwarp();
+    const bool in = lane < npieces;
+    const GatherSlot e = in ? sh.piece_part[lane] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
+    const int64_t row = d.row;
+    const uint32_t abort_flag = sh.abort ? kFlagAbort : 0u;
+    if constexpr (!kSample) {
+        const uint32_t hi = __reduce_max_sync(0xFFFFFFFFu, e.a);
+        const uint32_t region = __reduce_min_sync(0xFFFFFFFFu, (in && hi != 0u && e.a == hi) ? e.b : 0xFFFFFFFFu);
+        const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, in ? e.c : 0u);
+        const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, in ? e.d : 0u) | abort_flag;
+        // The first (chunk, warp) region holding the row maximum; its lowest valid token equal to
+        // the maximum is the row's argmax.
+        uint32_t found = 0xFFFFFFFFu;
+        if (region != 0xFFFFFFFFu) {
+            const float target = ordered_to_float(hi);
+            const int64_t r0 = static_cast<int64_t>(region / kConsumerWarps) * kTPC +
+                               static_cast<int64_t>(region % kConsumerWarps) * kTPW;
+            const int64_t my0 = r0 + lane * kFinPer;
+            Slice<E, kFinPer> sl;
+            load_slice<E, kFinPer>(lrow, mrow, my0, p.vocab, sl);
+#pragma unroll
+            for (int i = kFinPer - 1; i >= 0; --i)
+                if (((sl.bits >> i) & 1u) && sl.value(i) == target) found = static_cast<uint32_t>(my0 + i);
+        }
+        found = __reduce_min_sync(0xFFFFFFFFu, found);
+        if (lane == 0) {
+            const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
+            p.status[row] = code;
+            p.tokens[row] = (code == kOk && found != 0xFFFFFFFFu) ? p.token_offset + static_cast<int64_t>(found) : -1;
+            if (p.counts) p.counts[row] = total;
+        }
+    } else {
+        const SampleMerge mg = merge_sampler_lanes(e, in, p.uniforms[row], p.temperature, p.inv_temperature, abort_flag, lane);
+        int64_t chosen = -1;
+        if (mg.code == kOk) {
+            const int q = mg.owner;
+            const int oc0 = sh.piece_c0[q];
+            const int oc1 = q + 1 < npieces ? sh.piece_c0[q + 1] : row_chunks;
+            // The owner's granules are already relative to its max: every warp factor is the
+            // owner's rank factor.
+            const int64_t b0 = static_cast<int64_t>(oc0) * kTPC;
+            const int64_t b1 = static_cast<int64_t>(oc1) * kTPC < p.vocab ? static_cast<int64_t>(oc1) * kTPC : p.vocab;
+            chosen = sampler_owner_walk<T>(granules + oc0 * kConsumerWarps, (oc1 - oc0) * kConsumerWarps, 1.0, 1.0,
+                                           lane < kConsumerWarps, mg, p.temperature, p.inv_temperature, p.scale2, b0, b1,
+                                           lrow, mrow, ss.walk, ss.fac, lane);
+        }
+        if (lane == 0) {
+            p.status[row] = mg.code != kOk ? mg.code : chosen >= 0 ? kOk : kNoMass;
+            p.tokens[row] = mg.code == kOk && chosen >= 0 ? p.token_offset + chosen : -1;
+            if (p.counts) p.counts[row] = mg.total;
+        }
+    }
+    // The next launch (or graph replay) counts this row from zero.
+    if (lane == 0) atomicExch(ws_row_counter(p, t), 0ull);
+}
+
 template <typename T, bool kSample, bool kBulk, int kStages>
 __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectParams p) {
     using E = Elem<T>;
@@ -635,9 +845,10 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     const uint32_t csize = ptx::cluster_nctarank();
     const uint32_t cid = ptx::cluster_id_x();
     const uint32_t nclusters = ptx::ncluster_x();
+    const bool dynamic = p.ws != nullptr;  // tickets from the workspace (one-CTA clusters only)
 
-    // Contiguous, remainder-balanced block of rows per cluster: neighbouring rows (often of
-    // different mask densities, hence cost) land on the same cluster.
+    // Fixed schedule: a contiguous, remainder-balanced block of rows per cluster (neighbouring
+    // rows, often of different mask densities, hence cost, land on the same cluster).
     const int64_t rows_q = p.rows / nclusters, rows_r = p.rows % nclusters;
     const int64_t row_begin = static_cast<int64_t>(cid) * rows_q + (cid < rows_r ? cid : rows_r);
     const int64_t row_end = row_begin + rows_q + (cid < rows_r ? 1 : 0);
@@ -655,6 +866,10 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             ptx::mbar_init(ptx::smem_addr(&sh.part_full[s]), kConsumerWarps);
             ptx::mbar_init(ptx::smem_addr(&sh.part_empty[s]), 1);
             ptx::mbar_init(ptx::smem_addr(&sh.gather[s]), csize);
+        }
+        for (int s = 0; s < kUnitSlots; ++s) {
+            ptx::mbar_init(ptx::smem_addr(&sh.unit_full[s]), 1);
+            ptx::mbar_init(ptx::smem_addr(&sh.unit_empty[s]), kConsumerWarps);
         }
         sh.abort = 0;
         ptx::fence_mbarrier_init();
@@ -674,52 +889,100 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer warp
-        if (kBulk && lane == 0) {
-            uint32_t it = 0;
+        // Lane 0 publishes each unit's descriptor, then (bulk path) streams its chunks.
+        if (lane == 0) {
+            uint32_t it = 0;  // chunks issued (stage ring position)
+            uint32_t u = 0;   // units published (descriptor ring position)
             bool stop = false;
-            for (int64_t row = row_begin; row < row_end && !stop; ++row) {
-                const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
-                                      static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-                const int32_t* mbase = p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride);
-                for (int c = 0; c < nchunks; ++c, ++it) {
-                    const int stage = static_cast<int>(it % kStages);
-                    const uint32_t use = it / kStages;
-                    if (use > 0 && !wait_bounded(ptx::smem_addr(&sh.empty[stage]), (use - 1) & 1u, &sh.abort)) {
-                        stop = true;  // consumers stopped releasing stages: issue no more copies
-                        break;
+            auto push = [&](const Unit& d) -> bool {
+                const uint32_t s = u % kUnitSlots, use = u / kUnitSlots;
+                if (use > 0 && !wait_bounded(ptx::smem_addr(&sh.unit_empty[s]), (use - 1u) & 1u, &sh.abort)) return false;
+                sh.units[s] = d;
+                ptx::mbar_arrive(ptx::smem_addr(&sh.unit_full[s]));
+                ++u;
+                return true;
+            };
+            auto issue = [&](const Unit& d) -> bool {
+                if constexpr (kBulk) {
+                    const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                                          static_cast<size_t>(d.row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+                    const int32_t* mbase = p.masks + static_cast<size_t>(d.row) * static_cast<size_t>(p.mask_stride);
+                    for (int c = d.c0; c < d.c1; ++c, ++it) {
+                        const int stage = static_cast<int>(it % kStages);
+                        const uint32_t use = it / kStages;
+                        // Consumers stopped releasing stages: issue no more copies.
+                        if (use > 0 && !wait_bounded(ptx::smem_addr(&sh.empty[stage]), (use - 1) & 1u, &sh.abort))
+                            return false;
+                        const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
+                        const int64_t t1 = (t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end;
+                        const uint32_t lbytes = static_cast<uint32_t>((t1 - t0) * E::kBytes);
+                        const int64_t w0 = p.mask_word_offset + (t0 >> 5), w1 = p.mask_word_offset + ((t1 + 31) >> 5);
+                        const int64_t a0 = w0 & ~int64_t(3), a1 = (w1 + 3) & ~int64_t(3);
+                        const uint32_t mbytes = static_cast<uint32_t>((a1 - a0) * 4);
+                        uint8_t* st = stages + stage * L::kStageBytes;
+                        const uint32_t full = ptx::smem_addr(&sh.full[stage]);
+                        ptx::mbar_arrive_expect_tx(full, lbytes + mbytes);
+                        ptx::bulk_load(ptx::smem_addr(st), lrow + t0 * E::kBytes, lbytes, full);
+                        ptx::bulk_load(ptx::smem_addr(st + kChunkBytes), mbase + a0, mbytes, full);
                     }
-                    const int64_t t0 = seg_begin + static_cast<int64_t>(c) * kTPC;
-                    const int64_t t1 = (t0 + kTPC) < seg_end ? (t0 + kTPC) : seg_end;
-                    const uint32_t lbytes = static_cast<uint32_t>((t1 - t0) * E::kBytes);
-                    const int64_t w0 = p.mask_word_offset + (t0 >> 5), w1 = p.mask_word_offset + ((t1 + 31) >> 5);
-                    const int64_t a0 = w0 & ~int64_t(3), a1 = (w1 + 3) & ~int64_t(3);
-                    const uint32_t mbytes = static_cast<uint32_t>((a1 - a0) * 4);
-                    uint8_t* st = stages + stage * L::kStageBytes;
-                    const uint32_t full = ptx::smem_addr(&sh.full[stage]);
-                    ptx::mbar_arrive_expect_tx(full, lbytes + mbytes);
-                    ptx::bulk_load(ptx::smem_addr(st), lrow + t0 * E::kBytes, lbytes, full);
-                    ptx::bulk_load(ptx::smem_addr(st + kChunkBytes), mbase + a0, mbytes, full);
+                }
+                return true;
+            };
+            auto run = [&](int64_t row, int c0, int c1, int32_t kind) {
+                if (stop) return;
+                const Unit d{row, c0, c1, kind, {0, 0, 0}};
+                stop = !push(d) || !issue(d);
+            };
+            if (!dynamic) {
+                for (int64_t row = row_begin; row < row_end && !stop; ++row) run(row, 0, nchunks, kUnitWhole);
+            } else {
+                // Tickets: rows [0, whole_rows) whole, then blocks of `block` chunks over the
+                // remaining (split) rows' chunks in row-major order.
+                const int64_t split_chunks = (p.rows - p.whole_rows) * nchunks;
+                unsigned long long* tickets = &ws_header(p)->tickets;
+                while (!stop) {
+                    // One atomic per ticket (the counter starts every launch at 0).
+                    const int64_t tk = static_cast<int64_t>(atomicAdd(tickets, 1ull));
+                    if (tk >= p.tickets) break;
+                    if (tk < p.whole_rows) {
+                        run(tk, 0, nchunks, kUnitWhole);
+                        continue;
+                    }
+                    const int64_t g0 = (tk - p.whole_rows) * p.block;
+                    const int64_t g1 = (g0 + p.block) < split_chunks ? (g0 + p.block) : split_chunks;
+                    for (int64_t r = g0 / nchunks; r <= (g1 - 1) / nchunks; ++r) {
+                        const int c0 = static_cast<int>(g0 > r * nchunks ? g0 - r * nchunks : 0);
+                        const int c1 = static_cast<int>(g1 < (r + 1) * nchunks ? g1 - r * nchunks : nchunks);
+                        run(p.whole_rows + r, c0, c1, (c0 == 0 && c1 == nchunks) ? kUnitWhole : kUnitSplit);
+                    }
                 }
             }
+            // The end marker (if its slot never frees, the consumers' bounded waits end them).
+            push(Unit{0, 0, 0, kUnitEnd, {0, 0, 0}});
             // Every issued copy must have landed before this CTA's shared memory can go away.
-            for (int s = 0; s < kStages; ++s) {
-                if (it > static_cast<uint32_t>(s)) {
-                    const uint32_t last = (it - 1u - static_cast<uint32_t>(s)) / kStages;
-                    drain_wait(ptx::smem_addr(&sh.full[s]), last & 1u);
+            if constexpr (kBulk) {
+                for (int s = 0; s < kStages; ++s) {
+                    if (it > static_cast<uint32_t>(s)) {
+                        const uint32_t last = (it - 1u - static_cast<uint32_t>(s)) / kStages;
+                        drain_wait(ptx::smem_addr(&sh.full[s]), last & 1u);
+                    }
                 }
             }
         }
         __syncwarp();
     } else if (warp == kFinalizerWarp) {
         // ------------------------------------------------------------ finalizer warp
-        uint32_t k = 0;
-        for (int64_t row = row_begin; row < row_end; ++row, ++k) {
+        for (uint32_t k = 0;; ++k) {
             const uint32_t slot = k & 1u;
+            if (!wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort)) break;
+            const Unit d = sh.part_unit[slot];
+            if (d.kind == kUnitEnd) break;
+            const int64_t row = d.row;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow =
                 p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
-            wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort);
+            const int nch = d.c1 - d.c0;
             const bool in = lane < kConsumerWarps;
             const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u, 0.0, 0.0};
             const uint32_t cnt = __reduce_add_sync(0xFFFFFFFFu, wp.count);
@@ -734,6 +997,12 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 const uint32_t rmin = __reduce_min_sync(0xFFFFFFFFu, region);
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
+                if (d.kind == kUnitSplit && p.partials == nullptr) {
+                    // The index is recovered by the row's merge, from the winning piece only.
+                    finish_split_piece<T, false>(p, d, nchunks, GatherSlot{ckey, rmin, cnt, flags, 0.0, 0.0}, 0.0,
+                                                 nullptr, sh, ss, lrow, mrow, lane);
+                    continue;
+                }
                 uint32_t found = 0xFFFFFFFFu;
                 if (rmin != 0xFFFFFFFFu) {
                     const float target = ordered_to_float(ckey);
@@ -774,8 +1043,8 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             } else {
                 // Segment maximum and mass relative to it: the consumer warps already folded their
                 // granules to their own maxima; combine the 8 warp masses in warp order.
-                const double* granules = ss.granules[slot];
-                const int ngran = nchunks * kConsumerWarps;
+                double* granules = ss.granules[slot];
+                const int ngran = nch * kConsumerWarps;
                 const float seg_m = ckey ? ordered_to_float(ckey) : -kInf;
                 const bool seg_finite = seg_m > -kInf && seg_m < kInf;
                 const float wmax = in ? ordered_to_float(wp.key) : -kInf;
@@ -794,6 +1063,9 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     }
                     double* rg = reinterpret_cast<double*>(rec + SamplerRecord::kGranuleOffset);
                     for (int g = lane; g < ngran; g += 32) rg[g] = granules[g];
+                } else if (d.kind == kUnitSplit) {
+                    finish_split_piece<T, true>(p, d, nchunks, GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0},
+                                                wf, granules, sh, ss, lrow, mrow, lane);
                 } else {
                     // Rank partials, all-gathered in rank order, merged identically on every rank.
                     if (lane == 0) {
@@ -829,20 +1101,33 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     } else {
         // ------------------------------------------------------------ consumer warps
         uint32_t stage = 0, phase = 0;  // ring position of the next chunk (matches the producer)
-        uint32_t k = 0;                 // rows processed by this cluster
         // Chunks holding kTPC tokens (every chunk but a ragged last one) take the unpredicated path.
         const int nfull = static_cast<int>((seg_end - seg_begin) / kTPC);
         // A stage's mask words start at the 16-byte boundary at or below the chunk's first word;
         // chunks start on multiples of 128 words, so the word offset is the same for every chunk.
         const int moff = static_cast<int>((p.mask_word_offset + (seg_begin >> 5)) & 3);
-        for (int64_t row = row_begin; row < row_end; ++row, ++k) {
+        for (uint32_t u = 0, k = 0;; ++u, ++k) {  // u: units read, k: partial slots used
+            const uint32_t us = u % kUnitSlots;
+            const bool got = wait_bounded(ptx::smem_addr(&sh.unit_full[us]), (u / kUnitSlots) & 1u, &sh.abort);
+            const Unit d = got ? sh.units[us] : Unit{0, 0, 0, kUnitEnd, {0, 0, 0}};
+            __syncwarp();
+            if (got && lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.unit_empty[us]));
             const uint32_t slot = k & 1u;
+            // The finalizer has released this partial slot (and granule table).
+            if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
+            if (d.kind == kUnitEnd) {
+                if (lane == 0) {
+                    if (warp == 0) sh.part_unit[slot] = d;
+                    ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
+                }
+                break;
+            }
+            const int64_t row = d.row;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow =
                 p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
-            // The finalizer has released this row's partial slot (and granule table).
-            if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
+            const int nch = d.c1 - d.c0;
             double* granules = ss.granules[slot];
             float2* granules_f = reinterpret_cast<float2*>(granules);
             typename E::NanAcc nan_acc = E::nan_init();
@@ -1047,7 +1332,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
                         if (fast) mass *= corr;
                     }
-                    if (lane == 0) granules_f[c * kConsumerWarps + warp] = make_float2(ref, mass);
+                    if (lane == 0) granules_f[(c - d.c0) * kConsumerWarps + warp] = make_float2(ref, mass);
                 }
                 if constexpr (kBulk) {
                     if (++stage == static_cast<uint32_t>(kStages)) {
@@ -1056,8 +1341,9 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     }
                 }
             };
-            for (int c = 0; c < nfull; ++c) chunk(std::true_type{}, c);
-            if (nfull < nchunks) chunk(std::false_type{}, nfull);
+            const int cfull = d.c1 < nfull ? d.c1 : nfull;
+            for (int c = d.c0; c < cfull; ++c) chunk(std::true_type{}, c);
+            for (int c = d.c0 > nfull ? d.c0 : nfull; c < d.c1; ++c) chunk(std::false_type{}, c);
 
             // ---------------------------------------------------- warp partial -> finalizer
             const bool nan_local = E::has_nan(nan_acc);
@@ -1072,7 +1358,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 const double wm = static_cast<double>(ref);
                 __syncwarp();
                 double local = 0.0;
-                for (int c = lane; c < nchunks; c += 32) {
+                for (int c = lane; c < nch; c += 32) {
                     const float2 e = granules_f[c * kConsumerWarps + warp];
                     const double gm = !(e.y > 0.0f) ? 0.0
                                       : e.x == ref  ? static_cast<double>(e.y)
@@ -1090,6 +1376,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 wchunk = __reduce_min_sync(0xFFFFFFFFu, (has && key == wkey) ? chunk_id : 0xFFFFFFFFu);
             }
             if (lane == 0) {
+                if (warp == 0) sh.part_unit[slot] = d;
                 sh.part[slot][warp] = WarpPartial{wkey, wchunk, wcount, wflags, wmass, 0.0};
                 ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
             }
@@ -1097,10 +1384,25 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     }
 
     // No CTA may exit while a peer can still write into its shared memory.
+    if (csize > 1 || dynamic) __syncthreads();
     if (csize > 1) {
-        __syncthreads();
         ptx::cluster_arrive();
         ptx::cluster_wait();
+    }
+    // The last CTA of a dynamic launch to finish returns the ticket and done counters to zero
+    // (every CTA took its last ticket before counting itself done; every CTA gets here, bounded
+    // waits included, so the counters start each launch at zero).
+    if (dynamic && tid == 0) {
+        WsHeader* hd = ws_header(p);
+        __threadfence();
+        // Low word: CTAs done; high word: CTAs that timed out.
+        const unsigned long long before = atomicAdd(&hd->done, sh.abort ? (1ull << 32) + 1ull : 1ull);
+        if ((before & 0xFFFFFFFFull) + 1ull == gridDim.x) {
+            if ((before >> 32) != 0 || sh.abort)
+                for (int64_t r = 0; r < p.ws_rows; ++r) atomicExch(ws_row_counter(p, r), 0ull);
+            atomicExch(&hd->tickets, 0ull);
+            atomicExch(&hd->done, 0ull);
+        }
     }
 }
 

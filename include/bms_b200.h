@@ -88,13 +88,23 @@ BMS_API int bms_mask_count(const int32_t *mask, int64_t vocab, int64_t *count, i
 BMS_API int bms_masked_argmax(const void *logits, int32_t dtype, const int32_t *mask, int64_t vocab,
                       int64_t *token, int32_t *status, int32_t device, void *stream);
 
+/* Workspace of the batched entry points' dynamic schedule (no reference counterpart): bytes for
+ * `device` (-1 if invalid).  A workspace is device memory of at least this size, 256-byte aligned,
+ * zeroed once before its first use; every call leaves it ready for the next.  Calls that may run
+ * concurrently (different streams) need different workspaces.  With a workspace, rows of at most
+ * 64 chunks (8,192 tokens per chunk for 16-bit logits, 4,096 for float32) are handed to CTAs
+ * dynamically and the last rows are split across CTAs; without one (NULL), each group of CTAs
+ * owns a fixed block of rows. */
+BMS_API int64_t bms_workspace_bytes(int32_t device);
+
 /* Replaces csrc/argmax.cu:127-137 masked_reduce_batch_cuda: per row of a
  * contiguous [rows, vocab] logits / [rows, ceil(vocab/32)] mask batch, the
- * masked argmax, the valid count and a status.  `counts` may be NULL.  No row
- * limit (the reference stopped at 65,535 rows, csrc/checks.h:36). */
+ * masked argmax, the valid count and a status.  `counts` may be NULL; `workspace`
+ * may be NULL (see bms_workspace_bytes).  No row limit (the reference stopped at
+ * 65,535 rows, csrc/checks.h:36). */
 BMS_API int bms_masked_reduce_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t rows,
                             int64_t vocab, int64_t *tokens, int64_t *counts, int32_t *status,
-                            int32_t device, void *stream);
+                            void *workspace, int64_t workspace_bytes, int32_t device, void *stream);
 
 /* Replaces csrc/sample.cu:116-132 masked_sample_cuda: inverse-CDF sample of
  * the masked softmax at `temperature` with the device float64 scalar
@@ -104,11 +114,12 @@ BMS_API int bms_masked_sample(const void *logits, int32_t dtype, const int32_t *
                       int32_t device, void *stream);
 
 /* Batched form of bms_masked_sample with one uniform per row (no reference
- * counterpart; the reference sampled one row per launch).  `counts` may be NULL. */
+ * counterpart; the reference sampled one row per launch).  `counts` and
+ * `workspace` may be NULL. */
 BMS_API int bms_masked_sample_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t rows,
                             int64_t vocab, double temperature, const double *uniforms,
-                            int64_t *tokens, int64_t *counts, int32_t *status, int32_t device,
-                            void *stream);
+                            int64_t *tokens, int64_t *counts, int32_t *status, void *workspace,
+                            int64_t workspace_bytes, int32_t device, void *stream);
 
 /* Device form of grammar/density.py:23-53 (packed_mask_count / density) and
  * decoding/scheduling.py:40-46 (DensityPolicy.budget) for a [rows, words]
@@ -126,13 +137,13 @@ BMS_API int bms_mask_budget(const int32_t *masks, int64_t rows, int64_t vocab, c
  * prefix length, the correction / bonus / fallback token, its kind (0
  * correction, 1 bonus, 2 fallback) and a status that is nonzero only when a
  * row the reference would have consumed failed.  row_counts and row_budget
- * may be NULL (then policy may be NULL). */
+ * may be NULL (then policy may be NULL); `workspace` may be NULL. */
 BMS_API int bms_verify_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t seqs,
                      int64_t rows_per_seq, int64_t vocab, const int64_t *proposals,
                      const int32_t *lengths, const bms_policy *policy, int64_t *row_tokens,
                      int64_t *row_counts, int32_t *row_status, int32_t *row_budget,
                      int32_t *accept_len, int64_t *token, int32_t *kind, int32_t *seq_status,
-                     int32_t device, void *stream);
+                     void *workspace, int64_t workspace_bytes, int32_t device, void *stream);
 
 /* ---- vocabulary shards ----------------------------------------------------------------
  * A row's vocabulary split across ranks (GPUs), each holding logits [rows, vocab_shard] of its
@@ -173,8 +184,9 @@ BMS_API int bms_shard_merge(const bms_partial *partials, int32_t shards, int32_t
                             int32_t *status, int32_t device, void *stream);
 
 /* Test hook: force the cluster size (1, 2, 4, 8 or 16) and the number of
- * clusters of the selection kernels; 0 restores the automatic choice.
- * Process-wide; not for concurrent use with other calls. */
+ * clusters of the selection kernels' fixed schedule; 0 restores the automatic
+ * choice.  With cluster 0 and a workspace, `clusters` caps the number of CTAs of
+ * the dynamic schedule.  Process-wide; not for concurrent use with other calls. */
 BMS_API int bms_set_launch_override(int32_t cluster, int32_t clusters);
 
 #ifdef __cplusplus

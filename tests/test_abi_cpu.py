@@ -55,16 +55,16 @@ def test_runtime_version_without_gpu(lib):
 def test_invalid_arguments_fail_before_any_launch(lib):
     null = None
     # Unknown dtype
-    rc = lib.bms_masked_reduce_batch(null, 7, null, 1, 32, null, null, null, 0, null)
+    rc = lib.bms_masked_reduce_batch(null, 7, null, 1, 32, null, null, null, null, 0, 0, null)
     assert rc == _native.ERROR_INVALID_ARGUMENT
     assert b"float32" in lib.bms_last_error()
     # Invalid vocabulary
-    rc = lib.bms_masked_reduce_batch(null, 0, null, 1, 0, null, null, null, 0, null)
+    rc = lib.bms_masked_reduce_batch(null, 0, null, 1, 0, null, null, null, null, 0, 0, null)
     assert rc == _native.ERROR_INVALID_ARGUMENT and b"vocabulary" in lib.bms_last_error()
     rc = lib.bms_masked_argmax(null, 0, null, 2**31, null, null, 0, null)
     assert rc == _native.ERROR_INVALID_ARGUMENT
     # Negative rows
-    rc = lib.bms_masked_reduce_batch(null, 0, null, -1, 32, null, null, null, 0, null)
+    rc = lib.bms_masked_reduce_batch(null, 0, null, -1, 32, null, null, null, null, 0, 0, null)
     assert rc == _native.ERROR_INVALID_ARGUMENT
     # Temperature contract
     for t in (-1.0, float("nan"), float("inf")):
@@ -83,13 +83,13 @@ def test_invalid_arguments_fail_before_any_launch(lib):
     assert rc == _native.ERROR_INVALID_ARGUMENT
     # Verification shape contract
     rc = lib.bms_verify_batch(null, 0, null, 1, 0, 32, null, null, null, null, null, null, null,
-                              null, null, null, null, 0, null)
+                              null, null, null, null, null, 0, 0, null)
     assert rc == _native.ERROR_INVALID_ARGUMENT and b"rows_per_seq" in lib.bms_last_error()
 
 
 def test_error_message_is_thread_local(lib):
     import threading
-    lib.bms_masked_reduce_batch(None, 9, None, 1, 32, None, None, None, 0, None)
+    lib.bms_masked_reduce_batch(None, 9, None, 1, 32, None, None, None, None, 0, 0, None)
     seen = []
 
     def other():
