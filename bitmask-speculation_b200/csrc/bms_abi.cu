@@ -222,7 +222,7 @@ bool launch_dynamic(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t&
     if (p.ws == nullptr || p.partials != nullptr || g_force_cluster != 0 || n > kWsChunks) return false;
     int64_t grid = info.max_clusters[0];
     if (g_force_clusters > 0 && g_force_clusters < grid) grid = g_force_clusters;
-    else if (2 * p.rows < 3 * grid) return false;
+    else if (!p.dynamic_always && 2 * p.rows < 3 * grid) return false;
     int64_t split, block;
     if (p.rows <= grid) {
         split = p.rows;
@@ -555,6 +555,32 @@ int attach_workspace(SelectParams& p, void* ws, int64_t bytes, int device) {
     return BMS_SUCCESS;
 }
 
+// Workspace of bms_masked_reduce_batch_noalloc: a file-scope device array (one instance per
+// device), so that entry point allocates nothing.  Split-row capacity kStaticWsRows (the dynamic
+// schedule splits at most that many rows), about 1.8 MB.
+constexpr int64_t kStaticWsRows = 256;
+constexpr int64_t kStaticWsBytes = ws_bytes(kStaticWsRows);
+static __device__ __align__(256) uint8_t g_static_ws[kStaticWsBytes];
+void* g_static_ws_ptr[kMaxDevices] = {};  // guarded by g_mutex
+
+// Device address of this device's static workspace (the device must be current).  The first call
+// per device resolves the symbol and clears the counters on `stream` -- setup that must not run
+// under stream capture; later calls only return the cached address.
+int static_workspace(int device, cudaStream_t stream, void*& out) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_static_ws_ptr[device] == nullptr) {
+        void* ptr = nullptr;
+        BMS_CUDA(cudaGetSymbolAddress(&ptr, g_static_ws), "cudaGetSymbolAddress(static workspace)");
+        // Header and row counters start at zero (pieces carry launch epochs); every call leaves
+        // them at zero again.
+        BMS_CUDA(cudaMemsetAsync(ptr, 0, static_cast<size_t>(ws_pieces_offset(kStaticWsRows)), stream),
+                 "clearing the static workspace");
+        g_static_ws_ptr[device] = ptr;
+    }
+    out = g_static_ws_ptr[device];
+    return BMS_SUCCESS;
+}
+
 SelectParams base_params(const void* logits, const int32_t* masks, int64_t rows, int64_t vocab) {
     SelectParams p = {};
     p.logits = logits;
@@ -614,6 +640,33 @@ int bms_masked_reduce_batch(const void* logits, int32_t dtype, const int32_t* ma
     p.counts = counts;
     p.status = status;
     return launch_select<false>(dtype, p, device, static_cast<cudaStream_t>(stream));
+}
+
+int bms_masked_reduce_batch_noalloc(const void* logits, int32_t dtype, const int32_t* masks, int64_t rows,
+                                    int64_t vocab, int64_t* tokens, int64_t* counts, int32_t* status, int32_t device,
+                                    void* stream) {
+    BMS_CHECK(select_common(dtype, logits, masks, rows, vocab, device));
+    if (rows == 0) return BMS_SUCCESS;
+    const int64_t tpc = dtype == BMS_FLOAT32 ? Layout<float>::kTokensPerChunk : Layout<__half>::kTokensPerChunk;
+    if (vocab > kWsChunks * tpc)
+        return fail(BMS_ERROR_UNSUPPORTED, "vocabulary of %lld tokens exceeds the %lld-token rows the static workspace splits",
+                    static_cast<long long>(vocab), static_cast<long long>(kWsChunks * tpc));
+    BMS_CHECK(check_ptr(tokens, device, "tokens", 8));
+    if (counts) BMS_CHECK(check_ptr(counts, device, "counts", 8));
+    BMS_CHECK(check_ptr(status, device, "status", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* ws = nullptr;
+    BMS_CHECK(static_workspace(device, s, ws));
+    SelectParams p = base_params(logits, masks, rows, vocab);
+    p.ws = static_cast<uint8_t*>(ws);
+    p.ws_rows = kStaticWsRows;
+    p.dynamic_always = 1;
+    p.tokens = tokens;
+    p.counts = counts;
+    p.status = status;
+    return launch_select<false>(dtype, p, device, s);
 }
 
 int bms_masked_argmax(const void* logits, int32_t dtype, const int32_t* mask, int64_t vocab, int64_t* token,

@@ -287,6 +287,7 @@ struct SelectParams {
     int64_t tickets;           // then ceil((rows - whole_rows) * row_chunks / block) blocks of chunks
     int32_t block;             // chunks per block of the split rows
     uint32_t epoch;            // this launch's tag, never 0
+    int32_t dynamic_always;    // host only: take the dynamic schedule for any batch size
 };
 
 // Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).

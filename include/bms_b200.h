@@ -106,6 +106,16 @@ BMS_API int bms_masked_reduce_batch(const void *logits, int32_t dtype, const int
                             int64_t vocab, int64_t *tokens, int64_t *counts, int32_t *status,
                             void *workspace, int64_t workspace_bytes, int32_t device, void *stream);
 
+/* bms_masked_reduce_batch on the dynamic schedule with a workspace that is a file-scope device
+ * array (about 1.8 MB per device) instead of caller memory: the call allocates nothing.  No
+ * reference counterpart.  Rows of at most 64 chunks (524,288 16-bit or 262,144 float32 tokens;
+ * longer rows fail with BMS_ERROR_UNSUPPORTED).  Calls that overlap in time on one device (other
+ * streams or threads) share the array and race: serialize them.  The first call on a device
+ * resolves the array's address and clears its counters; make it before any stream capture. */
+BMS_API int bms_masked_reduce_batch_noalloc(const void *logits, int32_t dtype, const int32_t *masks, int64_t rows,
+                                            int64_t vocab, int64_t *tokens, int64_t *counts, int32_t *status,
+                                            int32_t device, void *stream);
+
 /* Replaces csrc/sample.cu:116-132 masked_sample_cuda: inverse-CDF sample of
  * the masked softmax at `temperature` with the device float64 scalar
  * `uniform` in [0, 1).  temperature == 0 is the masked argmax (uniform unused). */
