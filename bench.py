@@ -71,6 +71,15 @@ def parse_args():
 
 
 # ---------------------------------------------------------------- environment
+def host_threads() -> int:
+    """Host threads this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks; the
+    CPU arms ask for every core of the affinity mask explicitly)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -448,7 +457,7 @@ def cpu_baseline_verify(w: Workload, budget_s=8.0):
     import numpy as np
     import torch
     import oracle
-    threads = oracle.max_threads()
+    threads = host_threads()
     host_logits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
     host_masks = w.masks.cpu().numpy()
     proposals = w.proposals.cpu().numpy()
@@ -472,7 +481,7 @@ def cpu_baseline_rows(w: Workload, budget_s=8.0):
     import numpy as np
     import torch
     import oracle
-    threads = oracle.max_threads()
+    threads = host_threads()
     logits, masks = w._batch()
     if w.dtype == "f32":
         vals, dt = logits.cpu().numpy(), None
@@ -507,7 +516,7 @@ def run_reference_arm(args):
     device = torch.device("cuda", local) if torch.cuda.is_available() else None
     if device is not None:
         torch.cuda.set_device(device)
-    threads = oracle.max_threads()
+    threads = host_threads()
     w = Workload(args, 0, device)
     if args.workload == "verify":
         host_logits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
