@@ -209,7 +209,7 @@ std::atomic<uint32_t> g_epoch{0};
 
 // Dynamic schedule (a workspace is given, at least 1.5x as many rows as resident one-CTA
 // clusters, rows of at most kWsChunks chunks, no forced cluster size): one-CTA clusters fill
-// every resident slot and take tickets -- whole rows first, then quarter-row blocks of the last
+// every resident slot and take tickets -- whole rows first, then half-row blocks of the last
 // rows (half as many as CTAs), whose pieces are merged through the workspace; the blocks absorb
 // the spread of the CTAs' finishing times.  Smaller batches keep the fixed schedule: measured on
 // B200 at V = 248,320 (256 to 1,500 rows), splitting them gained no bandwidth for the argmax and
@@ -229,7 +229,7 @@ bool launch_dynamic(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t&
         block = (split * n + grid - 1) / grid;
     } else {
         split = grid / 2 > 1 ? grid / 2 : 1;
-        block = (n + 3) / 4;
+        block = (n + 1) / 2;
     }
     if (split > p.ws_rows) split = p.ws_rows;
     block = block < 4 ? 4 : block > kWsChunks ? kWsChunks : block;
