@@ -250,3 +250,79 @@ def scale_rows_torch(rows: int, vocab: int = VOCAB, seed: int = 5, device="cuda"
         dens = torch.exp(torch.empty(n, device=device).uniform_(np.log(1e-4), 0.0, generator=g))
         masks[r0:r1] = pack_bits_torch(bernoulli_masks_torch(n, vocab, dens, g, device))
     return logits, masks
+
+
+# ---------------------------------------------------------------- synthetic grammar
+class SyntheticDFAGrammar:
+    """Token-level DFA grammar of the end-to-end configuration's shape: ``states`` states, each
+    allowing either an enumerated set of 1-8 token IDs or a Bernoulli(``free_density``) free-text
+    set; accepting token t in state q moves to ``(q * 31 + t * 7 + 1) % states``.  Accepting an
+    EOS token (``eos`` IDs, allowed in the free-text states) terminates it.
+
+    Implements the reference's ``ForkableGrammarState`` protocol (grammar/state.py:13-44) plus
+    ``packed_mask`` (an owned CPU int32 row, grammar/xgrammar.py:63-70) and ``mask_density``.
+    Masks are precomputed per state and shared by forks (read-only).
+    """
+
+    def __init__(self, vocab: int, *, states: int = 64, seed: int = 7, free_density: float = 0.3,
+                 eos=(0,), _tables=None, _state: int = 0, _terminated: bool = False):
+        self._vocab = int(vocab)
+        if _tables is None:
+            rng = np.random.default_rng(seed)
+            valid = np.zeros((states, self._vocab), dtype=bool)
+            free = rng.random(states) < 0.5
+            for q in range(states):
+                if free[q]:
+                    valid[q] = rng.random(self._vocab) < free_density
+                    valid[q, list(eos)] = True
+                else:
+                    ids = rng.choice(np.arange(len(eos), self._vocab), size=int(rng.integers(1, 9)), replace=False)
+                    valid[q, ids] = True
+            _tables = (pack_bits_np(valid), [np.flatnonzero(v) for v in valid], frozenset(int(e) for e in eos),
+                       valid.sum(axis=1))
+        self._tables = _tables
+        self._state = _state
+        self._terminated = _terminated
+
+    @property
+    def vocab_size(self) -> int:
+        return self._vocab
+
+    @property
+    def state(self) -> int:
+        return self._state
+
+    def is_terminated(self) -> bool:
+        return self._terminated
+
+    def allowed_token_ids(self):
+        return () if self._terminated else tuple(int(t) for t in self._tables[1][self._state])
+
+    def packed_mask(self):
+        import torch
+        words = self._tables[0][self._state]
+        return torch.from_numpy(np.zeros_like(words) if self._terminated else words.copy())
+
+    def packed_mask_np(self) -> np.ndarray:
+        """The current state's mask row (read-only view; zeros once terminated)."""
+        return np.zeros_like(self._tables[0][0]) if self._terminated else self._tables[0][self._state]
+
+    def mask_density(self) -> float:
+        return 0.0 if self._terminated else float(self._tables[3][self._state]) / self._vocab
+
+    def accept_token(self, token: int) -> bool:
+        token = int(token)
+        if self._terminated or not (0 <= token < self._vocab):
+            return False
+        words = self._tables[0][self._state]
+        if not (int(words[token >> 5]) >> (token & 31)) & 1:
+            return False
+        if token in self._tables[2]:
+            self._terminated = True
+        else:
+            self._state = (self._state * 31 + token * 7 + 1) % len(self._tables[1])
+        return True
+
+    def fork(self) -> "SyntheticDFAGrammar":
+        return SyntheticDFAGrammar(self._vocab, _tables=self._tables, _state=self._state,
+                                   _terminated=self._terminated)

@@ -1,0 +1,174 @@
+"""Grammar-constrained batched verification (draft-fork masks, one launch and one sync per round)
+against the reference's lazy per-row loop restated with the oracle: models/transformers.py:181-201
+(`_choices` + `constrained_choices`) over decoding/verification.py:18-48 (`verify_prefix`), with
+each row selected by the masked argmax under the committed grammar (grammar/selection.py:12-32)."""
+
+import numpy as np
+import pytest
+
+import oracle
+from bitmask_speculation_b200 import workloads as wl
+from bitmask_speculation_b200.grammar_verification import fork_masks
+from bitmask_speculation_b200.verification import VerifiedToken
+
+
+def reference_choices(draft, rows_f32, grammar):
+    """The reference's loop: select row i under the committed grammar, advance it, stop at the
+    first mismatch, after the bonus, or once the grammar terminates (errors raise when reached)."""
+    vocab = rows_f32.shape[1]
+    out = []
+
+    def select(i):
+        mask = grammar.packed_mask_np()[None, :]
+        tok, _, st = oracle.reduce_rows(rows_f32[i:i + 1], mask)
+        if st[0] == 1:
+            raise ValueError("mask has no valid token")
+        if st[0] == 2:
+            raise ValueError("next-token logits contain NaN")
+        if not grammar.accept_token(int(tok[0])):
+            raise ValueError("grammar rejected its selected token")
+        return int(tok[0])
+
+    def choices():
+        for i, p in enumerate(draft):
+            t = select(i)
+            if t != p:
+                yield VerifiedToken(t, "correction")
+                return
+            yield VerifiedToken(p, "accepted")
+        yield VerifiedToken(select(len(draft)), "bonus" if draft else "fallback")
+
+    gen = choices()
+    while not grammar.is_terminated():
+        ev = next(gen, None)
+        if ev is None:
+            break
+        out.append(ev)
+    return out
+
+
+def make_round(rng, vocab, k, grammar, p_accept=0.85, eos_boost=False):
+    """Target rows and a draft that follows the target's own choices until a seeded mismatch."""
+    rows = rng.standard_normal((k + 1, vocab), dtype=np.float32) * np.float32(3)
+    if eos_boost:
+        rows[:, 0] += np.float32(6)
+    fork = grammar.fork()
+    draft = []
+    for i in range(k):
+        if fork.is_terminated():
+            break
+        mask = fork.packed_mask_np()[None, :]
+        tok = int(oracle.reduce_rows(rows[i:i + 1], mask)[0][0])
+        if tok < 0:
+            break
+        if rng.random() > p_accept:
+            allowed = np.asarray(fork.allowed_token_ids())
+            others = allowed[allowed != tok]
+            tok = int(rng.choice(others)) if others.size else int(rng.integers(vocab))
+        draft.append(tok)
+        if not fork.accept_token(tok):
+            break
+    return rows[: len(draft) + 1], draft
+
+
+def test_fork_masks_follow_the_draft_and_blank_unreachable_rows():
+    vocab = 4096
+    g = wl.SyntheticDFAGrammar(vocab, states=16, seed=3)
+    rng = np.random.default_rng(0)
+    for _ in range(20):
+        fork = g.fork()
+        draft, expect = [], [fork.packed_mask_np().copy()]
+        for _ in range(6):
+            allowed = fork.allowed_token_ids()
+            tok = int(rng.choice(allowed)) if allowed and rng.random() < 0.9 else int(rng.integers(vocab))
+            draft.append(tok)
+            ok = fork.accept_token(tok) and not fork.is_terminated()
+            expect.append(fork.packed_mask_np().copy() if ok else np.zeros_like(expect[0]))
+            if not ok:
+                while len(expect) < 7:
+                    draft.append(int(rng.integers(vocab)))
+                    expect.append(np.zeros_like(expect[0]))
+                break
+        out = np.full((8, (vocab + 31) // 32), 7, dtype=np.int32)
+        rows = fork_masks(g, draft, vocab, out)
+        assert rows == len(draft) + 1
+        assert np.array_equal(out[:rows], np.stack(expect[:rows]))
+        assert g.state == 0 and not g.is_terminated()  # the committed state is untouched
+
+
+def test_fork_masks_of_a_generic_grammar_from_allowed_ids():
+    class Ids:
+        vocab_size = 100
+
+        def __init__(self, allowed=(3, 64, 99)):
+            self.allowed = allowed
+
+        def fork(self):
+            return Ids(self.allowed)
+
+        def is_terminated(self):
+            return False
+
+        def allowed_token_ids(self):
+            return self.allowed
+
+        def accept_token(self, t):
+            return t in self.allowed
+
+    out = np.zeros((2, 4), dtype=np.int32)
+    fork_masks(Ids(), [64], 100, out)
+    words = out[0].view(np.uint32)
+    assert words[0] == 1 << 3 and words[2] == 1 << 0 and words[3] == 1 << 3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("vocab", [8320, 248320])
+def test_batched_grammar_verification_equals_the_lazy_reference_loop(cuda_module, vocab):
+    torch = pytest.importorskip("torch")
+    from bitmask_speculation_b200.grammar_verification import DraftForkMasks, verify_with_grammar
+    rng = np.random.default_rng(vocab)
+    buf = DraftForkMasks(vocab, 9, torch.device("cuda"))
+    for trial in range(24):
+        g_ref = wl.SyntheticDFAGrammar(vocab, states=64, seed=trial)
+        g_gpu = g_ref.fork()
+        for rnd in range(3):
+            k = int(rng.integers(0, 9))
+            rows, draft = make_round(rng, vocab, k, g_ref, eos_boost=(trial % 4 == 0))
+            bits = wl.to_bf16_bits(rows)
+            rows_bf = oracle.widen(bits, "bfloat16")
+            want = reference_choices(draft, rows_bf, g_ref)
+            logits = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
+            got = list(verify_with_grammar(draft, logits, g_gpu, buffer=buf))
+            assert got == want, (trial, rnd, draft)
+            assert (g_gpu.state, g_gpu.is_terminated()) == (g_ref.state, g_ref.is_terminated())
+            if g_ref.is_terminated():
+                break
+
+
+@pytest.mark.gpu
+def test_batch_of_sequences_in_one_round_equals_per_sequence_loops(cuda_module):
+    torch = pytest.importorskip("torch")
+    from bitmask_speculation_b200.grammar_verification import DraftForkMasks, verify_with_grammars
+    vocab, seqs, k = 151936, 48, 8
+    rng = np.random.default_rng(17)
+    refs = [wl.SyntheticDFAGrammar(vocab, states=64, seed=s % 5) for s in range(seqs)]
+    gpus = [g.fork() for g in refs]
+    buf = DraftForkMasks(vocab, seqs * (k + 1), torch.device("cuda"))
+    for rnd in range(3):
+        block = np.zeros((seqs * (k + 1), vocab), dtype=np.uint16)
+        drafts, wants = [], []
+        for s in range(seqs):
+            if refs[s].is_terminated():
+                drafts.append(())
+                wants.append([])
+                continue
+            rows, draft = make_round(rng, vocab, int(rng.integers(0, k + 1)), refs[s], eos_boost=(s % 7 == 0))
+            bits = wl.to_bf16_bits(rows)
+            block[s * (k + 1): s * (k + 1) + len(draft) + 1] = bits
+            drafts.append(draft)
+            wants.append(reference_choices(draft, oracle.widen(bits, "bfloat16"), refs[s]))
+        logits = torch.from_numpy(block.view(np.int16)).view(torch.bfloat16).cuda()
+        its = verify_with_grammars(drafts, logits, gpus, k=k, buffer=buf)
+        for s in range(seqs):
+            assert list(its[s]) == wants[s], (rnd, s)
+            assert (gpus[s].state, gpus[s].is_terminated()) == (refs[s].state, refs[s].is_terminated())
