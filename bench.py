@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["verify", "argmax", "sample", "scale", "vocab"], default="verify")
+    ap.add_argument("--workload", choices=["verify", "grammar", "argmax", "sample", "scale", "vocab"], default="verify")
     ap.add_argument("--seqs", type=int, default=256, help="verification sequences per GPU")
     ap.add_argument("--rows", type=int, default=8192, help="rows per GPU for the scale workload")
     ap.add_argument("--sample-rows", type=int, default=8,
@@ -166,7 +166,31 @@ class Workload:
         vocab = wl.VOCAB
         self.vocab = vocab
         self.words = wl.words_for(vocab)
-        if self.kind == "verify":
+        if self.kind == "grammar":
+            if args.impl == "reference":  # input synthesis on the host for the CPU arm
+                import numpy as np
+                import oracle
+
+                def select(rows, masks):
+                    bits = rows.cpu().view(torch.int16).numpy().view(np.uint16)
+                    tok, _, st = oracle.reduce_rows(bits, masks, dtype="bfloat16", threads=host_threads())
+                    return tok, st
+            else:
+                def select(rows, masks):
+                    tok, _, st = self.native.masked_reduce_batch(rows, torch.from_numpy(masks).to(device))
+                    return tok.cpu().numpy(), st.cpu().numpy()
+            (self.logits, self.masks, self.proposals, self.lengths, self.grammars,
+             self.drafts) = wl.grammar_round_torch(args.seqs, select, seed=11 + 1000 * rank, device=device)
+            self.rows = self.logits.shape[0]
+            self.batches = 1
+            self.esize = 2
+            self.dtype = "bf16"
+            from bitmask_speculation_b200.scheduling import DensityPolicy
+            self.policy = DensityPolicy().native()
+            self.name = (f"grammar: {args.seqs} sequences x (K+1)=9 rows bf16 N(0,3^2) at V={vocab}, each under a "
+                         "64-state token DFA (enum 1-8 / Bernoulli 0.3 states, EOS); drafts take the target's "
+                         "masked choice with p=0.88; fork masks of the drafts")
+        elif self.kind == "verify":
             self.logits, self.masks, self.proposals, self.lengths = wl.verify_batch_torch(
                 args.seqs, seed=3 + 1000 * rank, device=device)
             self.rows = self.logits.shape[0]
@@ -263,7 +287,7 @@ class Workload:
         self.row_counts = torch.empty(r, dtype=torch.int64, device=d)
         self.row_status = torch.empty(r, dtype=torch.int32, device=d)
         self.row_budget = torch.empty(r, dtype=torch.int32, device=d)
-        if self.kind == "verify":
+        if self.kind in ("verify", "grammar"):
             s = self.proposals.shape[0]
             self.accept = torch.empty(s, dtype=torch.int32, device=d)
             self.token = torch.empty(s, dtype=torch.int64, device=d)
@@ -278,7 +302,7 @@ class Workload:
         return self.logits_all[r0:r0 + self.rows], self.masks_all[r0:r0 + self.rows]
 
     def launches_per_step(self):
-        return 2 if self.kind in ("verify", "vocab") else 1
+        return 2 if self.kind in ("verify", "grammar", "vocab") else 1
 
     def step(self, stream_handle):
         """One hot-path step through the C ABI on inputs resident in HBM."""
@@ -288,7 +312,7 @@ class Workload:
         dev = self.device.index
         logits, masks = self._batch()
         self.step_index += 1
-        if self.kind == "verify":
+        if self.kind in ("verify", "grammar"):
             s, k = self.proposals.shape
             rc = lib.bms_verify_batch(
                 logits.data_ptr(), 1, masks.data_ptr(), s, k + 1, self.vocab, self.proposals.data_ptr(),
@@ -351,7 +375,7 @@ class Workload:
         self.step_index = 0
         logits, masks = self._batch()
         n = min(max_rows, self.rows)
-        if self.kind in ("verify", "scale", "argmax"):
+        if self.kind in ("verify", "grammar", "scale", "argmax"):
             self.step_index = 0
             self.kernel_only(self.stream_handle())
             import torch
@@ -378,7 +402,14 @@ class EndToEnd:
     def __init__(self, w: Workload):
         import torch
         self.w = w
-        if w.kind == "verify":
+        if w.kind == "grammar":
+            from bitmask_speculation_b200.grammar_verification import DraftForkMasks
+            s, k = w.proposals.shape
+            self.k = k
+            self.buf = DraftForkMasks(w.vocab, w.rows, w.device)
+            self.h2d = w.rows * w.words * 4 + s * k * 8 + s * 4
+            self.d2h = w.rows * (8 + 8 + 4 + 4) + s * (4 + 8 + 4 + 4)
+        elif w.kind == "verify":
             self.h_masks = w.masks.cpu().pin_memory()
             self.h_prop = w.proposals.cpu().pin_memory()
             self.h_len = w.lengths.cpu().pin_memory()
@@ -406,7 +437,13 @@ class EndToEnd:
 
     def step(self):
         w = self.w
-        if w.kind == "verify":
+        if w.kind == "grammar":
+            # The whole round through the public API: fork masks filled on the host, one H2D, one
+            # launch pair, one sync, events replayed on fresh forks of the committed grammars.
+            from bitmask_speculation_b200.grammar_verification import verify_with_grammars
+            its = verify_with_grammars(w.drafts, w.logits, [g.fork() for g in w.grammars], k=self.k, buffer=self.buf)
+            self.events = sum(len(list(it)) for it in its)
+        elif w.kind == "verify":
             from bitmask_speculation_b200.verification import verify_batch
             self.d_masks.copy_(self.h_masks, non_blocking=True)
             self.d_prop.copy_(self.h_prop, non_blocking=True)
@@ -450,6 +487,28 @@ def timed_loop(fn, n, device, dist=None):
         seconds = float(t.item())
         dist.barrier()
     return seconds
+
+
+def cpu_baseline_grammar(w: Workload, budget_s=10.0):
+    """The reference's lazy per-row loop restated on the oracle (one masked argmax per consumed
+    row, the grammar advanced in turn) over whole sequences of the round, for ~budget_s seconds;
+    rows/s counts the round's K+1 rows per sequence, like the device path."""
+    import numpy as np
+    import torch
+    import oracle
+    k = w.proposals.shape[1]
+    bits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
+    seqs = len(w.drafts)
+    t0 = time.perf_counter()
+    done = 0
+    while time.perf_counter() - t0 < budget_s:
+        s = done % seqs
+        rows = bits[s * (k + 1): s * (k + 1) + len(w.drafts[s]) + 1]
+        if not w.grammars[s].is_terminated():
+            oracle.grammar_choices(w.drafts[s], rows, w.grammars[s].fork(), dtype="bfloat16")
+        done += 1
+    elapsed = time.perf_counter() - t0
+    return done * (k + 1) / elapsed, 1, f"{done} sequences of the round (reference loop, one thread)"
 
 
 def cpu_baseline_verify(w: Workload, budget_s=8.0):
@@ -518,7 +577,24 @@ def run_reference_arm(args):
         torch.cuda.set_device(device)
     threads = host_threads()
     w = Workload(args, 0, device)
-    if args.workload == "verify":
+    if args.workload == "grammar":
+        k = w.proposals.shape[1]
+        bits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
+
+        def step():
+            # Every sequence of the round through the reference's lazy loop, sequences spread
+            # over the host threads (each loop is sequential in its rows).
+            from concurrent.futures import ThreadPoolExecutor
+
+            def one(s):
+                rows = bits[s * (k + 1): s * (k + 1) + len(w.drafts[s]) + 1]
+                if not w.grammars[s].is_terminated():
+                    oracle.grammar_choices(w.drafts[s], rows, w.grammars[s].fork(), dtype="bfloat16")
+            with ThreadPoolExecutor(threads) as ex:
+                list(ex.map(one, range(len(w.drafts))))
+        rows_per_step = w.rows
+        sample = f"full grammar verification round ({len(w.drafts)} sequences, {rows_per_step} rows) per step"
+    elif args.workload == "verify":
         host_logits = w.logits.cpu().view(torch.int16).numpy().view(np.uint16)
         host_masks = w.masks.cpu().numpy()
         props, lens = w.proposals.cpu().numpy(), w.lengths.cpu().numpy()
@@ -610,7 +686,10 @@ def run_b200_arm(args):
             e2e = {"value": w.rows * world * args.steps / etime, "unit": "rows/s",
                    "h2d_bytes_per_step": e.h2d, "d2h_bytes_per_step": e.d2h,
                    "wall_value": w.rows * world * args.steps / wall,
-                   "path": ("verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
+                   "path": ("grammar_verification.verify_with_grammars (public API): fork masks of every "
+                            "draft filled into pinned memory on the host, one H2D, one launch pair, one sync, "
+                            "events replayed on the sequences' grammars every step" if w.kind == "grammar" else
+                            "verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
                             "device-resident logits, results D2H every step")}
 
     total_rows = w.rows if w.kind == "vocab" else w.rows * world  # vocab shards split the same rows
@@ -648,7 +727,9 @@ def run_b200_arm(args):
     if e2e is not None:
         line["e2e"] = e2e
     if not args.no_cpu_baseline and world == 1:
-        if w.kind == "verify":
+        if w.kind == "grammar":
+            v, cores, sample = cpu_baseline_grammar(w)
+        elif w.kind == "verify":
             v, cores, sample = cpu_baseline_verify(w)
         else:
             v, cores, sample = cpu_baseline_rows(w)

@@ -298,6 +298,10 @@ class SyntheticDFAGrammar:
     def allowed_token_ids(self):
         return () if self._terminated else tuple(int(t) for t in self._tables[1][self._state])
 
+    def allowed_ids_np(self) -> np.ndarray:
+        """Allowed token IDs of the current state as a numpy array (read-only)."""
+        return np.zeros(0, dtype=np.int64) if self._terminated else self._tables[1][self._state]
+
     def packed_mask(self):
         import torch
         words = self._tables[0][self._state]
@@ -326,3 +330,66 @@ class SyntheticDFAGrammar:
     def fork(self) -> "SyntheticDFAGrammar":
         return SyntheticDFAGrammar(self._vocab, _tables=self._tables, _state=self._state,
                                    _terminated=self._terminated)
+
+
+def grammar_round_torch(seqs: int, select, vocab: int = VOCAB, k: int = DRAFT_K, seed: int = 11, device="cuda",
+                        p_accept: float = 0.88):
+    """One grammar-constrained verification round of ``seqs`` sequences (input synthesis).
+
+    Each sequence gets a ``SyntheticDFAGrammar`` (shared 64-state tables) advanced by a few random
+    non-terminating tokens, target rows bf16 N(0, 3^2) [seqs*(k+1), vocab] on the device, and a
+    draft that takes the target's own masked choice (``select(rows, masks) -> (tokens, status)``
+    numpy arrays, for device rows [seqs, vocab] and int32 mask rows) with probability ``p_accept``
+    per position and another allowed token otherwise.  Returns
+    (logits, fork masks [seqs*(k+1), W] on the device, proposals int64 [seqs, k], lengths int32
+    [seqs], the sequences' committed grammars, the drafts).
+    """
+    import torch
+    rng = np.random.default_rng(seed)
+    base = SyntheticDFAGrammar(vocab, states=64, seed=seed)
+    eos = base._tables[2]
+    grammars = []
+    for _ in range(seqs):
+        g = base.fork()
+        for _ in range(int(rng.integers(0, 6))):
+            ids = g.allowed_ids_np()
+            ids = ids[~np.isin(ids, list(eos))]
+            if ids.size:
+                g.accept_token(int(rng.choice(ids)))
+        grammars.append(g)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    logits = (torch.randn(seqs * (k + 1), vocab, generator=gen, device=device) * 3).to(torch.bfloat16)
+    words = words_for(vocab)
+    masks = np.zeros((seqs * (k + 1), words), dtype=np.int32)
+    forks = [g.fork() for g in grammars]
+    live = [not f.is_terminated() for f in forks]
+    drafts = [[] for _ in range(seqs)]
+    for i in range(k + 1):
+        for s in range(seqs):
+            masks[s * (k + 1) + i] = forks[s].packed_mask_np() if live[s] else 0
+        if i == k:
+            break
+        rows = torch.arange(seqs, device=device) * (k + 1) + i
+        tok, st = select(logits[rows].contiguous(), masks[i::k + 1].copy())
+        for s in range(seqs):
+            if not live[s]:
+                continue
+            if st[s] != 0:
+                live[s] = False
+                continue
+            t = int(tok[s])
+            if rng.random() > p_accept:
+                ids = forks[s].allowed_ids_np()
+                ids = ids[ids != t]
+                if ids.size:
+                    t = int(rng.choice(ids))
+            drafts[s].append(t)
+            if not forks[s].accept_token(t) or forks[s].is_terminated():
+                live[s] = False
+    proposals = np.zeros((seqs, k), dtype=np.int64)
+    lengths = np.zeros(seqs, dtype=np.int32)
+    for s, d in enumerate(drafts):
+        proposals[s, : len(d)] = d
+        lengths[s] = len(d)
+    return (logits, torch.from_numpy(masks).to(device), torch.from_numpy(proposals).to(device),
+            torch.from_numpy(lengths).to(device), grammars, [tuple(d) for d in drafts])

@@ -180,3 +180,41 @@ def widen(logits, dtype: str) -> np.ndarray:
     out = np.empty(a.shape, np.float32)
     _load().orc_widen(_ptr(a), code, a.size, _ptr(out))
     return out
+
+
+def grammar_choices(draft, rows, grammar, *, dtype: str | None = None):
+    """The reference's grammar-constrained verification loop (models/transformers.py:181-201:
+    ``_choices`` + ``constrained_choices`` over decoding/verification.py:18-48 ``verify_prefix``),
+    restated on the oracle: row i is selected by the masked argmax under the committed grammar's
+    packed mask, which is then advanced; stop at the first mismatch, after the bonus, or once the
+    grammar terminates.  ``rows`` are the K+1 target rows (float32 values, or bit patterns of
+    ``dtype``).  Returns a list of (token, kind); a failed row raises ``ValueError`` when reached.
+    """
+    def select(i):
+        tok, _, st = reduce_rows(rows[i:i + 1], np.asarray(grammar.packed_mask_np())[None, :], dtype=dtype,
+                                 threads=1)
+        if st[0] == 1:
+            raise ValueError("mask has no valid token")
+        if st[0] == 2:
+            raise ValueError("next-token logits contain NaN")
+        if not grammar.accept_token(int(tok[0])):
+            raise ValueError("grammar rejected its selected token")
+        return int(tok[0])
+
+    def choices():
+        for i, p in enumerate(draft):
+            t = select(i)
+            if t != p:
+                yield (t, "correction")
+                return
+            yield (p, "accepted")
+        yield (select(len(draft)), "bonus" if draft else "fallback")
+
+    out = []
+    gen = choices()
+    while not grammar.is_terminated():
+        ev = next(gen, None)
+        if ev is None:
+            break
+        out.append(ev)
+    return out

@@ -13,38 +13,8 @@ from bitmask_speculation_b200.verification import VerifiedToken
 
 
 def reference_choices(draft, rows_f32, grammar):
-    """The reference's loop: select row i under the committed grammar, advance it, stop at the
-    first mismatch, after the bonus, or once the grammar terminates (errors raise when reached)."""
-    vocab = rows_f32.shape[1]
-    out = []
-
-    def select(i):
-        mask = grammar.packed_mask_np()[None, :]
-        tok, _, st = oracle.reduce_rows(rows_f32[i:i + 1], mask)
-        if st[0] == 1:
-            raise ValueError("mask has no valid token")
-        if st[0] == 2:
-            raise ValueError("next-token logits contain NaN")
-        if not grammar.accept_token(int(tok[0])):
-            raise ValueError("grammar rejected its selected token")
-        return int(tok[0])
-
-    def choices():
-        for i, p in enumerate(draft):
-            t = select(i)
-            if t != p:
-                yield VerifiedToken(t, "correction")
-                return
-            yield VerifiedToken(p, "accepted")
-        yield VerifiedToken(select(len(draft)), "bonus" if draft else "fallback")
-
-    gen = choices()
-    while not grammar.is_terminated():
-        ev = next(gen, None)
-        if ev is None:
-            break
-        out.append(ev)
-    return out
+    """The reference's lazy loop, restated on the oracle (``oracle.grammar_choices``)."""
+    return [VerifiedToken(t, k) for t, k in oracle.grammar_choices(draft, rows_f32, grammar)]
 
 
 def make_round(rng, vocab, k, grammar, p_accept=0.85, eos_boost=False):
