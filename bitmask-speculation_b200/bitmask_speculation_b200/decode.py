@@ -1,0 +1,289 @@
+"""End-to-end constrained decoding harness (the end-to-end measurement configuration).
+
+Random-init Qwen-style decoders in plain PyTorch stand in for the reference's Transformers models
+(models/transformers.py), and the reference's request loops are restated over this library's
+kernels:
+
+* ``constrained_greedy`` -- decoding/greedy.py:51-92 ``greedy_decode`` with a grammar: one target
+  forward and one masked argmax per token, the grammar advanced by each choice;
+* ``speculative_c4`` -- decoding/speculative.py:96-208 ``speculative_decode`` with
+  ``constrain_draft=True`` and a ``DensityPolicy`` (the reference's c4 mode): per round the density
+  of the committed grammar sets K, the draft model proposes up to K tokens greedily on a grammar
+  fork (decoding/speculative.py:63-95), one target forward scores prefix + draft, and the whole
+  round is verified by ``grammar_verification.verify_with_grammar`` (one launch pair, one sync)
+  instead of the reference's per-row loop.
+
+Speculative decoding with greedy verification reproduces target-only greedy decoding token for
+token; ``tests/test_gpu_decode.py`` checks that, and ``bench.py --workload decode`` measures it.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .grammar_verification import DraftForkMasks, verify_with_grammar
+from .scheduling import DensityPolicy
+
+
+def _torch():
+    import torch
+    return torch
+
+
+# ---------------------------------------------------------------- model
+def build_decoder(vocab: int, *, layers: int, dim: int, heads: int, kv_heads: int | None = None,
+                  ffn: int | None = None, dtype=None, device="cuda", seed: int = 0):
+    """A random-init Qwen-style decoder: token embedding, ``layers`` blocks of RMSNorm ->
+    grouped-query causal attention with rotary positions -> RMSNorm -> SwiGLU MLP, final RMSNorm and
+    an untied LM head.  Weights are N(0, 0.02^2) from ``seed``."""
+    torch = _torch()
+    nn = torch.nn
+    dtype = torch.bfloat16 if dtype is None else dtype
+    kv_heads = kv_heads or max(1, heads // 4)
+    ffn = ffn or 3 * dim
+    head_dim = dim // heads
+
+    class RMSNorm(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(dim))
+
+        def forward(self, x):
+            v = x.float()
+            v = v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-6)
+            return (v * self.weight.float()).to(x.dtype)
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.n1, self.n2 = RMSNorm(), RMSNorm()
+            self.q = nn.Linear(dim, heads * head_dim, bias=False)
+            self.kv = nn.Linear(dim, 2 * kv_heads * head_dim, bias=False)
+            self.o = nn.Linear(heads * head_dim, dim, bias=False)
+            self.up = nn.Linear(dim, 2 * ffn, bias=False)
+            self.down = nn.Linear(ffn, dim, bias=False)
+
+        def forward(self, x, cos, sin):
+            t = x.shape[0]
+            h = self.n1(x)
+            q = self.q(h).view(t, heads, head_dim).transpose(0, 1)
+            k, v = self.kv(h).view(t, 2, kv_heads, head_dim).unbind(1)
+            k, v = k.transpose(0, 1), v.transpose(0, 1)
+            q, k = _rotate(q, cos, sin), _rotate(k, cos, sin)
+            k = k.repeat_interleave(heads // kv_heads, 0)
+            v = v.repeat_interleave(heads // kv_heads, 0)
+            a = torch.nn.functional.scaled_dot_product_attention(q[None], k[None], v[None], is_causal=True)[0]
+            x = x + self.o(a.transpose(0, 1).reshape(t, heads * head_dim))
+            g, u = self.up(self.n2(x)).chunk(2, -1)
+            return x + self.down(torch.nn.functional.silu(g) * u)
+
+    class Decoder(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.vocab_size = vocab
+            self.embed = nn.Embedding(vocab, dim)
+            self.blocks = nn.ModuleList(Block() for _ in range(layers))
+            self.norm = RMSNorm()
+            self.head = nn.Linear(dim, vocab, bias=False)
+            inv = 1.0 / (1e6 ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+            self.register_buffer("inv_freq", inv.float(), persistent=False)
+
+        @torch.inference_mode()
+        def logits(self, tokens, first: int, rows: int):
+            """Logits of positions [first, first + rows) after one forward over ``tokens``.  The
+            sequence is padded at the end to a multiple of 64 tokens (causal attention: padding
+            never reaches earlier positions) so that kernel shapes repeat across calls."""
+            n = len(tokens)
+            padded = list(tokens) + [0] * (-n % 64)
+            ids = torch.tensor(padded, dtype=torch.long).to(self.head.weight.device, non_blocking=True)
+            pos = torch.arange(ids.shape[0], device=ids.device, dtype=torch.float32)
+            ang = pos[:, None] * self.inv_freq[None, :]
+            cos, sin = ang.cos().to(self.head.weight.dtype), ang.sin().to(self.head.weight.dtype)
+            x = self.embed(ids)
+            for b in self.blocks:
+                x = b(x, cos, sin)
+            return self.head(self.norm(x[first:first + rows])).contiguous()
+
+    gen = torch.Generator().manual_seed(seed)
+    model = Decoder()
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "weight" in name and p.dim() == 2:
+                p.copy_(torch.randn(p.shape, generator=gen) * 0.02)
+    return model.to(device=device, dtype=dtype).eval()
+
+
+def _rotate(x, cos, sin):
+    half = x.shape[-1] // 2
+    a, b = x[..., :half], x[..., half:]
+    return _torch().cat((a * cos - b * sin, a * sin + b * cos), -1)
+
+
+# ---------------------------------------------------------------- selection
+class _Selector:
+    """Masked argmax of one row under a grammar's current mask (the reference's _select_token:
+    select without advancing, then advance; NaN or an empty mask raise).  ``seconds`` accumulates
+    the host time spent selecting (a synchronizing call, so it covers the device work)."""
+
+    seconds = 0.0
+
+    def __init__(self, vocab: int, device):
+        torch = _torch()
+        from .kernels._extension import load_extension
+        self.native = load_extension()
+        self.words = (vocab + 31) // 32
+        self.host = torch.zeros(self.words, dtype=torch.int32).pin_memory()
+        self.dev = torch.empty(self.words, dtype=torch.int32, device=device)
+        self._np = self.host.numpy()
+
+    def __call__(self, row, grammar) -> int:
+        import time
+        from .kernels.cuda import masked_argmax
+        t0 = time.perf_counter()
+        self._np[:] = grammar.packed_mask_np()
+        self.dev.copy_(self.host, non_blocking=True)
+        token = int(masked_argmax(row, self.dev).item())
+        self.seconds += time.perf_counter() - t0
+        if not grammar.accept_token(token):
+            raise ValueError("grammar rejected its selected token")
+        return token
+
+
+@dataclass(frozen=True, slots=True)
+class DecodeResult:
+    token_ids: tuple
+    stop_reason: str
+    eos_token_id: int | None = None
+    rounds: int = 0
+    proposed: int = 0
+    accepted: int = 0
+    select_seconds: float = field(default=0.0, compare=False)  # host time in selection and verification calls
+
+
+# ---------------------------------------------------------------- request loops
+def constrained_greedy(target, prompt, grammar, *, max_new_tokens: int, eos=(), selector=None) -> DecodeResult:
+    """Target-only constrained greedy decoding (decoding/greedy.py:51-92)."""
+    prompt = tuple(int(t) for t in prompt)
+    eos = frozenset(int(t) for t in eos)
+    sel = selector or _Selector(target.vocab_size, target.head.weight.device)
+    out: list[int] = []
+
+    def finish(reason, token=None):
+        return DecodeResult(tuple(out), reason, token, select_seconds=sel.seconds)
+
+    for _ in range(max_new_tokens):
+        if grammar.is_terminated():
+            return finish("grammar")
+        seq = prompt + tuple(out)
+        token = sel(target.logits(seq, len(seq) - 1, 1)[0], grammar)
+        if token in eos:
+            return finish("eos", token)
+        out.append(token)
+        if grammar.is_terminated():
+            return finish("grammar")
+    return finish("length")
+
+
+def _lazy_rounds(draft, rows, grammar, sel):
+    """The reference's per-row verification (models/transformers.py:181-201 ``_choices`` over
+    decoding/verification.py:18-48): row i selected under the committed grammar when the event
+    is requested, stopping at the first mismatch or at termination."""
+    from .verification import VerifiedToken
+
+    def choices():
+        for i, p in enumerate(draft):
+            t = sel(rows[i], grammar)
+            if t != p:
+                yield VerifiedToken(t, "correction")
+                return
+            yield VerifiedToken(p, "accepted")
+        yield VerifiedToken(sel(rows[len(draft)], grammar), "bonus" if draft else "fallback")
+
+    gen = choices()
+    while not grammar.is_terminated():
+        event = next(gen, None)
+        if event is None:
+            return
+        yield event
+
+
+def speculative_c4(target, draft, prompt, grammar, *, max_new_tokens: int, eos=(), policy=None,
+                   selector=None, buffer=None, verify: str = "batched") -> DecodeResult:
+    """Density-scheduled constrained speculative decoding (decoding/speculative.py:96-208 with
+    constrain_draft=True and a DensityPolicy).  ``verify="batched"`` verifies each round with
+    ``verify_with_grammar`` (one launch pair, one sync); ``"lazy"`` with the reference's per-row
+    loop (one masked argmax and one sync per consumed row) on the same target rows."""
+    prompt = tuple(int(t) for t in prompt)
+    eos = frozenset(int(t) for t in eos)
+    policy = DensityPolicy() if policy is None else policy
+    device = target.head.weight.device
+    sel = selector or _Selector(target.vocab_size, device)
+    buf = buffer or DraftForkMasks(target.vocab_size, policy.max_budget + 1, device)
+    out: list[int] = []
+    rounds = proposed = accepted = 0
+
+    verify_seconds = 0.0
+
+    def finish(reason, token=None):
+        return DecodeResult(tuple(out), reason, token, rounds, proposed, accepted, sel.seconds + verify_seconds)
+
+    while len(out) < max_new_tokens:
+        if grammar.is_terminated():
+            return finish("grammar")
+        prefix = prompt + tuple(out)
+        budget = min(policy.budget(grammar.mask_density()), max_new_tokens - len(out))
+        # Draft on a fork (decoding/speculative.py:63-95): stop before a draft EOS or at the fork's
+        # termination; the fork is discarded before verification.
+        branch = grammar.fork()
+        proposals: list[int] = []
+        for _ in range(budget):
+            if branch.is_terminated():
+                break
+            ctx = prefix + tuple(proposals)
+            token = sel(draft.logits(ctx, len(ctx) - 1, 1)[0], branch)
+            if token in eos:
+                break
+            proposals.append(token)
+        proposed += len(proposals)
+        rounds += 1
+        seq = prefix + tuple(proposals)
+        rows = target.logits(seq, len(prefix) - 1, len(proposals) + 1)
+        before = len(out)
+        if verify == "batched":
+            import time
+            t0 = time.perf_counter()
+            events = verify_with_grammar(proposals, rows, grammar, buffer=buf, policy=policy)
+            verify_seconds += time.perf_counter() - t0
+        else:
+            events = _lazy_rounds(tuple(proposals), rows, grammar, sel)
+        for event in events:
+            accepted += event.kind == "accepted"
+            if event.token_id in eos:
+                return finish("eos", event.token_id)
+            out.append(event.token_id)
+            if grammar.is_terminated():
+                return finish("grammar")
+            if len(out) == max_new_tokens:
+                return finish("length")
+        if len(out) == before:
+            raise RuntimeError("target verification made no progress")
+    return finish("length")
+
+
+def random_prompts(n: int, length: int, vocab: int, seed: int = 0) -> list[tuple[int, ...]]:
+    rng = np.random.default_rng(seed)
+    return [tuple(int(t) for t in rng.integers(1, vocab, size=length)) for _ in range(n)]
+
+
+def config_models(vocab: int, device="cuda", dtype=None, seed: int = 0):
+    """The end-to-end configuration's target (4 layers, d=1024, 16 heads) and draft (1 layer,
+    d=512), random-init, bf16 by default."""
+    target = build_decoder(vocab, layers=4, dim=1024, heads=16, dtype=dtype, device=device, seed=seed)
+    draft = build_decoder(vocab, layers=1, dim=512, heads=8, dtype=dtype, device=device, seed=seed + 1)
+    return target, draft
+
+
+__all__ = ["build_decoder", "config_models", "constrained_greedy", "speculative_c4", "random_prompts",
+           "DecodeResult"]
