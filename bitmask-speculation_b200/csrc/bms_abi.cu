@@ -288,9 +288,11 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
     cfg.stream = stream;
-    // Only a grid that fills every resident slot: a smaller one, dispatched early into the slots
-    // its predecessor leaves free, would be spread unevenly over the SMs.
-    const bool full = plan.clusters >= info->max_clusters[cluster_index(plan.cluster)];
+    // A grid that fills every resident slot, or one of at most one CTA per SM (latency-bound: an
+    // early start hides ~1-2 us of launch).  Grids in between, dispatched early into the slots
+    // their predecessor leaves free, would be spread unevenly over the SMs.
+    const bool full = plan.clusters >= info->max_clusters[cluster_index(plan.cluster)] ||
+                      plan.cluster * plan.clusters <= info->sms;
     cfg.attrs = full ? attr : attr + 1;
     cfg.numAttrs = (full ? 1 : 0) + (plan.cluster > 1 ? 1 : 0);
     BMS_CUDA(cudaLaunchKernelEx(&cfg, select_rows_kernel<T, kSample, kBulk, kStages>, p), "selection launch");
