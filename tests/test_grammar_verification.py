@@ -142,3 +142,23 @@ def test_batch_of_sequences_in_one_round_equals_per_sequence_loops(cuda_module):
         for s in range(seqs):
             assert list(its[s]) == wants[s], (rnd, s)
             assert (gpus[s].state, gpus[s].is_terminated()) == (refs[s].state, refs[s].is_terminated())
+
+
+def test_grammar_round_synthesis_on_cpu():
+    """The bench's round synthesis: fork-mask rows agree with fork_masks, drafts follow grammars."""
+    torch = pytest.importorskip("torch")
+    from bitmask_speculation_b200.grammar_verification import fork_masks
+
+    def select(rows, masks):
+        bits = rows.view(torch.int16).numpy().view(np.uint16)
+        tok, _, st = oracle.reduce_rows(bits, masks, dtype="bfloat16")
+        return tok, st
+
+    vocab, seqs, k = 8320, 12, 8
+    logits, masks, prop, lens, grammars, drafts = wl.grammar_round_torch(seqs, select, vocab=vocab, device="cpu")
+    assert logits.shape == (seqs * (k + 1), vocab) and masks.shape == (seqs * (k + 1), (vocab + 31) // 32)
+    buf = np.zeros((k + 1, masks.shape[1]), np.int32)
+    for s in range(seqs):
+        assert lens[s].item() == len(drafts[s]) and prop[s, : len(drafts[s])].tolist() == list(drafts[s])
+        rows = fork_masks(grammars[s], drafts[s], vocab, buf)
+        assert np.array_equal(buf[:rows], masks.numpy()[s * (k + 1): s * (k + 1) + rows])
