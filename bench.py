@@ -322,7 +322,7 @@ class Workload:
                 self.lengths.data_ptr(), ctypes.byref(self.policy), self.row_tokens.data_ptr(),
                 self.row_counts.data_ptr(), self.row_status.data_ptr(), self.row_budget.data_ptr(),
                 self.accept.data_ptr(), self.token.data_ptr(), self.kindout.data_ptr(),
-                self.seq_status.data_ptr(), *self.workspace(), dev, stream_handle)
+                self.seq_status.data_ptr(), None, 0, *self.workspace(), dev, stream_handle)
         elif self.kind == "vocab":
             from bitmask_speculation_b200.sharding import vocab_sharded_select
             self.row_tokens, self.row_counts, self.row_status = vocab_sharded_select(logits, masks, self.vocab)
@@ -406,11 +406,16 @@ class EndToEnd:
         import torch
         self.w = w
         if w.kind == "grammar":
-            from bitmask_speculation_b200.grammar_verification import DraftForkMasks
+            from bitmask_speculation_b200.grammar_verification import DeviceMaskTable, DraftForkMasks
             s, k = w.proposals.shape
             self.k = k
             self.buf = DraftForkMasks(w.vocab, w.rows, w.device)
-            self.h2d = w.rows * w.words * 4 + s * k * 8 + s * 4
+            # Device-resident masks: the grammars' state masks live on the device; a round uploads
+            # one int32 table index per row.  ``use_table = False`` uploads every row's mask words.
+            self.table = DeviceMaskTable.for_grammar(w.grammars[0], w.rows, w.device)
+            self.use_table = True
+            self.h2d = w.rows * 4 + s * k * 8 + s * 4
+            self.h2d_masks = w.rows * w.words * 4 + s * k * 8 + s * 4
             self.d2h = w.rows * (8 + 8 + 4 + 4) + s * (4 + 8 + 4 + 4)
         elif w.kind == "verify":
             self.h_masks = w.masks.cpu().pin_memory()
@@ -453,7 +458,8 @@ class EndToEnd:
             # The whole round through the public API: fork masks filled on the host, one H2D, one
             # launch pair, one sync, events replayed on fresh forks of the committed grammars.
             from bitmask_speculation_b200.grammar_verification import verify_with_grammars
-            its = verify_with_grammars(w.drafts, w.logits, [g.fork() for g in w.grammars], k=self.k, buffer=self.buf)
+            its = verify_with_grammars(w.drafts, w.logits, [g.fork() for g in w.grammars], k=self.k,
+                                       buffer=self.buf, table=self.table if self.use_table else None)
             self.events = sum(len(list(it)) for it in its)
         elif w.kind == "verify":
             import torch
@@ -704,12 +710,21 @@ def run_b200_arm(args):
             t0 = time.perf_counter()
             etime = timed_loop(e.step, args.steps, device, dist)
             wall = time.perf_counter() - t0
+            if w.kind == "grammar":  # the same round uploading every row's mask words instead
+                e.use_table = False
+                e.step()
+                mtime = timed_loop(e.step, args.steps, device, dist)
+                e.use_table = True
+                uploaded = {"value": w.rows * world * args.steps / mtime, "unit": "rows/s",
+                            "h2d_bytes_per_step": e.h2d_masks, "d2h_bytes_per_step": e.d2h,
+                            "path": "verify_with_grammars with fork masks filled on the host and uploaded"}
             e2e = {"value": w.rows * world * args.steps / etime, "unit": "rows/s",
                    "h2d_bytes_per_step": e.h2d, "d2h_bytes_per_step": e.d2h,
                    "wall_value": w.rows * world * args.steps / wall,
-                   "path": ("grammar_verification.verify_with_grammars (public API): fork masks of every "
-                            "draft filled into pinned memory on the host, one H2D, one launch pair, one sync, "
-                            "events replayed on the sequences' grammars every step" if w.kind == "grammar" else
+                   "path": ("grammar_verification.verify_with_grammars (public API) with a device-resident "
+                            "mask table: fork state indices computed on the host, one H2D of 4 bytes per row, "
+                            "one launch pair, one sync, events replayed on the sequences' grammars every step"
+                            if w.kind == "grammar" else
                             "verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
                             "device-resident logits, results D2H every step; each step's upload on a copy "
                             "stream overlaps the previous step's kernels (two input buffers)")}
@@ -748,6 +763,8 @@ def run_b200_arm(args):
     }
     if e2e is not None:
         line["e2e"] = e2e
+        if w.kind == "grammar":
+            line["e2e_uploaded_masks"] = uploaded
     if not args.no_cpu_baseline and world == 1:
         if w.kind == "grammar":
             v, cores, sample = cpu_baseline_grammar(w)

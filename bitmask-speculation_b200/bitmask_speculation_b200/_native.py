@@ -52,7 +52,7 @@ def _declare(lib) -> None:
         "bms_masked_sample_batch": [p, i32, p, i64, i64, f64, p, p, p, p, p, i64, i32, p],
         "bms_mask_budget": [p, i64, i64, ctypes.POINTER(Policy), p, p, p, i32, p],
         "bms_verify_batch": [p, i32, p, i64, i64, i64, p, p, ctypes.POINTER(Policy), p, p, p, p,
-                             p, p, p, p, p, i64, i32, p],
+                             p, p, p, p, p, i64, p, i64, i32, p],
         "bms_set_launch_override": [i32, i32],
         "bms_shard_partials": [p, i32, p, i64, i64, i64, i64, f64, p, p, i64, i32, p],
         "bms_shard_merge": [p, i32, i32, i64, f64, p, p, i32, p, i64, i64, i64, p, i64, p, p, p, i32, p],

@@ -58,6 +58,45 @@ def fork_masks(grammar, draft: Sequence[int], vocab: int, out: np.ndarray) -> in
     return rows
 
 
+def fork_state_indices(grammar, draft: Sequence[int], out: np.ndarray, empty: int) -> int:
+    """Like ``fork_masks`` for a grammar with a finite state set (``mask_table()`` /
+    ``state_index()``): write into ``out[: len(draft) + 1]`` the table rows of the fork states,
+    ``empty`` for rows a fork cannot reach.  Returns the rows."""
+    rows = len(draft) + 1
+    fork = grammar.fork()
+    idx = fork.state_index()
+    out[0] = idx if idx >= 0 else empty
+    live = idx >= 0
+    for i, proposal in enumerate(draft):
+        live = live and fork.accept_token(proposal) and not fork.is_terminated()
+        out[i + 1] = fork.state_index() if live else empty
+    return rows
+
+
+class DeviceMaskTable:
+    """Device-resident masks of a grammar's finite state set (plus one empty row), so that a round
+    uploads one int32 table index per row instead of its mask words."""
+
+    def __init__(self, table: np.ndarray, max_rows: int, device):
+        import torch
+        table = np.ascontiguousarray(table, dtype=np.int32)
+        self.empty = table.shape[0]
+        full = np.vstack([table, np.zeros((1, table.shape[1]), dtype=np.int32)])
+        self.table = torch.from_numpy(full).to(device)
+        self.host = torch.zeros(max_rows, dtype=torch.int32).pin_memory()
+        self.device = torch.empty(max_rows, dtype=torch.int32, device=device)
+        self._host_np = self.host.numpy()
+
+    @classmethod
+    def for_grammar(cls, grammar, max_rows: int, device) -> "DeviceMaskTable":
+        return cls(grammar.mask_table(), max_rows, device)
+
+    def upload(self, rows: int):
+        dev = self.device[:rows]
+        dev.copy_(self.host[:rows], non_blocking=True)
+        return dev
+
+
 class DraftForkMasks:
     """Pinned host staging and device buffer for the packed masks of K+1 draft-fork states."""
 
@@ -119,14 +158,16 @@ def verify_with_grammar(draft: Sequence[int], logits, grammar, *, buffer: DraftF
 
 
 def verify_with_grammars(drafts: Sequence[Sequence[int]], logits, grammars, *, k: int,
-                         buffer: DraftForkMasks | None = None, policy=None) -> list[Iterator[VerifiedToken]]:
+                         buffer: DraftForkMasks | None = None, table: DeviceMaskTable | None = None,
+                         policy=None) -> list[Iterator[VerifiedToken]]:
     """One verification round for S sequences: one host-to-device mask copy, one ``verify_batch``
     launch pair and one host synchronization for the whole batch.
 
     ``logits`` [S*(k+1), V] on the device, row ``s*(k+1) + i`` predicting proposal i of sequence s
     (row ``s*(k+1) + len(drafts[s])`` its bonus); ``grammars[s]`` the committed grammar of sequence
     s, advanced by its iterator as the reference's loop would.  Sequences whose grammar has
-    terminated get an empty iterator.
+    terminated get an empty iterator.  With ``table`` (grammars sharing one finite state set, see
+    ``DeviceMaskTable``) the round uploads one int32 table index per row instead of mask words.
     """
     import torch
     seqs = len(drafts)
@@ -138,23 +179,35 @@ def verify_with_grammars(drafts: Sequence[Sequence[int]], logits, grammars, *, k
     drafts = [tuple(token_id(t, vocab, "proposal token") for t in d) for d in drafts]
     if any(len(d) > k for d in drafts):
         raise ValueError("a draft is longer than k")
-    buf = buffer if buffer is not None else DraftForkMasks(vocab, seqs * (k + 1), logits.device)
-    if buf.host.shape[0] < seqs * (k + 1):
-        raise ValueError("buffer too small for the batch")
+    rows = seqs * (k + 1)
+    if table is None:
+        buf = buffer if buffer is not None else DraftForkMasks(vocab, rows, logits.device)
+        if buf.host.shape[0] < rows:
+            raise ValueError("buffer too small for the batch")
+    elif table.host.shape[0] < rows or table.table.shape[1] != (vocab + 31) // 32:
+        raise ValueError("mask table too small for the batch or of another vocabulary")
     prop = np.zeros((seqs, k), dtype=np.int64)
     lens = np.zeros(seqs, dtype=np.int32)
     for s, (d, g) in enumerate(zip(drafts, grammars)):
         if getattr(g, "vocab_size", vocab) != vocab:
             raise ValueError("grammar and model vocabularies differ")
         base = s * (k + 1)
-        fork_masks(g, d, vocab, buf._host_np[base:base + k + 1])
-        buf._host_np[base + len(d) + 1:base + k + 1] = 0
+        if table is None:
+            fork_masks(g, d, vocab, buf._host_np[base:base + k + 1])
+            buf._host_np[base + len(d) + 1:base + k + 1] = 0
+        else:
+            fork_state_indices(g, d, table._host_np[base:base + k + 1], table.empty)
+            table._host_np[base + len(d) + 1:base + k + 1] = table.empty
         prop[s, : len(d)] = d
         lens[s] = len(d)
-    masks = buf.upload(seqs * (k + 1))
     dev = logits.device
-    host = verify_batch(logits, masks, torch.from_numpy(prop).to(dev, non_blocking=True),
-                        torch.from_numpy(lens).to(dev, non_blocking=True), policy=policy).to_host()
+    prop_d = torch.from_numpy(prop).to(dev, non_blocking=True)
+    lens_d = torch.from_numpy(lens).to(dev, non_blocking=True)
+    if table is None:
+        result = verify_batch(logits, buf.upload(rows), prop_d, lens_d, policy=policy)
+    else:
+        result = verify_batch(logits, table.table, prop_d, lens_d, policy=policy, mask_rows=table.upload(rows))
+    host = result.to_host()
 
     def replay(s: int, grammar) -> Iterator[VerifiedToken]:
         events = host.events(s, drafts[s])

@@ -67,7 +67,7 @@ def _check_selection(logits, mask) -> int:
     return logits.numel()
 
 
-def _check_batch(logits, masks):
+def _check_batch(logits, masks, table: bool = False):
     torch = _torch()
     if not (logits.is_cuda and masks.is_cuda):
         raise RuntimeError("batch inputs must be CUDA")
@@ -83,7 +83,7 @@ def _check_batch(logits, masks):
     rows, vocab = logits.shape
     if not (0 < vocab <= _INT32_MAX):
         raise RuntimeError("invalid vocabulary size")
-    if masks.shape[0] != rows or masks.shape[1] != (vocab + 31) // 32:
+    if (masks.shape[0] < 1 if table else masks.shape[0] != rows) or masks.shape[1] != (vocab + 31) // 32:
         raise RuntimeError("incorrect mask shape")
     return rows, vocab
 
@@ -229,11 +229,15 @@ class NativeModule:
                 density.data_ptr(), budget.data_ptr(), dev.index, _stream(dev)))
         return [counts, density, budget]
 
-    def verify_batch(self, logits, masks, proposals, lengths, policy):
-        """Batched verification round; see ``bms_verify_batch``."""
+    def verify_batch(self, logits, masks, proposals, lengths, policy, mask_rows=None):
+        """Batched verification round; see ``bms_verify_batch``.  With ``mask_rows`` (int32 [rows]),
+        ``masks`` is a table of mask rows on the device and row r uses row mask_rows[r]."""
         import ctypes
         torch = _torch()
-        rows, vocab = _check_batch(logits, masks)
+        rows, vocab = _check_batch(logits, masks, table=mask_rows is not None)
+        if mask_rows is not None and (mask_rows.dtype != torch.int32 or mask_rows.shape != (rows,)
+                                      or not mask_rows.is_contiguous() or mask_rows.device != logits.device):
+            raise RuntimeError("mask_rows must be a contiguous int32 [rows] tensor on the logits' device")
         if proposals.dtype != torch.int64 or proposals.dim() != 2 or not proposals.is_contiguous():
             raise RuntimeError("proposals must be a contiguous int64 [S, K] tensor")
         seqs, k = proposals.shape
@@ -263,7 +267,8 @@ class NativeModule:
                 out["row_tokens"].data_ptr(), out["row_counts"].data_ptr(),
                 out["row_status"].data_ptr(), out["row_budget"].data_ptr(),
                 out["accept_len"].data_ptr(), out["token"].data_ptr(), out["kind"].data_ptr(),
-                out["seq_status"].data_ptr(), ws, nbytes, dev.index, _stream(dev)))
+                out["seq_status"].data_ptr(), None if mask_rows is None else mask_rows.data_ptr(),
+                0 if mask_rows is None else masks.shape[0], ws, nbytes, dev.index, _stream(dev)))
         return out
 
 

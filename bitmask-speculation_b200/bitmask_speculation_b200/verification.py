@@ -29,6 +29,7 @@ _ROW_ERRORS = {
     2: "next-token logits contain NaN",
     6: "proposal count outside [0, K]",
     7: "device wait timed out",
+    8: "mask row index outside the mask table",
 }
 
 
@@ -87,19 +88,23 @@ class HostVerification:
         return gen()
 
 
-def verify_batch(logits, masks, proposals, lengths, *, policy=None) -> BatchVerification:
+def verify_batch(logits, masks, proposals, lengths, *, policy=None, mask_rows=None) -> BatchVerification:
     """Verify S sequences of K drafts against S*(K+1) target rows.
 
     ``logits`` [S*(K+1), V] (float32 / bfloat16 / float16), ``masks``
     [S*(K+1), ceil(V/32)] int32 with row ``s*(K+1)+i`` the grammar state after
     ``proposals[s, :i]``, ``proposals`` int64 [S, K], ``lengths`` int32 [S]
     (live proposals per sequence, at most K).  ``policy`` (default
-    ``DensityPolicy()``) turns each row's popcount into a draft budget.
+    ``DensityPolicy()``) turns each row's popcount into a draft budget.  With
+    ``mask_rows`` (int32 [S*(K+1)] on the device), ``masks`` is a device-resident
+    table of mask rows (e.g. one per grammar state) and row r uses ``masks[mask_rows[r]]``;
+    an index outside the table fails the row with status 8.
     """
     from .kernels._extension import load_extension
-    batched_selection_inputs(logits, masks)
+    if mask_rows is None:
+        batched_selection_inputs(logits, masks)
     policy = DensityPolicy() if policy is None else policy
-    out = load_extension().verify_batch(logits, masks, proposals, lengths, policy.native())
+    out = load_extension().verify_batch(logits, masks, proposals, lengths, policy.native(), mask_rows=mask_rows)
     return BatchVerification(**out)
 
 

@@ -314,6 +314,14 @@ class SyntheticDFAGrammar:
     def mask_density(self) -> float:
         return 0.0 if self._terminated else float(self._tables[3][self._state]) / self._vocab
 
+    def mask_table(self) -> np.ndarray:
+        """Packed masks of every state, [states, W] int32 (shared by forks, read-only)."""
+        return self._tables[0]
+
+    def state_index(self) -> int:
+        """Row of ``mask_table()`` holding the current state's mask; -1 once terminated."""
+        return -1 if self._terminated else self._state
+
     def accept_token(self, token: int) -> bool:
         token = int(token)
         if self._terminated or not (0 <= token < self._vocab):

@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
             const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, g.c);
             const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, g.d);
             if (lane == 0) {
-                const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
+                const int32_t code = argmax_status(fl, total);
                 status[row] = code;
                 tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
                 if (counts) counts[row] = total;
@@ -745,8 +745,9 @@ int bms_mask_count(const int32_t* mask, int64_t vocab, int64_t* count, int32_t d
 int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, int64_t seqs, int64_t rows_per_seq,
                      int64_t vocab, const int64_t* proposals, const int32_t* lengths, const bms_policy* policy,
                      int64_t* row_tokens, int64_t* row_counts, int32_t* row_status, int32_t* row_budget,
-                     int32_t* accept_len, int64_t* token, int32_t* kind, int32_t* seq_status, void* workspace,
-                     int64_t workspace_bytes, int32_t device, void* stream) {
+                     int32_t* accept_len, int64_t* token, int32_t* kind, int32_t* seq_status,
+                     const int32_t* mask_rows, int64_t mask_table_rows, void* workspace, int64_t workspace_bytes,
+                     int32_t device, void* stream) {
     if (seqs < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "seqs must be nonnegative");
     if (rows_per_seq < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows_per_seq must be at least 1");
     if (seqs > INT64_MAX / rows_per_seq) return fail(BMS_ERROR_INVALID_ARGUMENT, "batch too large");
@@ -771,8 +772,14 @@ int bms_verify_batch(const void* logits, int32_t dtype, const int32_t* masks, in
     BMS_CHECK(check_ptr(seq_status, device, "seq_status", 4));
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    if (mask_rows != nullptr) {
+        if (mask_table_rows < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "mask_table_rows must be at least 1");
+        BMS_CHECK(check_ptr(mask_rows, device, "mask_rows", 4));
+    }
     SelectParams p = base_params(logits, masks, rows, vocab);
     BMS_CHECK(attach_workspace(p, workspace, workspace_bytes, device));
+    p.mask_rows = mask_rows;
+    p.mask_table_rows = mask_table_rows;
     p.tokens = row_tokens;
     p.counts = row_counts;
     p.status = row_status;

@@ -75,9 +75,17 @@ enum Status : int32_t {
     kPosInf = 5,
     kBadLength = 6,
     kTimeout = 7,
+    kBadMaskRow = 8,
 };
 
-enum Flags : uint32_t { kFlagNaN = 1u, kFlagAbort = 2u };
+enum Flags : uint32_t { kFlagNaN = 1u, kFlagAbort = 2u, kFlagBadMaskRow = 4u };
+
+// Status of a merged argmax partial: a timed-out wait, then a bad mask-table index, then NaN
+// anywhere in the row, then no valid token (csrc/argmax.cu:77-98 for the last two).
+__host__ __device__ constexpr int32_t argmax_status(uint32_t flags, uint32_t total) {
+    return (flags & kFlagAbort) ? kTimeout : (flags & kFlagBadMaskRow) ? kBadMaskRow : (flags & kFlagNaN) ? kNaN
+                                                                       : (total == 0u) ? kEmpty : kOk;
+}
 
 // ----------------------------------------------------------------- dtypes
 template <typename T>
@@ -288,6 +296,10 @@ struct SelectParams {
     int32_t block;             // chunks per block of the split rows
     uint32_t epoch;            // this launch's tag, never 0
     int32_t dynamic_always;    // host only: take the dynamic schedule for any batch size
+    // mask table (nullable): row r's mask is row mask_rows[r] of `masks` ([mask_table_rows, W]);
+    // an index outside [0, mask_table_rows) fails the row with status 8
+    const int32_t* mask_rows;
+    int64_t mask_table_rows;
 };
 
 // Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).
@@ -332,7 +344,8 @@ struct alignas(16) Unit {
     int64_t row;
     int32_t c0, c1;
     int32_t kind;
-    int32_t pad[3];
+    int32_t mask_bad;  // the row's mask-table index was out of range (table row 0 is read instead)
+    int64_t mask_row;  // row of `masks` holding this row's mask words
 };
 
 constexpr int kUnitSlots = 4;  // producer -> consumers descriptor ring
@@ -526,6 +539,7 @@ __device__ __forceinline__ SampleMerge merge_sampler_lanes(const GatherSlot& e, 
     const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, in ? e.c : 0u) | extra_flags;
     r.total = total;
     r.code = (fl & kFlagAbort) ? kTimeout
+             : (fl & kFlagBadMaskRow) ? kBadMaskRow
              : (fl & kFlagNaN) ? kNaN
              : (rm == kInf) ? kPosInf
              : (total == 0u) ? kEmpty
@@ -794,7 +808,7 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
         }
         found = __reduce_min_sync(0xFFFFFFFFu, found);
         if (lane == 0) {
-            const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
+            const int32_t code = argmax_status(fl, total);
             p.status[row] = code;
             p.tokens[row] = (code == kOk && found != 0xFFFFFFFFu) ? p.token_offset + static_cast<int64_t>(found) : -1;
             if (p.counts) p.counts[row] = total;
@@ -907,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 if constexpr (kBulk) {
                     const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                           static_cast<size_t>(d.row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-                    const int32_t* mbase = p.masks + static_cast<size_t>(d.row) * static_cast<size_t>(p.mask_stride);
+                    const int32_t* mbase = p.masks + static_cast<size_t>(d.mask_row) * static_cast<size_t>(p.mask_stride);
                     for (int c = d.c0; c < d.c1; ++c, ++it) {
                         const int stage = static_cast<int>(it % kStages);
                         const uint32_t use = it / kStages;
@@ -931,7 +945,14 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             };
             auto run = [&](int64_t row, int c0, int c1, int32_t kind) {
                 if (stop) return;
-                const Unit d{row, c0, c1, kind, {0, 0, 0}};
+                int64_t mr = row;
+                int32_t bad = 0;
+                if (p.mask_rows != nullptr) {
+                    mr = p.mask_rows[row];
+                    bad = (mr < 0 || mr >= p.mask_table_rows) ? 1 : 0;
+                    if (bad) mr = 0;
+                }
+                const Unit d{row, c0, c1, kind, bad, mr};
                 stop = !push(d) || !issue(d);
             };
             if (!dynamic) {
@@ -959,7 +980,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 }
             }
             // The end marker (if its slot never frees, the consumers' bounded waits end them).
-            push(Unit{0, 0, 0, kUnitEnd, {0, 0, 0}});
+            push(Unit{0, 0, 0, kUnitEnd, 0, 0});
             // Every issued copy must have landed before this CTA's shared memory can go away.
             if constexpr (kBulk) {
                 for (int s = 0; s < kStages; ++s) {
@@ -982,12 +1003,13 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow =
-                p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
+                p.masks + static_cast<size_t>(d.mask_row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
             const int nch = d.c1 - d.c0;
             const bool in = lane < kConsumerWarps;
             const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u, 0.0, 0.0};
             const uint32_t cnt = __reduce_add_sync(0xFFFFFFFFu, wp.count);
-            const uint32_t flags = __reduce_or_sync(0xFFFFFFFFu, wp.flags) | (sh.abort ? kFlagAbort : 0u);
+            const uint32_t flags = __reduce_or_sync(0xFFFFFFFFu, wp.flags) | (sh.abort ? kFlagAbort : 0u) |
+                                   (d.mask_bad ? kFlagBadMaskRow : 0u);
             const uint32_t ckey = __reduce_max_sync(0xFFFFFFFFu, wp.key);
 
             if constexpr (!kSample) {
@@ -1036,7 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     fl = __reduce_or_sync(0xFFFFFFFFu, g.d) | (sh.abort ? kFlagAbort : 0u);
                 }
                 if (crank == 0 && lane == 0) {
-                    const int32_t code = (fl & kFlagAbort) ? kTimeout : (fl & kFlagNaN) ? kNaN : (total == 0u) ? kEmpty : kOk;
+                    const int32_t code = argmax_status(fl, total);
                     p.status[row] = code;
                     p.tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
                     if (p.counts) p.counts[row] = total;
@@ -1110,7 +1132,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
         for (uint32_t u = 0, k = 0;; ++u, ++k) {  // u: units read, k: partial slots used
             const uint32_t us = u % kUnitSlots;
             const bool got = wait_bounded(ptx::smem_addr(&sh.unit_full[us]), (u / kUnitSlots) & 1u, &sh.abort);
-            const Unit d = got ? sh.units[us] : Unit{0, 0, 0, kUnitEnd, {0, 0, 0}};
+            const Unit d = got ? sh.units[us] : Unit{0, 0, 0, kUnitEnd, 0, 0};
             __syncwarp();
             if (got && lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.unit_empty[us]));
             const uint32_t slot = k & 1u;
@@ -1127,7 +1149,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
             const int32_t* mrow =
-                p.masks + static_cast<size_t>(row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
+                p.masks + static_cast<size_t>(d.mask_row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
             const int nch = d.c1 - d.c0;
             double* granules = ss.granules[slot];
             float2* granules_f = reinterpret_cast<float2*>(granules);

@@ -56,7 +56,8 @@ enum {
     BMS_STATUS_NO_MASS = 4,     /* every valid logit is -inf (sampler) */
     BMS_STATUS_POS_INF = 5,     /* a valid logit is +inf (sampler) */
     BMS_STATUS_BAD_LENGTH = 6,  /* verification: proposal count outside [0, K] */
-    BMS_STATUS_TIMEOUT = 7      /* a bounded device wait expired; row result undefined */
+    BMS_STATUS_TIMEOUT = 7,     /* a bounded device wait expired; row result undefined */
+    BMS_STATUS_BAD_MASK_ROW = 8 /* verification with a mask table: index outside the table */
 };
 
 /* Draft budget policy.  kind 0: decoding/scheduling.py:21-46 DensityPolicy
@@ -147,13 +148,18 @@ BMS_API int bms_mask_budget(const int32_t *masks, int64_t rows, int64_t vocab, c
  * prefix length, the correction / bonus / fallback token, its kind (0
  * correction, 1 bonus, 2 fallback) and a status that is nonzero only when a
  * row the reference would have consumed failed.  row_counts and row_budget
- * may be NULL (then policy may be NULL); `workspace` may be NULL. */
+ * may be NULL (then policy may be NULL); `workspace` may be NULL.  Mask table (no
+ * reference counterpart): with `mask_rows` non-NULL, `masks` is a table of
+ * `mask_table_rows` mask rows resident on the device (e.g. one per grammar state)
+ * and row r uses table row mask_rows[r] (int32, device); an index outside the
+ * table fails that row with BMS_STATUS_BAD_MASK_ROW. */
 BMS_API int bms_verify_batch(const void *logits, int32_t dtype, const int32_t *masks, int64_t seqs,
                      int64_t rows_per_seq, int64_t vocab, const int64_t *proposals,
                      const int32_t *lengths, const bms_policy *policy, int64_t *row_tokens,
                      int64_t *row_counts, int32_t *row_status, int32_t *row_budget,
                      int32_t *accept_len, int64_t *token, int32_t *kind, int32_t *seq_status,
-                     void *workspace, int64_t workspace_bytes, int32_t device, void *stream);
+                     const int32_t *mask_rows, int64_t mask_table_rows, void *workspace,
+                     int64_t workspace_bytes, int32_t device, void *stream);
 
 /* ---- vocabulary shards ----------------------------------------------------------------
  * A row's vocabulary split across ranks (GPUs), each holding logits [rows, vocab_shard] of its

@@ -83,7 +83,7 @@ def test_invalid_arguments_fail_before_any_launch(lib):
     assert rc == _native.ERROR_INVALID_ARGUMENT
     # Verification shape contract
     rc = lib.bms_verify_batch(null, 0, null, 1, 0, 32, null, null, null, null, null, null, null,
-                              null, null, null, null, null, 0, 0, null)
+                              null, null, null, null, null, 0, null, 0, 0, null)
     assert rc == _native.ERROR_INVALID_ARGUMENT and b"rows_per_seq" in lib.bms_last_error()
 
 

@@ -162,3 +162,64 @@ def test_grammar_round_synthesis_on_cpu():
         assert lens[s].item() == len(drafts[s]) and prop[s, : len(drafts[s])].tolist() == list(drafts[s])
         rows = fork_masks(grammars[s], drafts[s], vocab, buf)
         assert np.array_equal(buf[:rows], masks.numpy()[s * (k + 1): s * (k + 1) + rows])
+
+
+def test_fork_state_indices_match_fork_masks():
+    from bitmask_speculation_b200.grammar_verification import fork_state_indices
+    vocab = 4096
+    g = wl.SyntheticDFAGrammar(vocab, states=16, seed=5)
+    table = np.vstack([g.mask_table(), np.zeros((1, g.mask_table().shape[1]), np.int32)])
+    rng = np.random.default_rng(1)
+    for _ in range(30):
+        draft = [int(rng.choice(g.allowed_ids_np())) if rng.random() < 0.9 else int(rng.integers(vocab))
+                 for _ in range(int(rng.integers(0, 9)))]
+        masks = np.zeros((9, table.shape[1]), np.int32)
+        idx = np.full(9, -5, np.int32)
+        rows = fork_masks(g, draft, vocab, masks)
+        assert fork_state_indices(g, draft, idx, g.mask_table().shape[0]) == rows
+        assert np.array_equal(table[idx[:rows]], masks[:rows])
+
+
+@pytest.mark.gpu
+def test_device_mask_table_round_equals_uploaded_masks(cuda_module):
+    """Table indices instead of mask words: same events, same grammar states; an index outside
+    the table fails its row with status 8."""
+    torch = pytest.importorskip("torch")
+    from bitmask_speculation_b200.grammar_verification import (DeviceMaskTable, DraftForkMasks,
+                                                               verify_with_grammars)
+    from bitmask_speculation_b200.verification import verify_batch
+    vocab, seqs, k = 248320, 32, 8
+    rng = np.random.default_rng(23)
+    base = wl.SyntheticDFAGrammar(vocab, states=64, seed=2)
+    a = [base.fork() for _ in range(seqs)]
+    for g in a:
+        for _ in range(int(rng.integers(0, 4))):
+            ids = g.allowed_ids_np()
+            g.accept_token(int(rng.choice(ids[ids != 0])) if (ids != 0).any() else 0)
+    b = [g.fork() for g in a]
+    buf = DraftForkMasks(vocab, seqs * (k + 1), torch.device("cuda"))
+    table = DeviceMaskTable.for_grammar(base, seqs * (k + 1), torch.device("cuda"))
+    for rnd in range(2):
+        block = np.zeros((seqs * (k + 1), vocab), dtype=np.uint16)
+        drafts = []
+        for s in range(seqs):
+            if a[s].is_terminated():
+                drafts.append(())
+                continue
+            rows, draft = make_round(rng, vocab, int(rng.integers(0, k + 1)), a[s].fork())
+            block[s * (k + 1): s * (k + 1) + len(draft) + 1] = wl.to_bf16_bits(rows)
+            drafts.append(draft)
+        logits = torch.from_numpy(block.view(np.int16)).view(torch.bfloat16).cuda()
+        want = [list(it) for it in verify_with_grammars(drafts, logits, a, k=k, buffer=buf)]
+        got = [list(it) for it in verify_with_grammars(drafts, logits, b, k=k, table=table)]
+        assert got == want, rnd
+        assert [(g.state, g.is_terminated()) for g in a] == [(g.state, g.is_terminated()) for g in b]
+    # out-of-range table indices fail exactly those rows
+    rows = seqs * (k + 1)
+    idx = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    idx[3] = 65
+    idx[4] = -1
+    res = verify_batch(logits, table.table, torch.zeros((seqs, k), dtype=torch.int64, device="cuda"),
+                       torch.zeros(seqs, dtype=torch.int32, device="cuda"), mask_rows=idx).to_host()
+    assert res.row_status[3] == 8 and res.row_status[4] == 8
+    assert all(s != 8 for i, s in enumerate(res.row_status) if i not in (3, 4))
