@@ -791,15 +791,17 @@ def run_decode(args):
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    from bitmask_speculation_b200.grammar_verification import DeviceMaskTable
     vocab = wl.VOCAB
     target, draft = config_models(vocab, device=device)
     prompts = random_prompts(args.prompts, 64, vocab, seed=4)
     grammar0 = wl.SyntheticDFAGrammar(vocab, states=64, seed=4)
+    table = DeviceMaskTable.for_grammar(grammar0, 16, device)  # the grammar's state masks on the device
     # warm-up over every padded sequence length the timed runs reach (kernels, cuBLAS heuristics)
-    speculative_c4(target, draft, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,))
+    speculative_c4(target, draft, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,), table=table)
     speculative_c4(target, draft, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,),
-                   verify="lazy")
-    constrained_greedy(target, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,))
+                   verify="lazy", table=table)
+    constrained_greedy(target, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,), table=table)
     torch.cuda.synchronize(device)
 
     def run(fn, *extra):
@@ -807,7 +809,8 @@ def run_decode(args):
         with ClockSampler(local) as clocks:
             t0 = time.perf_counter()
             for p in prompts:
-                outs.append(fn(target, *extra, p, grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,)))
+                outs.append(fn(target, *extra, p, grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,),
+                               table=table))
             torch.cuda.synchronize(device)
             secs = time.perf_counter() - t0
         return outs, secs, clocks.summary()
@@ -826,7 +829,8 @@ def run_decode(args):
         "data": "synthetic (random-init weights, random prompts, synthetic DFA grammar)",
         "config": {"workload": (f"decode: c4 speculative decoding, {len(prompts)} prompts x 64 random tokens, "
                                 f"{args.new_tokens} new tokens; target 4 layers d=1024 16 heads, draft 1 layer "
-                                "d=512, V=248320 bf16 random-init; 64-state token DFA grammar, EOS id 0"),
+                                "d=512, V=248320 bf16 random-init; 64-state token DFA grammar, EOS id 0; "
+                                "state masks resident on the device"),
                    "rounds": sum(o.rounds for o in spec), "proposed": sum(o.proposed for o in spec),
                    "accepted": sum(o.accepted for o in spec), "tokens": tokens,
                    "stop_reasons": {r: sum(o.stop_reason == r for o in spec) for r in ("eos", "grammar", "length")}},

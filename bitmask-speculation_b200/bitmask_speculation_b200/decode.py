@@ -23,7 +23,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from .grammar_verification import DraftForkMasks, verify_with_grammar
+from .grammar_verification import DeviceMaskTable, DraftForkMasks, verify_with_grammar, verify_with_grammars
 from .scheduling import DensityPolicy
 
 
@@ -129,7 +129,7 @@ class _Selector:
 
     seconds = 0.0
 
-    def __init__(self, vocab: int, device):
+    def __init__(self, vocab: int, device, table: DeviceMaskTable | None = None):
         torch = _torch()
         from .kernels._extension import load_extension
         self.native = load_extension()
@@ -137,14 +137,20 @@ class _Selector:
         self.host = torch.zeros(self.words, dtype=torch.int32).pin_memory()
         self.dev = torch.empty(self.words, dtype=torch.int32, device=device)
         self._np = self.host.numpy()
+        self.table = table
 
     def __call__(self, row, grammar) -> int:
         import time
         from .kernels.cuda import masked_argmax
         t0 = time.perf_counter()
-        self._np[:] = grammar.packed_mask_np()
-        self.dev.copy_(self.host, non_blocking=True)
-        token = int(masked_argmax(row, self.dev).item())
+        if self.table is not None:  # the state's mask is already on the device: a view of the table
+            idx = grammar.state_index()
+            mask = self.table.table[idx if idx >= 0 else self.table.empty]
+        else:
+            self._np[:] = grammar.packed_mask_np()
+            self.dev.copy_(self.host, non_blocking=True)
+            mask = self.dev
+        token = int(masked_argmax(row, mask).item())
         self.seconds += time.perf_counter() - t0
         if not grammar.accept_token(token):
             raise ValueError("grammar rejected its selected token")
@@ -163,11 +169,12 @@ class DecodeResult:
 
 
 # ---------------------------------------------------------------- request loops
-def constrained_greedy(target, prompt, grammar, *, max_new_tokens: int, eos=(), selector=None) -> DecodeResult:
+def constrained_greedy(target, prompt, grammar, *, max_new_tokens: int, eos=(), selector=None,
+                       table: DeviceMaskTable | None = None) -> DecodeResult:
     """Target-only constrained greedy decoding (decoding/greedy.py:51-92)."""
     prompt = tuple(int(t) for t in prompt)
     eos = frozenset(int(t) for t in eos)
-    sel = selector or _Selector(target.vocab_size, target.head.weight.device)
+    sel = selector or _Selector(target.vocab_size, target.head.weight.device, table)
     out: list[int] = []
 
     def finish(reason, token=None):
@@ -210,17 +217,20 @@ def _lazy_rounds(draft, rows, grammar, sel):
 
 
 def speculative_c4(target, draft, prompt, grammar, *, max_new_tokens: int, eos=(), policy=None,
-                   selector=None, buffer=None, verify: str = "batched") -> DecodeResult:
+                   selector=None, buffer=None, verify: str = "batched",
+                   table: DeviceMaskTable | None = None) -> DecodeResult:
     """Density-scheduled constrained speculative decoding (decoding/speculative.py:96-208 with
     constrain_draft=True and a DensityPolicy).  ``verify="batched"`` verifies each round with
     ``verify_with_grammar`` (one launch pair, one sync); ``"lazy"`` with the reference's per-row
-    loop (one masked argmax and one sync per consumed row) on the same target rows."""
+    loop (one masked argmax and one sync per consumed row) on the same target rows.  With ``table``
+    (the grammar's state masks resident on the device) selections read their masks from it and
+    batched rounds upload table indices instead of mask words."""
     prompt = tuple(int(t) for t in prompt)
     eos = frozenset(int(t) for t in eos)
     policy = DensityPolicy() if policy is None else policy
     device = target.head.weight.device
-    sel = selector or _Selector(target.vocab_size, device)
-    buf = buffer or DraftForkMasks(target.vocab_size, policy.max_budget + 1, device)
+    sel = selector or _Selector(target.vocab_size, device, table)
+    buf = buffer or (None if table is not None else DraftForkMasks(target.vocab_size, policy.max_budget + 1, device))
     out: list[int] = []
     rounds = proposed = accepted = 0
 
@@ -254,7 +264,11 @@ def speculative_c4(target, draft, prompt, grammar, *, max_new_tokens: int, eos=(
         if verify == "batched":
             import time
             t0 = time.perf_counter()
-            events = verify_with_grammar(proposals, rows, grammar, buffer=buf, policy=policy)
+            if table is not None:
+                events = verify_with_grammars([proposals], rows, [grammar], k=len(proposals), table=table,
+                                              policy=policy)[0]
+            else:
+                events = verify_with_grammar(proposals, rows, grammar, buffer=buf, policy=policy)
             verify_seconds += time.perf_counter() - t0
         else:
             events = _lazy_rounds(tuple(proposals), rows, grammar, sel)

@@ -52,3 +52,19 @@ def test_batched_and_lazy_verification_agree_in_bf16(cuda_module):
         a = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=40, eos=(0,))
         b = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=40, eos=(0,), verify="lazy")
         assert a == b, i
+
+
+def test_device_mask_table_decoding_equals_uploaded_masks(models):
+    """Selections and rounds reading the grammar's state masks from a device table choose exactly
+    what the uploaded-mask path chooses."""
+    from bitmask_speculation_b200.decode import random_prompts, speculative_c4
+    from bitmask_speculation_b200.grammar_verification import DeviceMaskTable
+    vocab, target, draft = models
+    for i, prompt in enumerate(random_prompts(4, 16, vocab, seed=9)):
+        g0 = wl.SyntheticDFAGrammar(vocab, states=64, seed=30 + i)
+        table = DeviceMaskTable.for_grammar(g0, 16, torch.device("cuda"))
+        a = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=40, eos=(0,))
+        b = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=40, eos=(0,), table=table)
+        c = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=40, eos=(0,), table=table,
+                           verify="lazy")
+        assert a == b == c, i
