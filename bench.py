@@ -721,13 +721,19 @@ def run_b200_arm(args):
             e2e = {"value": w.rows * world * args.steps / etime, "unit": "rows/s",
                    "h2d_bytes_per_step": e.h2d, "d2h_bytes_per_step": e.d2h,
                    "wall_value": w.rows * world * args.steps / wall,
-                   "path": ("grammar_verification.verify_with_grammars (public API) with a device-resident "
-                            "mask table: fork state indices computed on the host, one H2D of 4 bytes per row, "
-                            "one launch pair, one sync, events replayed on the sequences' grammars every step"
-                            if w.kind == "grammar" else
-                            "verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
-                            "device-resident logits, results D2H every step; each step's upload on a copy "
-                            "stream overlaps the previous step's kernels (two input buffers)")}
+                   "path": {
+                       "grammar": ("grammar_verification.verify_with_grammars (public API) with a device-resident "
+                                   "mask table: fork state indices computed on the host, one H2D of 4 bytes per "
+                                   "row, one launch pair, one sync, events replayed on the sequences' grammars "
+                                   "every step"),
+                       "verify": ("verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
+                                  "device-resident logits, results D2H every step; each step's upload on a copy "
+                                  "stream overlaps the previous step's kernels (two input buffers)"),
+                       "sample": ("kernels.cuda.batched_masked_sample (public API): pinned host masks H2D, "
+                                  "device-resident logits, uniforms drawn on the device, tokens and status D2H "
+                                  "every step"),
+                   }.get(w.kind, "kernels.cuda.batched_masked_reduce (public API): pinned host masks H2D, "
+                                 "device-resident logits, tokens and status D2H every step")}
 
     total_rows = w.rows if w.kind == "vocab" else w.rows * world  # vocab shards split the same rows
     value = total_rows * args.steps / seconds
