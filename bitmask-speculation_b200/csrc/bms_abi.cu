@@ -275,8 +275,9 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     p.segment = plan.segment;
     cudaLaunchConfig_t cfg = {};
     // Programmatic dependent launch: CTAs may be dispatched and initialise their barriers while
-    // the previous grid in the stream drains (the kernel waits for it before touching memory).
-    // A launch without a cluster dimension is a grid of one-CTA clusters.
+    // the previous grid in the stream finishes its row-end work (the previous grid signals once
+    // all its CTAs streamed their last chunk; this one waits for its completion before touching
+    // memory).  A launch without a cluster dimension is a grid of one-CTA clusters.
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -288,9 +289,10 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
     cfg.stream = stream;
-    // A grid that fills every resident slot, or one of at most one CTA per SM (latency-bound: an
-    // early start hides ~1-2 us of launch).  Grids in between, dispatched early into the slots
-    // their predecessor leaves free, would be spread unevenly over the SMs.
+    // A grid that fills every resident slot, or one of at most one CTA per SM, hides its launch
+    // behind its predecessor's row-end work.  Grids in between, dispatched early into the slots
+    // their predecessor leaves free, would be spread unevenly over the SMs (measured on B200:
+    // 256 sampler rows 48 instead of 40 us).
     const bool full = plan.clusters >= info->max_clusters[cluster_index(plan.cluster)] ||
                       plan.cluster * plan.clusters <= info->sms;
     cfg.attrs = full ? attr : attr + 1;

@@ -27,10 +27,14 @@ __device__ __forceinline__ uint64_t atom_add_acq_rel_gpu(unsigned long long* p, 
     return old;
 }
 
-// 16-byte global -> shared copy through L2 (no registers); cp_async_wait_all completes this
-// thread's copies.
+// 16-byte (through L2) and 8-byte global -> shared copies without registers; cp_async_wait_all
+// completes this thread's copies.
 __device__ __forceinline__ void cp_async_16(uint32_t smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_8(uint32_t smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem), "l"(gmem) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }

@@ -360,6 +360,7 @@ struct alignas(16) Shared {
     uint64_t unit_empty[kUnitSlots];  // consumers -> producer, one arrive per consumer warp
     Unit units[kUnitSlots];
     Unit part_unit[2];                // the unit of each partial slot (consumers -> finalizer)
+    double part_uniform[2];           // sampler: the unit row's uniform, fetched while it streams
     GatherSlot slots[2][kMaxCluster];
     WarpPartial part[2][kConsumerWarps];
     int32_t piece_c0[32];             // finalizer: first chunks of a split row's pieces, in order
@@ -714,10 +715,10 @@ __device__ __forceinline__ double* ws_granules(const SelectParams& p, int64_t t,
 // shards -- and writes the row's outputs: the argmax index is recovered from the winning region
 // only, the sampler walks the owning piece.  Sampler: `granules` (shared memory) holds the
 // piece's granules, lanes w < 8 pass warp w's factor to the piece max; the buffer is then reused
-// for the row's granules.
+// for the row's granules; `uniform` is the row's uniform.
 template <typename T, bool kSample>
 __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row_chunks, const GatherSlot& part, double wf,
-                                   double* granules, Shared& sh, SamplerShared& ss, const uint8_t* lrow,
+                                   double* granules, double uniform, Shared& sh, SamplerShared& ss, const uint8_t* lrow,
                                    const int32_t* mrow, int lane) {
     using E = Elem<T>;
     constexpr int kTPC = Layout<T>::kTokensPerChunk;
@@ -814,7 +815,7 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
             if (p.counts) p.counts[row] = total;
         }
     } else {
-        const SampleMerge mg = merge_sampler_lanes(e, in, p.uniforms[row], p.temperature, p.inv_temperature, abort_flag, lane);
+        const SampleMerge mg = merge_sampler_lanes(e, in, uniform, p.temperature, p.inv_temperature, abort_flag, lane);
         int64_t chosen = -1;
         if (mg.code == kOk) {
             const int q = mg.owner;
@@ -837,6 +838,13 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
     // The next launch (or graph replay) counts this row from zero.
     if (lane == 0) atomicExch(ws_row_counter(p, t), 0ull);
 }
+
+// Programmatic dependent launch: a dependent grid (the next selection launch, the verification
+// epilogue) may be scheduled once every thread of every CTA executed this or exited.  The
+// finalizer warp executes it on entry and the producer and consumer warps when they have
+// streamed their last chunk, so the dependent's launch overlaps the row-end work of the last
+// rows; the dependent still waits for this grid's completion before touching memory.
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <typename T, bool kSample, bool kBulk, int kStages>
 __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectParams p) {
@@ -893,9 +901,6 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     // Launched as a programmatic dependent, this grid may have started while the previous grid in
     // the stream was still running: no global memory is touched before that grid completed.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // A programmatic dependent (the verification epilogue, the next selection launch) may start
-    // launching now; it waits for this grid's completion before touching global memory.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Every CTA of the cluster has initialised its barriers before any remote arrive.
     if (csize > 1) {
         ptx::cluster_arrive();
@@ -992,8 +997,10 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             }
         }
         __syncwarp();
+        launch_dependents();
     } else if (warp == kFinalizerWarp) {
         // ------------------------------------------------------------ finalizer warp
+        launch_dependents();
         for (uint32_t k = 0;; ++k) {
             const uint32_t slot = k & 1u;
             if (!wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort)) break;
@@ -1023,7 +1030,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 if (d.kind == kUnitSplit && p.partials == nullptr) {
                     // The index is recovered by the row's merge, from the winning piece only.
                     finish_split_piece<T, false>(p, d, nchunks, GatherSlot{ckey, rmin, cnt, flags, 0.0, 0.0}, 0.0,
-                                                 nullptr, sh, ss, lrow, mrow, lane);
+                                                 nullptr, 0.0, sh, ss, lrow, mrow, lane);
                     continue;
                 }
                 uint32_t found = 0xFFFFFFFFu;
@@ -1088,7 +1095,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     for (int g = lane; g < ngran; g += 32) rg[g] = granules[g];
                 } else if (d.kind == kUnitSplit) {
                     finish_split_piece<T, true>(p, d, nchunks, GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0},
-                                                wf, granules, sh, ss, lrow, mrow, lane);
+                                                wf, granules, sh.part_uniform[slot], sh, ss, lrow, mrow, lane);
                 } else {
                     // Rank partials, all-gathered in rank order, merged identically on every rank.
                     if (lane == 0) {
@@ -1097,7 +1104,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         else sh.slots[slot][0] = mine;
                     }
                     __syncwarp();
-                    const SampleMerge mg = merge_sampler_ranks(sh.slots[slot], 1, csize, p.uniforms[row], p.temperature,
+                    const SampleMerge mg = merge_sampler_ranks(sh.slots[slot], 1, csize, sh.part_uniform[slot], p.temperature,
                                                                p.inv_temperature, sh.abort ? kFlagAbort : 0u, lane);
                     if (mg.code != kOk) {
                         if (crank == 0 && lane == 0) {
@@ -1143,8 +1150,13 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     if (warp == 0) sh.part_unit[slot] = d;
                     ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
                 }
+                launch_dependents();
                 break;
             }
+            // Sampler: the row's uniform is copied to the partial slot while the row streams (the
+            // finalizer needs it right after the last chunk).
+            const bool fetch_uniform = kSample && warp == 0 && lane == 0 && p.uniforms != nullptr && p.partials == nullptr;
+            if (fetch_uniform) ptx::cp_async_8(ptx::smem_addr(&sh.part_uniform[slot]), p.uniforms + d.row);
             const int64_t row = d.row;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                   static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
@@ -1273,15 +1285,20 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     }
                     if (first_valid_chunk < 0 && anyb != 0u) first_valid_chunk = c;
                 } else {
-                    // Pass 1 over registers: NaN, count, masked values (-inf where invalid).
+                    // Pass 1 over registers: NaN, count, masked values (-inf where invalid).  A
+                    // warp without valid tokens in the chunk records mass 0 and computes no weights.
                     uint32_t anyb = 0u;
-                    uint32_t q16[kVecsPerLane][4];
-                    float q32[kVecsPerLane][kVec];
 #pragma unroll
                     for (int j = 0; j < kVecsPerLane; ++j) {
                         E::nan_update(nan_acc, raw[j]);
                         if constexpr (!kFull) count += __popc(bits[j]);
                         anyb |= bits[j];
+                    }
+                    const bool warp_any = __any_sync(0xFFFFFFFFu, anyb != 0u);
+                    uint32_t q16[kVecsPerLane][4];
+                    float q32[kVecsPerLane][kVec];
+#pragma unroll
+                    for (int j = 0; j < kVecsPerLane && warp_any; ++j) {
                         if constexpr (E::kBytes == 2) {
                             mask_pairs<E>(raw[j], bits[j], q16[j]);
                         } else {
@@ -1327,12 +1344,14 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                     // tiny temperature or huge logits) it is raised to every chunk's max.
                     float mass = 0.0f;
                     bool done = false, any_mass = false;
-                    if (fast) {
+                    if (!warp_any) {
+                        done = true;
+                    } else if (fast) {
                         mass = lane_mass_fast<E>(q16, q32, chi, sc);
                         any_mass = true;
                         if (__any_sync(0xFFFFFFFFu, mass > kRaiseMass)) raise();
                         else done = true;
-                    } else if (__any_sync(0xFFFFFFFFu, anyb != 0u)) {
+                    } else {
                         raise();
                         any_mass = true;
                     }
@@ -1398,6 +1417,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 const uint32_t chunk_id = static_cast<uint32_t>(best_idx >= 0 ? best_idx : first_valid_chunk);
                 wchunk = __reduce_min_sync(0xFFFFFFFFu, (has && key == wkey) ? chunk_id : 0xFFFFFFFFu);
             }
+            if (fetch_uniform) ptx::cp_async_wait_all();
             if (lane == 0) {
                 if (warp == 0) sh.part_unit[slot] = d;
                 sh.part[slot][warp] = WarpPartial{wkey, wchunk, wcount, wflags, wmass, 0.0};
