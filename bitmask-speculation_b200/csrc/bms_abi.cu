@@ -180,13 +180,16 @@ constexpr double kRowCostArgmax[5] = {1.1, 2.4, 3.6, 5.0, 7.0};
 constexpr double kRowCostSampler[5] = {5.0, 8.0, 12.0, 16.0, 20.0};
 
 // Choose the cluster size that minimises the streaming plus row-end work of the busiest CTA.
+// Clusters only pay while most SMs would idle: from one row per two SMs on, one-CTA clusters
+// are as fast or faster (measured on B200 with one- and two-CTA clusters: 148 rows 13.3 / 16.4
+// us for the argmax and 29.5 / 36.6 us for the sampler, 100 rows 13.1 / 14.3 and 29.3 / 32.2 us).
 Plan plan_launch(const KernelInfo& info, int64_t rows, int64_t vocab, int tokens_per_chunk, int max_chunks,
                  bool sampler, bool single) {
     Plan best{0, 0, 0};
     double best_cost = 0.0;
     for (int i = 0; i < 5; ++i) {
         const int c = kClusterSizes[i];
-        if (single ? c != 1 : (g_force_cluster && c != g_force_cluster)) continue;
+        if (single ? c != 1 : (g_force_cluster ? c != g_force_cluster : (c > 1 && 2 * rows >= info.sms))) continue;
         const int resident = info.max_clusters[i];
         if (resident <= 0) continue;
         const int64_t seg = ((vocab + c - 1) / c + 31) / 32 * 32;
