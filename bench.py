@@ -40,7 +40,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per row from one ncu capture of the dominant kernel
 # on a smaller case of the same workload (profiles/select_rows_bf16_verify.md and
 # profiles/select_rows_f16_sample.md); traffic grows with the rows processed.
-NCU_TRAFFIC_PER_ROW = {"verify": 533240, "sample": 533320}
+NCU_TRAFFIC_PER_ROW = {"verify": 533530, "sample": 533980}
 
 
 def parse_args():

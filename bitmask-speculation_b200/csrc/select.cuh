@@ -451,6 +451,13 @@ __device__ __forceinline__ double warp_sum(double v) {
     return v;
 }
 
+// Sum of lanes 0..7 (every other lane holds 0), complete on lanes 0..7.
+__device__ __forceinline__ double warp_sum8(double v) {
+#pragma unroll
+    for (int o = 4; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
 // exp((x - M) / T) for a valid, finite-or(-inf) logit; the reference's weight.
 // exp(d / T) (d below about 14 T: references trail maxima by at most 2^20 in weight), multiplying by 1 / T where that is finite (inv > 0) and dividing
 // otherwise (denormal temperatures).
@@ -583,6 +590,40 @@ __device__ __forceinline__ SampleMerge merge_sampler_lanes(const GatherSlot& e, 
 
 __device__ __forceinline__ SampleMerge merge_sampler_ranks(const GatherSlot* g, int64_t stride, uint32_t n, double u,
                                                            double temp, double inv, uint32_t extra_flags, int lane) {
+    if (n == 1) {
+        // One rank: its max is the row max and its mass the total (the scan of merge_sampler_lanes
+        // over one lane, without the warp round trips).
+        const float kInf = __int_as_float(0x7F800000);
+        const GatherSlot e = g[0];
+        const float rm = __uint_as_float(e.a);
+        const uint32_t fl = e.c | extra_flags;
+        SampleMerge r;
+        r.total = e.b;
+        r.code = (fl & kFlagAbort) ? kTimeout
+                 : (fl & kFlagBadMaskRow) ? kBadMaskRow
+                 : (fl & kFlagNaN) ? kNaN
+                 : (rm == kInf) ? kPosInf
+                 : (e.b == 0u) ? kEmpty
+                 : (rm == -kInf) ? kNoMass
+                 : !(u >= 0.0 && u < 1.0) ? kBadUniform
+                                          : kOk;
+        r.M = rm;
+        r.owner = -1;
+        r.fallback = false;
+        r.cutoff = 0.0;
+        r.prefix = 0.0;
+        r.rank_fac = 1.0;
+        if (r.code != kOk) return r;
+        const double m = e.s > 0.0 ? e.s : 0.0;
+        r.cutoff = u * m;
+        if (m > 0.0) {
+            r.owner = 0;
+            r.fallback = !(r.cutoff < m);
+        } else {
+            r.fallback = true;
+        }
+        return r;
+    }
     const bool in = static_cast<uint32_t>(lane) < n;
     GatherSlot e{0u, 0u, 0u, 0u, 0.0, 0.0};
     if (in) e = g[static_cast<int64_t>(lane) * stride];
@@ -1082,7 +1123,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                                       ? warp_factor(wmax, seg_m, p.temperature, p.inv_temperature)
                                       : 0.0;
                 const double term = wp.mass * wf;
-                const double seg_s = warp_sum(term);
+                const double seg_s = warp_sum8(term);  // read on lane 0
                 if (p.partials != nullptr) {
                     // Vocabulary shard: the row's partial and granule record are the output.
                     if (lane == 0) p.partials[row] = GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
