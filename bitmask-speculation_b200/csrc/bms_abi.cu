@@ -480,7 +480,8 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
                 const uint8_t* lrow = logits + static_cast<size_t>(row) * static_cast<size_t>(vocab_shard) * sizeof(T);
                 const int32_t* mrow = masks + static_cast<size_t>(row) * static_cast<size_t>(mask_words) + (token_offset >> 5);
                 const int64_t chosen = sampler_owner_walk<T>(
-                    reinterpret_cast<const double*>(rec + SamplerRecord::kGranuleOffset), nchunks * kConsumerWarps, wf,
+                    reinterpret_cast<const double*>(rec + SamplerRecord::kGranuleOffset), kConsumerWarps, 1,
+                    nchunks * kConsumerWarps, wf,
                     wmass, has, mg, temperature, inv, scale2, 0, vocab_shard, lrow, mrow, walk[wib], fac[wib], lane);
                 token = chosen >= 0 ? token_offset + chosen : -1;
                 if (chosen < 0) code = kNoMass;

@@ -375,7 +375,7 @@ struct alignas(16) Shared {
 // counters to zero (after a timed-out wait, its last CTA clears every row counter) and tags its
 // pieces with its epoch (never 0), so that consecutive launches and graph replays need no
 // clearing and pieces of an earlier launch are never merged.  Layout: WsHeader | row counters [rows_cap] | pieces [rows_cap][kWsChunks] |
-// granules [rows_cap][kWsChunks][kConsumerWarps] doubles.
+// granules [rows_cap][kConsumerWarps][kWsChunks] doubles (warp-major, as in shared memory).
 constexpr int kWsChunks = 64;  // chunks per split row (longer rows are not split)
 
 struct alignas(64) WsHeader {
@@ -405,8 +405,10 @@ __host__ __device__ constexpr int64_t ws_bytes(int64_t rows_cap) {
 
 // Sampler-only shared memory after the control block.
 struct SamplerShared {
-    // Per row slot, one entry per (chunk, warp) granule: while streaming a float2 (running max,
-    // mass relative to it); after the row, the granule's mass relative to its warp's max (double).
+    // Per row slot, one entry per (chunk, warp) granule at [warp * kMaxChunksSampler + chunk]
+    // (warp-major: a warp's lanes walking consecutive chunks hit distinct banks): while streaming
+    // a float2 (running max, mass relative to it); after the row, the granule's mass relative to
+    // its warp's max (double).
     double granules[2][kMaxChunksSampler * kConsumerWarps];
     float walk[32][33];                                       // finalizer: the walked granule, one row per lane
     double fac[kConsumerWarps];                               // finalizer: warp max -> row max factors
@@ -638,10 +640,14 @@ __device__ __forceinline__ double warp_factor(float wmax, float seg_m, double te
 // The owning rank's walk (one warp): find the granule holding the crossing from the granule
 // masses (each relative to its warp's reference max; `fac` = warp factor x rank factor rescales
 // them to the row max), then the lane of that granule with fp32 weights, then the token with the
-// reference's exact fp64 weights.  Lane w < 8 passes its warp's factor to the rank max
-// (warp_factor) and mass.  Returns the token's index within the row (-1 if none).
+// reference's exact fp64 weights.  Granule g (chunk g / 8, warp g % 8, in token order) is read at
+// granules[(g / 8) * cstride + (g % 8) * wstride]: the shared-memory table is warp-major (cstride
+// 1, wstride kMaxChunksSampler), a vocabulary shard's record chunk-major (cstride 8, wstride 1).
+// Lane w < 8 passes its warp's factor to the rank max (warp_factor) and mass.  Returns the token's
+// index within the row (-1 if none).
 template <typename T>
-__device__ int64_t sampler_owner_walk(const double* granules, int ngran, double wfac, double wmass, bool has_warp,
+__device__ int64_t sampler_owner_walk(const double* granules, int cstride, int wstride, int ngran, double wfac,
+                                      double wmass, bool has_warp,
                                       const SampleMerge& mg, double temp, double inv, float scale2, int64_t seg_begin,
                                       int64_t seg_end, const uint8_t* lrow, const int32_t* mrow, float (*walk)[33],
                                       double* fac, int lane) {
@@ -656,13 +662,17 @@ __device__ int64_t sampler_owner_walk(const double* granules, int ngran, double 
     const int per = (ngran + 31) / 32;
     const int g0 = lane * per, g1 = min(g0 + per, ngran);
     double local = 0.0;
-    for (int g = g0; g < g1; ++g) local += granules[g] * fac[g % kConsumerWarps];
+    auto mass_at = [&](int g) {
+        const int w = g % kConsumerWarps;
+        return granules[(g / kConsumerWarps) * cstride + w * wstride] * fac[w];
+    };
+    for (int g = g0; g < g1; ++g) local += mass_at(g);
     const double incl = warp_inclusive_scan(local, lane);
     double acc = prefix + incl - local;
     int cand = 0x7FFFFFFF, lastg = -1;
     double cand_prefix = 0.0;
     for (int g = g0; g < g1; ++g) {
-        const double m = granules[g] * fac[g % kConsumerWarps];
+        const double m = mass_at(g);
         if (!(m > 0.0)) continue;
         lastg = g;
         if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m) {
@@ -744,8 +754,9 @@ __device__ __forceinline__ unsigned long long* ws_row_counter(const SelectParams
 __device__ __forceinline__ WsPiece* ws_piece(const SelectParams& p, int64_t t, int c) {
     return reinterpret_cast<WsPiece*>(p.ws + ws_pieces_offset(p.ws_rows)) + (t * kWsChunks + c);
 }
-__device__ __forceinline__ double* ws_granules(const SelectParams& p, int64_t t, int c) {
-    return reinterpret_cast<double*>(p.ws + ws_granules_offset(p.ws_rows)) + (t * kWsChunks + c) * kConsumerWarps;
+// Split row t's granule block, [warp][chunk] with kWsChunks chunks per warp.
+__device__ __forceinline__ double* ws_granules(const SelectParams& p, int64_t t) {
+    return reinterpret_cast<double*>(p.ws + ws_granules_offset(p.ws_rows)) + t * kWsChunks * kConsumerWarps;
 }
 
 // ----------------------------------------------------------------- the kernel
@@ -776,8 +787,11 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
     if constexpr (kSample) {
         if (lane < kConsumerWarps) ss.fac[lane] = wf;
         __syncwarp();
-        double* g = ws_granules(p, t, d.c0);
-        for (int i = lane; i < nch * kConsumerWarps; i += 32) g[i] = granules[i] * ss.fac[i % kConsumerWarps];
+        double* g = ws_granules(p, t) + d.c0;
+        for (int i = lane; i < nch * kConsumerWarps; i += 32) {
+            const int w = i / nch, c = i - w * nch;
+            g[w * kWsChunks + c] = granules[w * kMaxChunksSampler + c] * ss.fac[w];
+        }
     }
     // Publish the piece and count its chunks in with one acquire-release add: the add that
     // reaches the row's total identifies the merging CTA, which then sees every piece.
@@ -793,10 +807,17 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
     // compacted in chunk order (at most 32 pieces: rows of <= 64 chunks in blocks of >= 4 chunks,
     // split at most once more at a row boundary).
     if constexpr (kSample) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(ws_granules(p, t, 0));
+        // Both tables are [warp][64 chunks]: each warp's row_chunks doubles in 16-byte copies (an
+        // odd count copies one unused double past them).
+        static_assert(kWsChunks == kMaxChunksSampler, "workspace and shared granule rows match");
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(ws_granules(p, t));
         const uint32_t dst = ptx::smem_addr(granules);
-        const int copies = row_chunks * kConsumerWarps * 8 / 16;
-        for (int i = lane; i < copies; i += 32) ptx::cp_async_16(dst + 16 * i, src + 16 * i);
+        const int pairs = (row_chunks + 1) / 2;
+        for (int i = lane; i < pairs * kConsumerWarps; i += 32) {
+            const int w = i / pairs, k = i - w * pairs;
+            const int off = (w * kMaxChunksSampler + 2 * k) * 8;
+            ptx::cp_async_16(dst + off, src + off);
+        }
     }
     auto head = [&](int c, uint32_t& epoch, GatherSlot& g) {
         const uint4* src = reinterpret_cast<const uint4*>(ws_piece(p, t, c));
@@ -866,7 +887,7 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
             // owner's rank factor.
             const int64_t b0 = static_cast<int64_t>(oc0) * kTPC;
             const int64_t b1 = static_cast<int64_t>(oc1) * kTPC < p.vocab ? static_cast<int64_t>(oc1) * kTPC : p.vocab;
-            chosen = sampler_owner_walk<T>(granules + oc0 * kConsumerWarps, (oc1 - oc0) * kConsumerWarps, 1.0, 1.0,
+            chosen = sampler_owner_walk<T>(granules + oc0, 1, kMaxChunksSampler, (oc1 - oc0) * kConsumerWarps, 1.0, 1.0,
                                            lane < kConsumerWarps, mg, p.temperature, p.inv_temperature, p.scale2, b0, b1,
                                            lrow, mrow, ss.walk, ss.fac, lane);
         }
@@ -1133,7 +1154,11 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         reinterpret_cast<double*>(rec + SamplerRecord::kWarpMassOffset)[lane] = wp.mass;
                     }
                     double* rg = reinterpret_cast<double*>(rec + SamplerRecord::kGranuleOffset);
-                    for (int g = lane; g < ngran; g += 32) rg[g] = granules[g];
+                    // The record is chunk-major ([chunk][warp]); the table warp-major.
+                    for (int i = lane; i < ngran; i += 32) {
+                        const int w = i / nch, c = i - w * nch;
+                        rg[c * kConsumerWarps + w] = granules[w * kMaxChunksSampler + c];
+                    }
                 } else if (d.kind == kUnitSplit) {
                     finish_split_piece<T, true>(p, d, nchunks, GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0},
                                                 wf, granules, sh.part_uniform[slot], sh, ss, lrow, mrow, lane);
@@ -1155,7 +1180,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         }
                     } else if (mg.owner == static_cast<int>(crank)) {
                         const int64_t chosen =
-                            sampler_owner_walk<T>(granules, ngran, wf, wp.mass, in, mg, p.temperature,
+                            sampler_owner_walk<T>(granules, 1, kMaxChunksSampler, ngran, wf, wp.mass, in, mg, p.temperature,
                                                   p.inv_temperature, p.scale2, seg_begin, seg_end, lrow, mrow, ss.walk,
                                                   ss.fac, lane);
                         if (lane == 0) {
@@ -1415,7 +1440,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
                         if (fast) mass *= corr;
                     }
-                    if (lane == 0) granules_f[(c - d.c0) * kConsumerWarps + warp] = make_float2(ref, mass);
+                    if (lane == 0) granules_f[warp * kMaxChunksSampler + (c - d.c0)] = make_float2(ref, mass);
                 }
                 if constexpr (kBulk) {
                     if (++stage == static_cast<uint32_t>(kStages)) {
@@ -1442,12 +1467,12 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 __syncwarp();
                 double local = 0.0;
                 for (int c = lane; c < nch; c += 32) {
-                    const float2 e = granules_f[c * kConsumerWarps + warp];
+                    const float2 e = granules_f[warp * kMaxChunksSampler + c];
                     const double gm = !(e.y > 0.0f) ? 0.0
                                       : e.x == ref  ? static_cast<double>(e.y)
                                                     : static_cast<double>(e.y) *
                                                           scaled_exp(static_cast<double>(e.x) - wm, p.temperature, p.inv_temperature);
-                    granules[c * kConsumerWarps + warp] = gm;
+                    granules[warp * kMaxChunksSampler + c] = gm;
                     local += gm;
                 }
                 wmass = warp_sum(local);
