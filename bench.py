@@ -821,9 +821,18 @@ def run_decode(args):
             secs = time.perf_counter() - t0
         return outs, secs, clocks.summary()
 
-    spec, spec_s, clocks = run(speculative_c4, draft)
+    eager, eager_s, _ = run(speculative_c4, draft)
     lazy, lazy_s, _ = run(lambda *a, **k: speculative_c4(*a, verify="lazy", **k), draft)
     greedy, greedy_s, _ = run(constrained_greedy)
+    # The same decoding with each model's embedding and blocks replayed from CUDA graphs (one per
+    # padded length, captured by the warm-up).
+    target.enable_graphs()
+    draft.enable_graphs()
+    speculative_c4(target, draft, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,), table=table)
+    constrained_greedy(target, prompts[0], grammar0.fork(), max_new_tokens=args.new_tokens, eos=(0,), table=table)
+    torch.cuda.synchronize(device)
+    spec, spec_s, clocks = run(speculative_c4, draft)
+    greedy_g, greedy_g_s, _ = run(constrained_greedy)
     tokens = sum(len(o.token_ids) for o in spec)
 
     def same(x, y):
@@ -836,22 +845,26 @@ def run_decode(args):
         "config": {"workload": (f"decode: c4 speculative decoding, {len(prompts)} prompts x 64 random tokens, "
                                 f"{args.new_tokens} new tokens; target 4 layers d=1024 16 heads, draft 1 layer "
                                 "d=512, V=248320 bf16 random-init; 64-state token DFA grammar, EOS id 0; "
-                                "state masks resident on the device"),
+                                "state masks resident on the device; model trunks replayed from CUDA graphs"),
                    "rounds": sum(o.rounds for o in spec), "proposed": sum(o.proposed for o in spec),
                    "accepted": sum(o.accepted for o in spec), "tokens": tokens,
                    "stop_reasons": {r: sum(o.stop_reason == r for o in spec) for r in ("eos", "grammar", "length")}},
         "selection_share_of_wall": sum(o.select_seconds for o in spec) / spec_s,
+        "eager_tokens_per_s": sum(len(o.token_ids) for o in eager) / eager_s,
+        "identical_to_eager": same(spec, eager),
         "lazy_verification_tokens_per_s": sum(len(o.token_ids) for o in lazy) / lazy_s,
         "lazy_selection_share_of_wall": sum(o.select_seconds for o in lazy) / lazy_s,
-        "identical_to_lazy_verification": same(spec, lazy),
-        "greedy_tokens_per_s": sum(len(o.token_ids) for o in greedy) / greedy_s,
-        "identical_to_greedy": same(spec, greedy),
-        "note": ("lazy verification = the reference's per-row loop on the same target rows (must be identical); "
-                 "greedy = target-only decoding, whose bf16 logits come from forwards of other lengths and may "
-                 "differ in near-ties"),
+        "identical_to_lazy_verification": same(eager, lazy),
+        "greedy_tokens_per_s": sum(len(o.token_ids) for o in greedy_g) / greedy_g_s,
+        "eager_greedy_tokens_per_s": sum(len(o.token_ids) for o in greedy) / greedy_s,
+        "identical_to_greedy": same(spec, greedy_g),
+        "note": ("value: c4 with CUDA-graph model trunks; eager = the same without graphs (must be identical); "
+                 "lazy verification = the reference's per-row loop on the same target rows, eager (must be "
+                 "identical); greedy = target-only decoding, whose bf16 logits come from forwards of other lengths "
+                 "and may differ in near-ties"),
         "roofline": None, "clocks": clocks,
         "e2e": {"value": tokens / spec_s, "unit": "tokens/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
-                "path": "decode.speculative_c4 per prompt (host wall clock, model forwards included)"},
+                "path": "decode.speculative_c4 per prompt (host wall clock, model forwards included, graphs)"},
     }
     print(json.dumps(line), flush=True)
 

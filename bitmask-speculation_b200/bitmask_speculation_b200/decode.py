@@ -89,6 +89,46 @@ def build_decoder(vocab: int, *, layers: int, dim: int, heads: int, kv_heads: in
             self.head = nn.Linear(dim, vocab, bias=False)
             inv = 1.0 / (1e6 ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
             self.register_buffer("inv_freq", inv.float(), persistent=False)
+            self._graphs = None  # padded length -> (CUDA graph, token buffer, trunk output, rotary tables)
+            self._pool = None
+
+        def _rope(self, length: int):
+            pos = torch.arange(length, device=self.inv_freq.device, dtype=torch.float32)
+            ang = pos[:, None] * self.inv_freq[None, :]
+            return ang.cos().to(self.head.weight.dtype), ang.sin().to(self.head.weight.dtype)
+
+        def _trunk(self, ids, cos, sin):
+            x = self.embed(ids)
+            for b in self.blocks:
+                x = b(x, cos, sin)
+            return x
+
+        def enable_graphs(self):
+            """Replay the embedding and the blocks from one CUDA graph per padded length (captured
+            on first use), so that a forward costs a handful of launches: the token copy, the graph
+            and the final norm and LM head of the requested rows.  The graph holds the same
+            kernels as the eager forward."""
+            if self._graphs is None:
+                self._graphs = {}
+                self._pool = torch.cuda.graph_pool_handle()
+            return self
+
+        def _captured(self, length: int):
+            entry = self._graphs.get(length)
+            if entry is None:
+                ids = torch.zeros(length, dtype=torch.long, device=self.head.weight.device)
+                cos, sin = self._rope(length)
+                side = torch.cuda.Stream(device=ids.device)
+                side.wait_stream(torch.cuda.current_stream(ids.device))
+                with torch.cuda.stream(side):
+                    for _ in range(2):  # library handles and workspaces exist before capture
+                        self._trunk(ids, cos, sin)
+                torch.cuda.current_stream(ids.device).wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, pool=self._pool):
+                    out = self._trunk(ids, cos, sin)
+                entry = self._graphs[length] = (graph, ids, out, cos, sin)
+            return entry
 
         @torch.inference_mode()
         def logits(self, tokens, first: int, rows: int):
@@ -97,13 +137,15 @@ def build_decoder(vocab: int, *, layers: int, dim: int, heads: int, kv_heads: in
             never reaches earlier positions) so that kernel shapes repeat across calls."""
             n = len(tokens)
             padded = list(tokens) + [0] * (-n % 64)
-            ids = torch.tensor(padded, dtype=torch.long).to(self.head.weight.device, non_blocking=True)
-            pos = torch.arange(ids.shape[0], device=ids.device, dtype=torch.float32)
-            ang = pos[:, None] * self.inv_freq[None, :]
-            cos, sin = ang.cos().to(self.head.weight.dtype), ang.sin().to(self.head.weight.dtype)
-            x = self.embed(ids)
-            for b in self.blocks:
-                x = b(x, cos, sin)
+            host = torch.tensor(padded, dtype=torch.long)
+            if self._graphs is not None:
+                graph, ids, out, _, _ = self._captured(len(padded))
+                ids.copy_(host, non_blocking=True)
+                graph.replay()
+                x = out
+            else:
+                ids = host.to(self.head.weight.device, non_blocking=True)
+                x = self._trunk(ids, *self._rope(ids.shape[0]))
             return self.head(self.norm(x[first:first + rows])).contiguous()
 
     gen = torch.Generator().manual_seed(seed)

@@ -68,3 +68,35 @@ def test_device_mask_table_decoding_equals_uploaded_masks(models):
         c = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=40, eos=(0,), table=table,
                            verify="lazy")
         assert a == b == c, i
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+def test_graph_replayed_trunk_matches_eager_forward(cuda_module, dtype):
+    """The CUDA-graph forward (one graph per padded length) holds the eager forward's kernels: the
+    logits of every requested slice are bit-identical, across lengths that reuse a graph."""
+    from bitmask_speculation_b200.decode import build_decoder, random_prompts
+    vocab = 8320
+    eager = build_decoder(vocab, layers=2, dim=256, heads=4, dtype=getattr(torch, dtype), seed=11)
+    graphed = build_decoder(vocab, layers=2, dim=256, heads=4, dtype=getattr(torch, dtype), seed=11).enable_graphs()
+    for prompt in random_prompts(3, 50, vocab, seed=12):
+        for n in (1, 14, 64, 65, 100):  # 64-token padded lengths 64, 128 and 64 again
+            seq = (prompt * 3)[:n]
+            for first, rows in ((n - 1, 1), (max(0, n - 9), min(9, n))):
+                a = eager.logits(seq, first, rows)
+                b = graphed.logits(seq, first, rows)
+                assert torch.equal(a, b), (dtype, n, first, rows)
+    assert sorted(graphed._graphs) == [64, 128]
+
+
+def test_speculative_c4_with_graphs_equals_eager(models):
+    from bitmask_speculation_b200.decode import build_decoder, constrained_greedy, random_prompts, speculative_c4
+    vocab, target, draft = models
+    g_target = build_decoder(vocab, layers=2, dim=256, heads=4, dtype=torch.float32, seed=1).enable_graphs()
+    g_draft = build_decoder(vocab, layers=1, dim=128, heads=2, dtype=torch.float32, seed=2).enable_graphs()
+    for i, prompt in enumerate(random_prompts(3, 16, vocab, seed=13)):
+        g0 = wl.SyntheticDFAGrammar(vocab, states=64, seed=40 + i)
+        a = speculative_c4(target, draft, prompt, g0.fork(), max_new_tokens=48, eos=(0,))
+        b = speculative_c4(g_target, g_draft, prompt, g0.fork(), max_new_tokens=48, eos=(0,))
+        c = constrained_greedy(g_target, prompt, g0.fork(), max_new_tokens=48, eos=(0,))
+        assert a == b, i
+        assert b.token_ids == c.token_ids, i
