@@ -61,6 +61,8 @@ def parse_args():
                     help="override every sampling row's mask density (default: the configuration's mix)")
     ap.add_argument("--sample-dtype", choices=["float16", "bfloat16"], default="float16",
                     help="logits type of the sampling workload (the configuration's rows are fp16)")
+    ap.add_argument("--p2p", action="store_true",
+                    help="vocab workload: exchange the shard partials through peer memory instead of NCCL")
     ap.add_argument("--no-workspace", action="store_true",
                     help="run the selection kernels on their fixed schedule (no dynamic-schedule workspace)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -249,8 +251,19 @@ class Workload:
             self.batches = 1
             self.esize = 2
             self.dtype = "bf16"
+            self.exchange = None
+            if args.p2p:
+                # Partials stored into every rank's exchange area by the selection kernel itself.
+                from bitmask_speculation_b200.sharding import PeerExchange
+                if world > 1:
+                    self.exchange = PeerExchange(args.rows, device=device)
+                else:
+                    own, _ = PeerExchange.create(device, 1, args.rows)
+                    self.exchange = PeerExchange(args.rows, areas=[own], rank=0, device=device)
+            self.transport = ("peer-memory exchange of 32-byte partials (stores over NVLink from the selection "
+                              "kernel, epoch flags)" if args.p2p else "NCCL all-gather of 32-byte partials")
             self.name = (f"vocab-sharded: {args.rows} rows bf16 N(0,3^2) at V=248320 split {world} ways, "
-                         "log-uniform mask density; NCCL all-gather of 32-byte partials")
+                         f"log-uniform mask density; {self.transport}")
         else:
             self.logits, self.masks = wl.scale_rows_torch(args.rows, seed=5 + 1000 * rank, device=device)
             self.rows = args.rows
@@ -325,7 +338,8 @@ class Workload:
                 self.seq_status.data_ptr(), None, 0, *self.workspace(), dev, stream_handle)
         elif self.kind == "vocab":
             from bitmask_speculation_b200.sharding import vocab_sharded_select
-            self.row_tokens, self.row_counts, self.row_status = vocab_sharded_select(logits, masks, self.vocab)
+            self.row_tokens, self.row_counts, self.row_status = vocab_sharded_select(
+                logits, masks, self.vocab, exchange=self.exchange)
             return
         elif self.kind == "sample":
             b = (self.step_index - 1) % self.batches
@@ -757,7 +771,7 @@ def run_b200_arm(args):
                    "bytes_per_row": w.bytes_per_row,
                    "l2": (f"inputs {w.rows * w.bytes_per_row * w.batches / 1e9:.2f} GB per GPU rotated "
                           f"({w.batches} batch(es)) > 126 MB L2; no flush"),
-                   "parallelism": (f"vocab-sharded x{world}, NCCL all-gather of partials" if w.kind == "vocab"
+                   "parallelism": (f"vocab-sharded x{world}, {w.transport}" if w.kind == "vocab"
                                    else f"row-sharded x{world}, no collective")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,

@@ -35,7 +35,15 @@ EXPORTS = (
     "bms_masked_reduce_batch", "bms_masked_sample", "bms_masked_sample_batch",
     "bms_mask_budget", "bms_verify_batch", "bms_set_launch_override", "bms_shard_granule_bytes",
     "bms_shard_partials", "bms_shard_merge", "bms_workspace_bytes", "bms_masked_reduce_batch_noalloc",
+    "bms_exchange_bytes", "bms_exchange_create", "bms_exchange_open", "bms_exchange_close", "bms_exchange_destroy",
+    "bms_shard_partials_exchange", "bms_shard_merge_exchange",
 )
+
+
+class IpcHandle(ctypes.Structure):
+    """``bms_ipc_handle``: an exported exchange area (cudaIpcMemHandle_t)."""
+
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 def _declare(lib) -> None:
@@ -56,6 +64,12 @@ def _declare(lib) -> None:
         "bms_set_launch_override": [i32, i32],
         "bms_shard_partials": [p, i32, p, i64, i64, i64, i64, f64, p, p, i64, i32, p],
         "bms_shard_merge": [p, i32, i32, i64, f64, p, p, i32, p, i64, i64, i64, p, i64, p, p, p, i32, p],
+        "bms_exchange_create": [i32, i32, i64, ctypes.POINTER(p), ctypes.POINTER(IpcHandle)],
+        "bms_exchange_open": [i32, ctypes.POINTER(IpcHandle), ctypes.POINTER(p)],
+        "bms_exchange_close": [i32, p],
+        "bms_exchange_destroy": [i32, p],
+        "bms_shard_partials_exchange": [p, i32, p, i64, i64, i64, i64, p, i32, i32, i64, ctypes.c_uint32, i32, p],
+        "bms_shard_merge_exchange": [p, i32, i32, i64, ctypes.c_uint32, i64, p, p, p, i32, p],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -65,6 +79,8 @@ def _declare(lib) -> None:
     lib.bms_shard_granule_bytes.restype = i64
     lib.bms_workspace_bytes.argtypes = [i32]
     lib.bms_workspace_bytes.restype = i64
+    lib.bms_exchange_bytes.argtypes = [i32, i64]
+    lib.bms_exchange_bytes.restype = i64
 
 
 def library():

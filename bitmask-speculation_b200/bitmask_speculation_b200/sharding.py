@@ -11,6 +11,11 @@ partials are all-gathered over NCCL in rank order, and every rank merges them
 sampling, the rank holding the crossing walks its shard and a max all-reduce shares the token.
 Argmax, counts and status are identical on every rank; a single-GPU run whose cluster ranks cover
 the same slices (cluster size = world size) gives bit-identical results.
+
+``PeerExchange`` replaces the all-gather for argmax steps (at most 8 ranks, one GPU each): every
+rank maps every other rank's exchange area (CUDA IPC over NVLink), the selection kernel stores
+each row's partial into all areas while it streams, and the merge waits on epoch flags in its
+own area -- no collective call on the data path.
 """
 
 from __future__ import annotations
@@ -85,20 +90,114 @@ class NativeShardBackend:
         return tokens, counts, status
 
 
+class PeerExchange:
+    """Exchange areas of a vocabulary-sharded group (``bms_exchange_*``): this rank's own area and
+    the peers' mapped areas in rank order, for batches of at most ``rows_cap`` rows.  ``areas`` may
+    be given directly (ranks emulated in one process on one device); otherwise the areas are
+    created and exported on every rank of ``group`` and the handles all-gathered once.  Every rank
+    runs the same steps in the same order; ``step`` is the epoch of the last one."""
+
+    def __init__(self, rows_cap: int, *, group=None, device=None, areas=None, rank=None):
+        import torch
+        self.rows_cap = int(rows_cap)
+        self._lib = _native.library()
+        self._owned = []
+        self._opened = []
+        self.step = 0
+        if areas is not None:
+            self.ranks, self.rank = len(areas), int(rank)
+            self.device = torch.device(device)
+            self.areas = list(areas)
+        else:
+            import torch.distributed as dist
+            self.rank, self.ranks = dist.get_rank(group), dist.get_world_size(group)
+            self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            own, handle = self.create(self.device, self.ranks, self.rows_cap)
+            self._owned.append(own)
+            mine = torch.tensor(bytearray(bytes(handle.bytes)), dtype=torch.uint8, device=self.device)
+            allh = torch.empty((self.ranks, 64), dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(allh, mine, group=group)
+            allh = allh.cpu().numpy()
+            self.areas = []
+            for q in range(self.ranks):
+                if q == self.rank:
+                    self.areas.append(own)
+                    continue
+                h = _native.IpcHandle()
+                ctypes.memmove(h.bytes, bytes(allh[q]), 64)
+                ptr = ctypes.c_void_p()
+                _native.check(self._lib.bms_exchange_open(self.device.index, ctypes.byref(h), ctypes.byref(ptr)))
+                self._opened.append(ptr.value)
+                self.areas.append(ptr.value)
+            dist.barrier(group=group)  # every peer mapped before any step stores into it
+        self._areas_c = (ctypes.c_void_p * self.ranks)(*self.areas)
+
+    @staticmethod
+    def create(device, ranks: int, rows_cap: int):
+        """Allocate one zeroed exchange area on ``device``: (device pointer, IPC handle)."""
+        lib = _native.library()
+        ptr, handle = ctypes.c_void_p(), _native.IpcHandle()
+        _native.check(lib.bms_exchange_create(device.index, ranks, rows_cap, ctypes.byref(ptr), ctypes.byref(handle)))
+        return ptr.value, handle
+
+    @staticmethod
+    def destroy(device, area):
+        _native.check(_native.library().bms_exchange_destroy(device.index, area))
+
+    def close(self):
+        """Unmap the peers' areas and free this rank's own (call on every rank, after its last step
+        and a barrier, so that no peer still stores into it)."""
+        for a in self._opened:
+            _native.check(self._lib.bms_exchange_close(self.device.index, a))
+        for a in self._owned:
+            self.destroy(self.device, a)
+        self._opened, self._owned = [], []
+
+    def partials(self, logits_shard, masks, token_offset: int, step: int):
+        import torch
+        rows, vocab_shard = logits_shard.shape
+        dtype = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[logits_shard.dtype]
+        _native.check(self._lib.bms_shard_partials_exchange(
+            logits_shard.data_ptr(), dtype, masks.data_ptr(), masks.shape[1], rows, vocab_shard, token_offset,
+            self._areas_c, self.ranks, self.rank, self.rows_cap, step, self.device.index,
+            torch.cuda.current_stream(self.device).cuda_stream))
+
+    def merge(self, rows: int, step: int):
+        import torch
+        tokens = torch.empty(rows, dtype=torch.int64, device=self.device)
+        counts = torch.empty(rows, dtype=torch.int64, device=self.device)
+        status = torch.empty(rows, dtype=torch.int32, device=self.device)
+        _native.check(self._lib.bms_shard_merge_exchange(
+            self._areas_c, self.ranks, self.rank, self.rows_cap, step, rows, tokens.data_ptr(), counts.data_ptr(),
+            status.data_ptr(), self.device.index, torch.cuda.current_stream(self.device).cuda_stream))
+        return tokens, counts, status
+
+    def select(self, logits_shard, masks, token_offset: int):
+        """One argmax step: this rank's partials into every area, then the merge of the step."""
+        if logits_shard.shape[0] > self.rows_cap:
+            raise ValueError(f"{logits_shard.shape[0]} rows exceed the exchange's rows_cap {self.rows_cap}")
+        self.step += 1
+        self.partials(logits_shard, masks, token_offset, self.step)
+        return self.merge(logits_shard.shape[0], self.step)
+
+
 def vocab_sharded_select(logits_shard, masks, vocab: int, *, temperature: float = 0.0, uniforms=None,
-                         group=None, backend=None):
+                         group=None, backend=None, exchange: PeerExchange | None = None):
     """Masked argmax (temperature 0) or sample of rows whose vocabulary is split across ranks.
 
     ``logits_shard`` is this rank's [rows, size] slice (``shard_bounds(vocab, world)[rank]``),
     ``masks`` the full [rows, ceil(vocab / 32)] mask rows, ``uniforms`` float64 [rows] (sampling;
     the same values on every rank).  Returns (tokens, counts, status), identical on every rank.
-    One all-gather of 32-byte partials (plus one max all-reduce when sampling).
+    One all-gather of 32-byte partials (plus one max all-reduce when sampling); with ``exchange``
+    (argmax only) the partials travel through peer memory instead and no collective is called.
     """
     import torch
     import torch.distributed as dist
     backend = backend or NativeShardBackend()
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
+    if exchange is not None:
+        rank, world = exchange.rank, exchange.ranks
+    else:
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
     offset, size = shard_bounds(vocab, world)[rank]
     rows = logits_shard.shape[0]
     if logits_shard.shape[1] != size:
@@ -107,6 +206,10 @@ def vocab_sharded_select(logits_shard, masks, vocab: int, *, temperature: float 
         raise ValueError("masks must be the full [rows, ceil(vocab / 32)] rows")
     if temperature != 0 and (uniforms is None or uniforms.shape != (rows,)):
         raise ValueError("sampling needs one float64 uniform per row")
+    if exchange is not None:
+        if temperature != 0:
+            raise ValueError("the peer-memory exchange carries argmax partials only (temperature 0)")
+        return exchange.select(logits_shard, masks, offset)
     partials, aux = backend.partials(logits_shard, masks, offset, temperature)
     flat = torch.empty((world * rows, PARTIAL_BYTES), dtype=partials.dtype, device=partials.device)
     dist.all_gather_into_tensor(flat, partials, group=group)

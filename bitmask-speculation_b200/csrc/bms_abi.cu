@@ -166,6 +166,11 @@ int cluster_index(int c) {
     return 0;
 }
 
+// Every rank's exchange area, passed by value to the merge kernel.
+struct ExchangeAreas {
+    uint8_t* a[kMaxExchangeRanks];
+};
+
 struct Plan {
     int cluster;
     int clusters;
@@ -492,6 +497,63 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
                 tokens[row] = token;
                 if (counts) counts[row] = mg.total;
             }
+        }
+    }
+}
+
+// Merge of a peer-memory exchange step (argmax partials), one warp per row (grid-stride) over
+// this rank's area: waits (bounded) until every rank published the step, merges exactly like
+// shard_merge_kernel, then the last CTA tells every rank that this rank's slot of the step is
+// free again.  A wait that gives up reports status 7 for the CTA's rows.
+__global__ void __launch_bounds__(128) exchange_merge_kernel(ExchangeAreas areas, int32_t ranks, int32_t rank,
+                                                             int64_t rows_cap, uint32_t epoch, int64_t rows,
+                                                             int64_t* __restrict__ tokens, int64_t* __restrict__ counts,
+                                                             int32_t* __restrict__ status) {
+    __shared__ int32_t gave_up;
+    ExchangeHeader* own = reinterpret_cast<ExchangeHeader*>(areas.a[rank]);
+    // An empty step has no partials to wait for (its selection launches nothing).
+    if (threadIdx.x == 0) gave_up = (rows == 0 || wait_flags_at_least(own->ready, ranks, epoch)) ? 0 : 1;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wib; row < rows; row += nwarps) {
+        if (gave_up) {
+            if (lane == 0) {
+                status[row] = kTimeout;
+                tokens[row] = -1;
+                if (counts) counts[row] = 0;
+            }
+            continue;
+        }
+        const bool in = lane < ranks;
+        GatherSlot g{0u, 0u, 0u, 0u, 0.0, 0.0};
+        if (in) {  // written by peer GPUs: read through L2
+            const uint4 x = __ldcg(reinterpret_cast<const uint4*>(exchange_slot(areas.a[rank], ranks, rows_cap, epoch, lane) + row));
+            g.a = x.x;
+            g.b = x.y;
+            g.c = x.z;
+            g.d = x.w;
+        }
+        const uint32_t hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
+        const uint32_t lo = __reduce_max_sync(0xFFFFFFFFu, (in && g.a == hi) ? g.b : 0u);
+        const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, g.c);
+        const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, g.d);
+        if (lane == 0) {
+            const int32_t code = argmax_status(fl, total);
+            status[row] = code;
+            tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
+            if (counts) counts[row] = total;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const uint32_t before = atomicAdd(&own->merge_done, 1u);
+        if (before + 1u == gridDim.x) {
+            atomicExch(&own->merge_done, 0u);
+            __threadfence_system();
+            for (int q = 0; q < ranks; ++q)
+                ptx::st_release_sys(&reinterpret_cast<ExchangeHeader*>(areas.a[q])->consumed[rank], epoch);
         }
     }
 }
@@ -912,6 +974,137 @@ int bms_shard_merge(const bms_partial* partials, int32_t shards, int32_t shard, 
                                                               granule_stride, tokens, counts, status);
     }
     BMS_CUDA(cudaGetLastError(), "shard merge launch");
+    return BMS_SUCCESS;
+}
+
+// ---------------------------------------------------------------- peer-memory shard exchange
+static_assert(sizeof(bms_ipc_handle) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+
+int64_t bms_exchange_bytes(int32_t ranks, int64_t rows_cap) {
+    if (ranks < 1 || ranks > kMaxExchangeRanks || rows_cap < 1) return -1;
+    return exchange_bytes(ranks, rows_cap);
+}
+
+int bms_exchange_create(int32_t device, int32_t ranks, int64_t rows_cap, void** area, bms_ipc_handle* handle) {
+    if (area == nullptr || handle == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "area and handle must not be NULL");
+    if (ranks < 1 || ranks > kMaxExchangeRanks) return fail(BMS_ERROR_INVALID_ARGUMENT, "ranks must be in [1, 8]");
+    if (rows_cap < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows_cap must be positive");
+    BMS_CHECK(check_device(device));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    void* p = nullptr;
+    const size_t bytes = static_cast<size_t>(exchange_bytes(ranks, rows_cap));
+    BMS_CUDA(cudaMalloc(&p, bytes), "exchange area allocation");
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(BMS_ERROR_CUDA, "exchange area export: %s", cudaGetErrorString(e));
+    }
+    memcpy(handle->bytes, &h, sizeof(h));
+    *area = p;
+    return BMS_SUCCESS;
+}
+
+int bms_exchange_open(int32_t device, const bms_ipc_handle* handle, void** area) {
+    if (area == nullptr || handle == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "area and handle must not be NULL");
+    BMS_CHECK(check_device(device));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle->bytes, sizeof(h));
+    void* p = nullptr;
+    BMS_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "exchange area mapping");
+    *area = p;
+    return BMS_SUCCESS;
+}
+
+int bms_exchange_close(int32_t device, void* area) {
+    if (area == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "area must not be NULL");
+    BMS_CHECK(check_device(device));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    BMS_CUDA(cudaIpcCloseMemHandle(area), "exchange area unmapping");
+    return BMS_SUCCESS;
+}
+
+int bms_exchange_destroy(int32_t device, void* area) {
+    if (area == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "area must not be NULL");
+    BMS_CHECK(check_device(device));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    BMS_CUDA(cudaFree(area), "exchange area release");
+    return BMS_SUCCESS;
+}
+
+namespace {
+int check_exchange(void* const* areas, int32_t ranks, int32_t rank, int64_t rows_cap, uint32_t epoch, int64_t rows,
+                   int device) {
+    if (areas == nullptr) return fail(BMS_ERROR_INVALID_ARGUMENT, "areas must not be NULL");
+    if (ranks < 1 || ranks > kMaxExchangeRanks) return fail(BMS_ERROR_INVALID_ARGUMENT, "ranks must be in [1, 8]");
+    if (rank < 0 || rank >= ranks) return fail(BMS_ERROR_INVALID_ARGUMENT, "rank must be in [0, ranks)");
+    if (rows_cap < 1 || rows > rows_cap) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows exceed the exchange area's rows_cap");
+    if (epoch == 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "epoch must be at least 1");
+    for (int q = 0; q < ranks; ++q)
+        if (areas[q] == nullptr || reinterpret_cast<uintptr_t>(areas[q]) % 256 != 0)
+            return fail(BMS_ERROR_INVALID_ARGUMENT, "exchange areas must be non-NULL and 256-byte aligned");
+    return check_ptr(areas[rank], device, "this rank's exchange area", 256);
+}
+}  // namespace
+
+int bms_shard_partials_exchange(const void* logits, int32_t dtype, const int32_t* masks, int64_t mask_words,
+                                int64_t rows, int64_t vocab_shard, int64_t token_offset, void* const* areas,
+                                int32_t ranks, int32_t rank, int64_t rows_cap, uint32_t epoch, int32_t device,
+                                void* stream) {
+    if (token_offset < 0 || token_offset % 32 != 0)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "token_offset must be a nonnegative multiple of 32");
+    BMS_CHECK(check_vocab(vocab_shard));
+    if (token_offset + vocab_shard > 2147483647LL) return fail(BMS_ERROR_INVALID_ARGUMENT, "vocabulary exceeds int32");
+    if (mask_words < (token_offset + vocab_shard + 31) / 32)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "mask_words must cover token_offset + vocab_shard");
+    BMS_CHECK(select_common(dtype, logits, masks, rows, vocab_shard, device));
+    BMS_CHECK(check_exchange(areas, ranks, rank, rows_cap, epoch, rows, device));
+    if (rows == 0) return BMS_SUCCESS;
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    SelectParams p = base_params(logits, masks, rows, vocab_shard);
+    p.mask_stride = mask_words;
+    p.mask_word_offset = token_offset / 32;
+    p.token_offset = token_offset;
+    for (int q = 0; q < ranks; ++q) {
+        p.xarea[q] = static_cast<uint8_t*>(areas[q]);
+        p.xpeer[q] = exchange_slot(p.xarea[q], ranks, rows_cap, epoch, rank);
+    }
+    p.partials = p.xpeer[rank];
+    p.xranks = ranks;
+    p.xrank = rank;
+    p.xepoch = epoch;
+    return launch_select<false>(dtype, p, device, static_cast<cudaStream_t>(stream));
+}
+
+int bms_shard_merge_exchange(void* const* areas, int32_t ranks, int32_t rank, int64_t rows_cap, uint32_t epoch,
+                             int64_t rows, int64_t* tokens, int64_t* counts, int32_t* status, int32_t device,
+                             void* stream) {
+    if (rows < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows must be nonnegative");
+    BMS_CHECK(check_device(device));
+    BMS_CHECK(check_exchange(areas, ranks, rank, rows_cap, epoch, rows, device));
+    BMS_CHECK(check_ptr(tokens, device, "tokens", 8));
+    if (counts) BMS_CHECK(check_ptr(counts, device, "counts", 8));
+    BMS_CHECK(check_ptr(status, device, "status", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    ExchangeAreas a{};
+    for (int q = 0; q < ranks; ++q) a.a[q] = static_cast<uint8_t*>(areas[q]);
+    // Every step launches at least one CTA: its last CTA releases this rank's slot even for an
+    // empty batch.
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
+    const int64_t need = rows > 0 ? (rows + 3) / 4 : 1;
+    const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+    exchange_merge_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(a, ranks, rank, rows_cap, epoch, rows,
+                                                                                 tokens, counts, status);
+    BMS_CUDA(cudaGetLastError(), "exchange merge launch");
     return BMS_SUCCESS;
 }
 

@@ -60,6 +60,7 @@ constexpr int kWarpBytes = kChunkBytes / kConsumerWarps;
 constexpr int kVecsPerLane = kWarpBytes / 16 / 32;  // 16-byte vectors per lane per chunk
 constexpr int kMaxCluster = 16;
 constexpr int kMaxChunksSampler = 64;  // granule table capacity (chunks per segment)
+constexpr int kMaxExchangeRanks = 8;   // ranks of a peer-memory shard exchange
 constexpr uint64_t kTimeoutNs = 1000000000ull;
 // Sampler: a lane mass above 2^20 raises the warp's reference max (no weight exceeds 2^20).
 constexpr float kRaiseMass = 0x1p20f;
@@ -300,7 +301,54 @@ struct SelectParams {
     // an index outside [0, mask_table_rows) fails the row with status 8
     const int32_t* mask_rows;
     int64_t mask_table_rows;
+    // peer-memory shard exchange (xranks > 0, argmax partials): every row's partial also goes to
+    // xpeer[q] + row, this rank's slot in rank q's exchange area (ExchangeHeader below)
+    GatherSlot* xpeer[kMaxExchangeRanks];
+    uint8_t* xarea[kMaxExchangeRanks];  // every rank's exchange area (xarea[xrank] is this rank's)
+    int32_t xranks;
+    int32_t xrank;
+    uint32_t xepoch;                    // this exchange step, >= 1, one more per step
 };
+
+// ----------------------------------------------------------------- peer-memory shard exchange
+// Each rank of a vocabulary-sharded group owns one exchange area in its device memory, mapped
+// by every peer (CUDA IPC): a header of epoch flags, then partial slots [2][ranks][rows_cap],
+// double-buffered by epoch parity.  Step e: rank q's selection launch waits until every rank
+// has merged step e - 2 (consumed[r] in q's own area, so slot e & 1 is free everywhere), stores
+// each row's partial into slot e & 1 of every area at [q][row] while it streams, and its last
+// CTA publishes ready[q] = e in every area (release, system scope).  Rank r's merge launch waits
+// for ready[q] >= e of every rank q in its own area, merges, and its last CTA publishes
+// consumed[r] = e in every area.  Every wait is bounded; a selection launch that gave up stores
+// and publishes nothing, so the peers' merges report status 7.
+struct alignas(128) ExchangeHeader {
+    uint32_t ready[kMaxExchangeRanks];     // rank q's partials of step ready[q] are in this area
+    uint32_t consumed[kMaxExchangeRanks];  // rank r merged step consumed[r]
+    uint32_t select_done;                  // CTAs of this rank's running selection launch (+ 2^16 per timeout)
+    uint32_t merge_done;                   // CTAs of this rank's running merge launch
+};
+
+__host__ __device__ constexpr int64_t exchange_slots_offset() { return 256; }
+static_assert(sizeof(ExchangeHeader) <= exchange_slots_offset(), "exchange header fits before the slots");
+__host__ __device__ constexpr int64_t exchange_bytes(int64_t ranks, int64_t rows_cap) {
+    return exchange_slots_offset() + 2 * ranks * rows_cap * static_cast<int64_t>(sizeof(GatherSlot));
+}
+// Rank q's slot of step `epoch` in an area.
+__host__ __device__ inline GatherSlot* exchange_slot(uint8_t* area, int64_t ranks, int64_t rows_cap, uint32_t epoch,
+                                                     int64_t q) {
+    return reinterpret_cast<GatherSlot*>(area + exchange_slots_offset()) + ((epoch & 1u) * ranks + q) * rows_cap;
+}
+
+// Bounded wait (one second of %globaltimer) until flags[i] - target >= 0 (as signed) for every
+// i < n; false on time-out.
+__device__ inline bool wait_flags_at_least(const uint32_t* flags, int n, uint32_t target) {
+    const uint64_t t0 = ptx::globaltimer();
+    for (int i = 0; i < n; ++i) {
+        while (static_cast<int32_t>(ptx::ld_acquire_sys(flags + i) - target) < 0) {
+            if (ptx::globaltimer() - t0 > kTimeoutNs) return false;
+        }
+    }
+    return true;
+}
 
 // Order-preserving map of a non-NaN float to uint32 (-0.0 folded onto +0.0).
 __device__ __forceinline__ uint32_t ordered_bits(float v) {
@@ -963,6 +1011,15 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     // Launched as a programmatic dependent, this grid may have started while the previous grid in
     // the stream was still running: no global memory is touched before that grid completed.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Peer-memory exchange: slot xepoch & 1 is free in every area once every rank merged step
+    // xepoch - 2.  A CTA that gives up stores nothing to its peers (its rows report status 7).
+    if (p.xranks > 0) {
+        if (tid == 0) {
+            const ExchangeHeader* own = reinterpret_cast<const ExchangeHeader*>(p.xarea[p.xrank]);
+            if (!wait_flags_at_least(own->consumed, p.xranks, p.xepoch - 2u)) sh.abort = 1;
+        }
+        __syncthreads();
+    }
     // Every CTA of the cluster has initialised its barriers before any remote arrive.
     if (csize > 1) {
         ptx::cluster_arrive();
@@ -1112,7 +1169,11 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - static_cast<uint32_t>(p.token_offset + lo);
                 uint32_t total = cnt, fl = flags;
                 if (p.partials != nullptr) {  // vocabulary shard: the row's partial is the output
-                    if (lane == 0) p.partials[row] = GatherSlot{hi, lo, total, fl, 0.0, 0.0};
+                    const GatherSlot rec{hi, lo, total, fl, 0.0, 0.0};
+                    if (lane == 0) p.partials[row] = rec;
+                    // Peer-memory exchange: the same record in every other rank's area (NVLink
+                    // stores overlapping the streaming of the next rows).
+                    if (lane < p.xranks && lane != p.xrank && !sh.abort) p.xpeer[lane][row] = rec;
                     continue;
                 }
                 if (csize > 1) {
@@ -1194,6 +1255,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
             }
         }
+        if (p.xranks > 0) __threadfence_system();  // this warp's peer stores before the grid's release
     } else {
         // ------------------------------------------------------------ consumer warps
         uint32_t stage = 0, phase = 0;  // ring position of the next chunk (matches the producer)
@@ -1493,7 +1555,21 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     }
 
     // No CTA may exit while a peer can still write into its shared memory.
-    if (csize > 1 || dynamic) __syncthreads();
+    if (csize > 1 || dynamic || p.xranks > 0) __syncthreads();
+    // Peer-memory exchange: the last CTA to finish publishes this step in every area, unless a
+    // CTA gave up waiting (its rows' partials never reached the peers).
+    if (p.xranks > 0 && tid == 0) {
+        ExchangeHeader* own = reinterpret_cast<ExchangeHeader*>(p.xarea[p.xrank]);
+        __threadfence_system();
+        const uint32_t before = atomicAdd(&own->select_done, sh.abort ? 0x10001u : 1u);
+        if ((before & 0xFFFFu) + 1u == gridDim.x) {
+            atomicExch(&own->select_done, 0u);
+            __threadfence_system();
+            if ((before >> 16) == 0u && !sh.abort)
+                for (int q = 0; q < p.xranks; ++q)
+                    ptx::st_release_sys(&reinterpret_cast<ExchangeHeader*>(p.xarea[q])->ready[p.xrank], p.xepoch);
+        }
+    }
     if (csize > 1) {
         ptx::cluster_arrive();
         ptx::cluster_wait();

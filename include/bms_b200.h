@@ -199,6 +199,45 @@ BMS_API int bms_shard_merge(const bms_partial *partials, int32_t shards, int32_t
                             const void *granules, int64_t granule_stride, int64_t *tokens, int64_t *counts,
                             int32_t *status, int32_t device, void *stream);
 
+/* ---- Peer-memory exchange of argmax shard partials (no reference counterpart: it replaces the
+ * NCCL all-gather between bms_shard_partials and bms_shard_merge with stores over NVLink).
+ * Each rank of a group of `ranks` (<= 8, one GPU each) creates one exchange area in its device
+ * memory and exports it; every rank opens the peers' areas.  `areas` below is a host array of
+ * `ranks` device pointers in rank order: this rank's own area at [rank], the peers' mapped areas
+ * elsewhere.  Step `epoch` starts at 1 and grows by one per step on every rank.  A step is one
+ * bms_shard_partials_exchange and one bms_shard_merge_exchange per rank on the same stream; the
+ * selection kernel stores each row's partial into every area while it streams, the merge waits
+ * (bounded, about one second) until every rank's partials of the step arrived.  A wait that gives
+ * up reports status 7 (BMS_STATUS_TIMEOUT) for the affected rows. */
+typedef struct bms_ipc_handle {
+    unsigned char bytes[64]; /* cudaIpcMemHandle_t */
+} bms_ipc_handle;
+
+/* Bytes of one exchange area for `ranks` ranks and batches of at most `rows_cap` rows (-1 if invalid). */
+BMS_API int64_t bms_exchange_bytes(int32_t ranks, int64_t rows_cap);
+
+/* Allocate this rank's exchange area (zeroed) on `device` and export it. */
+BMS_API int bms_exchange_create(int32_t device, int32_t ranks, int64_t rows_cap, void **area,
+                                bms_ipc_handle *handle);
+
+/* Map a peer's exported area into this process (peer access enabled on demand). */
+BMS_API int bms_exchange_open(int32_t device, const bms_ipc_handle *handle, void **area);
+
+/* Unmap a peer's area / free this rank's own area. */
+BMS_API int bms_exchange_close(int32_t device, void *area);
+BMS_API int bms_exchange_destroy(int32_t device, void *area);
+
+/* bms_shard_partials at temperature 0 with every row's partial also stored into each rank's area. */
+BMS_API int bms_shard_partials_exchange(const void *logits, int32_t dtype, const int32_t *masks, int64_t mask_words,
+                                        int64_t rows, int64_t vocab_shard, int64_t token_offset,
+                                        void *const *areas, int32_t ranks, int32_t rank, int64_t rows_cap,
+                                        uint32_t epoch, int32_t device, void *stream);
+
+/* bms_shard_merge at temperature 0 over the step's partials in this rank's area. */
+BMS_API int bms_shard_merge_exchange(void *const *areas, int32_t ranks, int32_t rank, int64_t rows_cap,
+                                     uint32_t epoch, int64_t rows, int64_t *tokens, int64_t *counts,
+                                     int32_t *status, int32_t device, void *stream);
+
 /* Test hook: force the cluster size (1, 2, 4, 8 or 16) and the number of
  * clusters of the selection kernels' fixed schedule; 0 restores the automatic
  * choice.  With cluster 0 and a workspace, `clusters` caps the number of CTAs of
