@@ -339,12 +339,14 @@ __host__ __device__ inline GatherSlot* exchange_slot(uint8_t* area, int64_t rank
 }
 
 // Bounded wait (one second of %globaltimer) until flags[i] - target >= 0 (as signed) for every
-// i < n; false on time-out.
+// i < n; false on time-out.  Polls back off (__nanosleep) so that many waiting CTAs do not crowd
+// the flag's memory while a peer's store to it is on its way.
 __device__ inline bool wait_flags_at_least(const uint32_t* flags, int n, uint32_t target) {
     const uint64_t t0 = ptx::globaltimer();
     for (int i = 0; i < n; ++i) {
         while (static_cast<int32_t>(ptx::ld_acquire_sys(flags + i) - target) < 0) {
             if (ptx::globaltimer() - t0 > kTimeoutNs) return false;
+            __nanosleep(128);
         }
     }
     return true;
