@@ -547,11 +547,11 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(ExchangeAreas areas
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence_system();
+        ptx::fence_acq_rel_sys();
         const uint32_t before = atomicAdd(&own->merge_done, 1u);
         if (before + 1u == gridDim.x) {
             atomicExch(&own->merge_done, 0u);
-            __threadfence_system();
+            ptx::fence_acq_rel_sys();
             for (int q = 0; q < ranks; ++q)
                 ptx::st_release_sys(&reinterpret_cast<ExchangeHeader*>(areas.a[q])->consumed[rank], epoch);
         }

@@ -33,6 +33,10 @@ __device__ __forceinline__ void cp_async_16(uint32_t smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
 }
 
+// Release/acquire fence at system scope (peer GPUs included); lighter than fence.sc.sys
+// (__threadfence_system), and all that a release or acquire pattern needs.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // System-scope acquire load / release store of a 32-bit flag (peer GPUs' memory included).
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;

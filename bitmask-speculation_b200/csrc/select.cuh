@@ -1257,7 +1257,6 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
             }
         }
-        if (p.xranks > 0) __threadfence_system();  // this warp's peer stores before the grid's release
     } else {
         // ------------------------------------------------------------ consumer warps
         uint32_t stage = 0, phase = 0;  // ring position of the next chunk (matches the producer)
@@ -1559,14 +1558,16 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     // No CTA may exit while a peer can still write into its shared memory.
     if (csize > 1 || dynamic || p.xranks > 0) __syncthreads();
     // Peer-memory exchange: the last CTA to finish publishes this step in every area, unless a
-    // CTA gave up waiting (its rows' partials never reached the peers).
+    // CTA gave up waiting (its rows' partials never reached the peers).  The finalizer's peer
+    // stores precede the barrier above, which orders them before thread 0's release pattern
+    // (fence + counter); the release is cumulative, so a peer that acquires the flag sees them.
     if (p.xranks > 0 && tid == 0) {
         ExchangeHeader* own = reinterpret_cast<ExchangeHeader*>(p.xarea[p.xrank]);
-        __threadfence_system();
+        ptx::fence_acq_rel_sys();
         const uint32_t before = atomicAdd(&own->select_done, sh.abort ? 0x10001u : 1u);
         if ((before & 0xFFFFu) + 1u == gridDim.x) {
             atomicExch(&own->select_done, 0u);
-            __threadfence_system();
+            ptx::fence_acq_rel_sys();
             if ((before >> 16) == 0u && !sh.abort)
                 for (int q = 0; q < p.xranks; ++q)
                     ptx::st_release_sys(&reinterpret_cast<ExchangeHeader*>(p.xarea[q])->ready[p.xrank], p.xepoch);
