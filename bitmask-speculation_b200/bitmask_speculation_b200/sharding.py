@@ -104,14 +104,16 @@ class PeerExchange:
         self._owned = []
         self._opened = []
         self.step = 0
+        device = torch.device("cuda") if device is None else torch.device(device)
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = device
         if areas is not None:
             self.ranks, self.rank = len(areas), int(rank)
-            self.device = torch.device(device)
             self.areas = list(areas)
         else:
             import torch.distributed as dist
             self.rank, self.ranks = dist.get_rank(group), dist.get_world_size(group)
-            self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
             own, handle = self.create(self.device, self.ranks, self.rows_cap)
             self._owned.append(own)
             mine = torch.tensor(bytearray(bytes(handle.bytes)), dtype=torch.uint8, device=self.device)
