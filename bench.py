@@ -38,8 +38,7 @@ sys.path.insert(0, str(ROOT))
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per row from one ncu capture of the dominant kernel
-# on a smaller case of the same workload (profiles/select_rows_bf16_verify.md and
-# profiles/select_rows_f16_sample.md); traffic grows with the rows processed.
+# on a smaller case of the same workload; traffic grows with the rows processed.
 NCU_TRAFFIC_PER_ROW = {"verify": 533530, "sample": 533980}
 
 
@@ -67,6 +66,8 @@ def parse_args():
                     help="run the selection kernels on their fixed schedule (no dynamic-schedule workspace)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sampler-roofline", action="store_true",
+                    help="skip the sampler's roofline lines (256 and 2,304 fp16 rows) of the default run")
     ap.add_argument("--roofline-seconds", type=float, default=1.5)
     ap.add_argument("--cluster", type=int, default=0,
                     help="force the selection kernel's cluster size (1/2/4/8/16; 0 = automatic)")
@@ -163,10 +164,8 @@ class Workload:
     def __init__(self, args, rank, device):
         import torch
         from bitmask_speculation_b200 import workloads as wl
-        from bitmask_speculation_b200.kernels._extension import load_extension
         self.args = args
         self.device = device
-        self.native = load_extension()
         self.kind = args.workload
         vocab = wl.VOCAB
         self.vocab = vocab
@@ -275,6 +274,12 @@ class Workload:
         self._alloc_outputs()
 
     @property
+    def native(self):
+        """The library's tensor front end (the b200 arm only: the reference arm never loads it)."""
+        from bitmask_speculation_b200.kernels._extension import load_extension
+        return load_extension()
+
+    @property
     def bytes_per_row(self):
         if self.kind == "vocab":  # this rank's slice of the logits and of the mask words
             return self.logits.shape[1] * self.esize + (self.logits.shape[1] // 32) * 4 + 20
@@ -338,8 +343,9 @@ class Workload:
                 self.seq_status.data_ptr(), None, 0, *self.workspace(), dev, stream_handle)
         elif self.kind == "vocab":
             from bitmask_speculation_b200.sharding import vocab_sharded_select
+            # Exchange statuses are checked once after the timed loop, not per step.
             self.row_tokens, self.row_counts, self.row_status = vocab_sharded_select(
-                logits, masks, self.vocab, exchange=self.exchange)
+                logits, masks, self.vocab, exchange=self.exchange, check_exchange=False)
             return
         elif self.kind == "sample":
             b = (self.step_index - 1) % self.batches
@@ -385,27 +391,57 @@ class Workload:
         rank = dist.get_rank() if dist.is_initialized() else 0
         return shard_bounds(self.vocab, self.world)[rank][0]
 
-    def check_against_oracle(self, max_rows=64):
-        """Untimed sanity check of the last step on a few rows (CPU oracle)."""
+    def check_against_oracle(self):
+        """Untimed check of one step against the CPU oracle on every row of the batch: tokens,
+        counts and statuses; for verification rounds also the budgets and every per-sequence
+        output (accepted length, token, kind, status); for the sampler the tokens within the
+        1e-6 CDF-boundary tolerance.  The vocabulary-sharded workload is checked by its tests."""
         import numpy as np
+        import torch
         import oracle
+        if self.kind == "vocab":
+            return
         self.step_index = 0
         logits, masks = self._batch()
-        n = min(max_rows, self.rows)
-        if self.kind in ("verify", "grammar", "scale", "argmax"):
-            self.step_index = 0
-            self.kernel_only(self.stream_handle())
-            import torch
-            torch.cuda.synchronize(self.device)
-            host = logits[:n].cpu()
-            dt = {"bf16": "bfloat16", "f16": "float16", "f32": None}[self.dtype]
-            vals = host.view(torch.int16).numpy().view(np.uint16) if dt else host.numpy()
-            exp = oracle.reduce_rows(vals, masks[:n].cpu().numpy(), dtype=dt)
-            got = (self.row_tokens[:n].cpu().numpy(), self.row_counts[:n].cpu().numpy(),
-                   self.row_status[:n].cpu().numpy())
-            for g, e in zip(got, exp):
-                if not np.array_equal(g, e):
-                    raise SystemExit("benchmark output differs from the oracle")
+        self.step(self.stream_handle())
+        torch.cuda.synchronize(self.device)
+        self.step_index = 0
+        dt = {"bf16": "bfloat16", "f16": "float16", "f32": None}[self.dtype]
+
+        def host(r0, r1):  # a slice of the batch in the oracle's format (bounded host memory)
+            part = logits[r0:r1].cpu()
+            return (part.view(torch.int16).numpy().view(np.uint16) if dt else part.numpy()), masks[r0:r1].cpu().numpy()
+
+        def same(name, got, want):
+            got = got.cpu().numpy() if hasattr(got, "cpu") else np.asarray(got)
+            bad = np.flatnonzero(got != want)
+            if bad.size:
+                raise SystemExit(f"benchmark output {name} differs from the oracle in {bad.size} rows "
+                                 f"(first {bad[:4].tolist()})")
+        if self.kind == "sample":
+            vals, m = host(0, self.rows)
+            u = self.uniforms_all[:self.rows].cpu().numpy()
+            tok, st = oracle.sample_rows(vals, m, self.temperature, u, dtype=dt)
+            same("status", self.row_status, st)
+            got = self.row_tokens.cpu().numpy()
+            for r in np.flatnonzero(got != tok):
+                row = oracle.widen(vals[r], dt) if dt else vals[r]
+                if not oracle.sample_matches(row, m[r], self.temperature, u[r], int(got[r]), int(tok[r])):
+                    raise SystemExit(f"benchmark sampler row {r} differs from the oracle beyond tolerance")
+            return
+        parts = [oracle.reduce_rows(*host(r0, min(self.rows, r0 + 4096)), dtype=dt) for r0 in range(0, self.rows, 4096)]
+        tok, cnt, st = (np.concatenate([p[i] for p in parts]) for i in range(3))
+        same("tokens", self.row_tokens, tok)
+        same("counts", self.row_counts, cnt)
+        same("status", self.row_status, st)
+        if self.kind in ("verify", "grammar"):
+            acc, token, kind, sst = oracle.verify(tok, st, self.proposals.cpu().numpy(), self.lengths.cpu().numpy())
+            _, budget = oracle.budget_rows(cnt, self.vocab)
+            same("row_budget", self.row_budget, budget)
+            same("accept_len", self.accept, acc)
+            same("token", self.token, token)
+            same("kind", self.kindout, kind)
+            same("seq_status", self.seq_status, sst)
 
     def stream_handle(self):
         import torch
@@ -605,6 +641,38 @@ def cpu_baseline_rows(w: Workload, budget_s=8.0):
 
 
 # ---------------------------------------------------------------- arms
+def bench_config(w: Workload, world: int) -> dict:
+    """The workload description both arms print (identical for the same arguments)."""
+    return {"workload": w.name, "rows_per_gpu": w.rows, "vocab": w.vocab, "bytes_per_row": w.bytes_per_row,
+            "l2": (f"inputs {w.rows * w.bytes_per_row * w.batches / 1e9:.2f} GB per GPU rotated "
+                   f"({w.batches} batch(es)) > 126 MB L2; no flush"),
+            "parallelism": (f"vocab-sharded x{world}, {w.transport}" if w.kind == "vocab"
+                            else f"row-sharded x{world}, no collective")}
+
+
+def sampler_roofline(args, device, peak, peak_kind, rows_list=(256, 2304)):
+    """The masked sampler alone at small and large batches (configuration-2 rows tiled, fp16,
+    T = 0.7, fresh uniforms; buffers rotated beyond L2): per-launch time and HBM fraction."""
+    import copy
+    out = {}
+    for rows in rows_list:
+        a = copy.copy(args)
+        a.workload, a.sample_rows, a.sample_density, a.sample_dtype = "sample", rows, None, "float16"
+        w = Workload(a, 0, device)
+        stream = w.stream_handle()
+        probe = timed_loop(lambda: w.kernel_only(stream), 3, device)
+        reps = max(20, int(0.75 / max(probe / 3, 1e-6)))
+        ktime = timed_loop(lambda: w.kernel_only(stream), reps, device)
+        kernel_s = ktime / reps
+        achieved = w.rows * w.bytes_per_row / kernel_s / 1e9
+        out[str(rows)] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                          "frac": achieved / peak, "peak_kind": peak_kind, "kernel_us": kernel_s * 1e6,
+                          "bytes_per_launch": w.rows * w.bytes_per_row, "launches": reps,
+                          "workload": w.name, "l2": f"{w.batches} rotated batches of {w.rows * w.bytes_per_row / 1e6:.0f} MB"}
+        del w
+    return out
+
+
 def run_reference_arm(args):
     """The reference algorithm on the host cores (oracle port, all threads), rank 0 only."""
     rank, world, local = dist_env()
@@ -667,12 +735,17 @@ def run_reference_arm(args):
         step()
     elapsed = time.perf_counter() - t0
     value = rows_per_step * args.steps / elapsed
+    port = ("oracle/oracle.c: the reference's CPU algorithm for the path restated in C (torch_reduce, "
+            "verify_prefix, DensityPolicy.budget; masked_sample_reference for sampling), OpenMP over "
+            f"{threads} host threads. The reference's own PyTorch/Python CPU path is slower than this port "
+            "(torch_reduce 508 rows/s on 8 threads at 64 bf16 rows), so ratios against it are conservative.")
     line = {
         "impl": "reference", "metric": "rows/s", "value": value, "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
-        "data": "synthetic (seeded)", "config": {"workload": w.name, "rows_per_step": rows_per_step},
-        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+        "higher_is_better": True, "scaling": "strong" if w.kind == "vocab" else "weak", "vs_baseline": None,
+        "dtype": w.dtype, "data": "synthetic (seeded, generated on device)", "config": bench_config(w, world),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample,
+                         "implementation": port},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -749,6 +822,13 @@ def run_b200_arm(args):
                    }.get(w.kind, "kernels.cuda.batched_masked_reduce (public API): pinned host masks H2D, "
                                  "device-resident logits, tokens and status D2H every step")}
 
+    sampler = None
+    if w.kind == "verify" and world == 1 and not args.no_sampler_roofline:
+        with ClockSampler(local) as sclocks:
+            sampler = sampler_roofline(args, device, peak, peak_kind)
+        sampler["clocks"] = sclocks.summary()
+    if w.kind == "vocab" and w.exchange is not None:
+        w.exchange.check_statuses(w.row_status)
     total_rows = w.rows if w.kind == "vocab" else w.rows * world  # vocab shards split the same rows
     value = total_rows * args.steps / seconds
     bytes_per_launch = w.rows * w.bytes_per_row
@@ -766,21 +846,18 @@ def run_b200_arm(args):
         "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3, "higher_is_better": True,
         "scaling": "strong" if w.kind == "vocab" else "weak", "vs_baseline": None, "dtype": w.dtype,
         "data": "synthetic (seeded, generated on device)",
-        "config": {"workload": w.name, "rows_per_gpu": w.rows, "vocab": w.vocab,
-                   "cluster": args.cluster or "auto",
-                   "bytes_per_row": w.bytes_per_row,
-                   "l2": (f"inputs {w.rows * w.bytes_per_row * w.batches / 1e9:.2f} GB per GPU rotated "
-                          f"({w.batches} batch(es)) > 126 MB L2; no flush"),
-                   "parallelism": (f"vocab-sharded x{world}, {w.transport}" if w.kind == "vocab"
-                                   else f"row-sharded x{world}, no collective")},
+        "config": bench_config(w, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": "select_rows_kernel (masked argmax + count)" if w.kind != "sample"
                      else "select_rows_kernel (masked sampler)",
-                     "kernel_us": kernel_s * 1e6, "bytes_per_launch": bytes_per_launch},
+                     "kernel_us": kernel_s * 1e6, "bytes_per_launch": bytes_per_launch,
+                     "cluster": args.cluster or "auto"},
         "gpu_launches": args.steps * w.launches_per_step(),
         "clocks": clocks.summary(),
     }
+    if sampler is not None:
+        line["roofline_sampler"] = sampler
     if e2e is not None:
         line["e2e"] = e2e
         if w.kind == "grammar":

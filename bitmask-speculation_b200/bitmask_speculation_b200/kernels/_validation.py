@@ -1,8 +1,10 @@
-"""Metadata validation before native dispatch; no device copies or compilation.
+"""Argument checks that run before anything is launched (tensor metadata only: no data is read,
+copied or moved).
 
-Mirrors kernels/_validation.py:6-60 of the reference with two deliberate
-extensions: float16/bfloat16 logits are accepted (the kernels read them
-natively) and batches are not capped at 65,535 rows.
+The checks, their order, exception types and messages are the reference's (kernels/_validation.py:
+6-60), because its callers and tests match on them.  Two checks are relaxed on purpose: float16 and
+bfloat16 logits pass (the kernels read them as they are), and a batch may hold more than 65,535
+rows.  ``uniforms_input`` is new: the batched sampler takes one float64 uniform per row.
 """
 
 from __future__ import annotations

@@ -1,9 +1,11 @@
-"""Explicit CUDA primitives; no implicit fallback or tensor copies.
+"""Tensor-level selection calls over the sm_100a library.
 
-Same functions, arguments, return types and errors as the reference's
-kernels/cuda.py:7-69 (``mask_count``, ``mask_density``, ``masked_argmax``,
-``masked_sample``, ``batched_masked_reduce``), backed by the sm_100a library,
-plus ``batched_masked_sample``.
+The functions a caller of the reference imports from kernels/cuda.py:7-69 --
+``mask_count``, ``mask_density``, ``masked_argmax``, ``masked_sample`` and
+``batched_masked_reduce`` -- with the same arguments, return types and errors,
+plus ``batched_masked_sample`` (one uniform per row).  Inputs must already be on
+the GPU: nothing here copies, widens or moves a tensor, and a missing library is
+an error, never a CPU computation.
 """
 
 from __future__ import annotations
@@ -25,20 +27,21 @@ _MESSAGES = {
 
 
 def mask_count(mask, vocab_size: int):
-    """Return an owned scalar int64 CUDA tensor; no host synchronization."""
+    """Valid tokens of one packed mask row, as a new 0-d int64 tensor on the mask's device.
+    Enqueued on the current stream; the host does not wait."""
     vocab_size = mask_input(mask, vocab_size)
     return load_extension().mask_count(mask, vocab_size)
 
 
 def mask_density(mask, vocab_size: int):
-    """Return a scalar float64 CUDA tensor including the count and division."""
+    """``mask_count / vocab_size`` as a 0-d float64 tensor on the device (no host wait)."""
     import torch
     return mask_count(mask, vocab_size).to(torch.float64) / vocab_size
 
 
 def _checked_selection(result):
     output, status = result[0], result[-1]
-    code = status.item()  # Explicit host synchronization to surface value errors.
+    code = status.item()  # the one device->host read of the call
     if code in _MESSAGES:
         raise ValueError(_MESSAGES[code])
     if code != 0:
@@ -47,38 +50,42 @@ def _checked_selection(result):
 
 
 def masked_argmax(logits, mask):
-    """Return the lowest-ID valid maximum as an owned scalar int64 CUDA tensor."""
+    """Highest-scoring allowed token of one row (ties: smallest ID) as a new 0-d int64 tensor.
+    Reads the status back to the host once, raising ValueError for NaN or an empty mask."""
     selection_inputs(logits, mask)
     return _checked_selection(load_extension().masked_argmax(logits, mask))
 
 
 def masked_sample(logits, mask, *, temperature: float = 1.0, generator=None):
-    """Sample masked softmax; temperature zero uses deterministic argmax.
+    """Draw one allowed token from softmax(logits / temperature) by inverse CDF.
 
-    Positive temperatures draw one float64 uniform on the input device using the
-    supplied PyTorch generator (or its default). Checked status synchronizes.
-    This is a standalone primitive, not stochastic speculative decoding.
+    ``temperature == 0`` is ``masked_argmax``.  Otherwise one float64 uniform is
+    drawn on the logits' device from ``generator`` (the device default if None),
+    after the library is loaded so that a load failure leaves the generator
+    untouched.  The status is read back once (ValueError on a data error).  One
+    row, one draw: speculative acceptance lives elsewhere.
     """
     import torch
     temperature = temperature_input(temperature)
     selection_inputs(logits, mask)
     if temperature == 0:
         return masked_argmax(logits, mask)
-    native = load_extension()  # Load errors must not consume generator state.
+    native = load_extension()  # before the draw: a failed load leaves the generator as it was
     uniform = torch.rand((), dtype=torch.float64, device=logits.device, generator=generator)
     return _checked_selection(native.masked_sample(logits, mask, temperature, uniform))
 
 
 @dataclass(frozen=True, slots=True)
 class BatchedMaskedReduction:
-    """Owned vectors, with one independent status per input row."""
+    """Per-row results of a batched call: token (-1 on error), valid count, status code.
+    ``check()`` reads the statuses back once and raises ValueError listing failed rows."""
 
     token_ids: object
     valid_counts: object
     status: object
 
     def check(self) -> "BatchedMaskedReduction":
-        codes = self.status.tolist()  # One explicit device-to-host synchronization.
+        codes = self.status.tolist()  # reads every row's status back in one transfer
         errors = [(row, code) for row, code in enumerate(codes) if code]
         if errors:
             raise ValueError(f"invalid reduction rows (row, status): {errors}")

@@ -174,24 +174,43 @@ class PeerExchange:
             status.data_ptr(), self.device.index, torch.cuda.current_stream(self.device).cuda_stream))
         return tokens, counts, status
 
-    def select(self, logits_shard, masks, token_offset: int):
-        """One argmax step: this rank's partials into every area, then the merge of the step."""
+    def select(self, logits_shard, masks, token_offset: int, *, check: bool = True):
+        """One argmax step: this rank's partials into every area, then the merge of the step.
+
+        Every rank must pass the same rows.  Status 7 marks rows whose partials did not arrive from
+        every rank -- a peer that stalled past the one-second device wait, or a peer whose step had
+        fewer rows.  With ``check`` (the default) that raises ``RuntimeError`` after the merge (one
+        device-to-host read of the statuses); with ``check=False`` the caller inspects the
+        statuses itself (``check_statuses``), e.g. once after many steps."""
         if logits_shard.shape[0] > self.rows_cap:
             raise ValueError(f"{logits_shard.shape[0]} rows exceed the exchange's rows_cap {self.rows_cap}")
         self.step += 1
         self.partials(logits_shard, masks, token_offset, self.step)
-        return self.merge(logits_shard.shape[0], self.step)
+        out = self.merge(logits_shard.shape[0], self.step)
+        if check:
+            self.check_statuses(out[2])
+        return out
+
+    @staticmethod
+    def check_statuses(status) -> None:
+        """Raise ``RuntimeError`` if any row of a merged exchange step reports status 7."""
+        bad = (status == 7).nonzero().flatten()
+        if bad.numel():
+            raise RuntimeError(f"peer-memory exchange: partials of {bad.numel()} rows did not arrive from every "
+                               f"rank (status 7; first row {int(bad[0])}): a peer stalled or passed other rows")
 
 
 def vocab_sharded_select(logits_shard, masks, vocab: int, *, temperature: float = 0.0, uniforms=None,
-                         group=None, backend=None, exchange: PeerExchange | None = None):
+                         group=None, backend=None, exchange: PeerExchange | None = None,
+                         check_exchange: bool = True):
     """Masked argmax (temperature 0) or sample of rows whose vocabulary is split across ranks.
 
     ``logits_shard`` is this rank's [rows, size] slice (``shard_bounds(vocab, world)[rank]``),
     ``masks`` the full [rows, ceil(vocab / 32)] mask rows, ``uniforms`` float64 [rows] (sampling;
     the same values on every rank).  Returns (tokens, counts, status), identical on every rank.
     One all-gather of 32-byte partials (plus one max all-reduce when sampling); with ``exchange``
-    (argmax only) the partials travel through peer memory instead and no collective is called.
+    (argmax only) the partials travel through peer memory instead and no collective is called
+    (``check_exchange``: raise on rows whose partials did not arrive, see ``PeerExchange.select``).
     """
     import torch
     import torch.distributed as dist
@@ -211,7 +230,7 @@ def vocab_sharded_select(logits_shard, masks, vocab: int, *, temperature: float 
     if exchange is not None:
         if temperature != 0:
             raise ValueError("the peer-memory exchange carries argmax partials only (temperature 0)")
-        return exchange.select(logits_shard, masks, offset)
+        return exchange.select(logits_shard, masks, offset, check=check_exchange)
     partials, aux = backend.partials(logits_shard, masks, offset, temperature)
     flat = torch.empty((world * rows, PARTIAL_BYTES), dtype=partials.dtype, device=partials.device)
     dist.all_gather_into_tensor(flat, partials, group=group)

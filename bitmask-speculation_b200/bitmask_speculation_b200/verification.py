@@ -21,7 +21,7 @@ from dataclasses import dataclass
 from typing import Literal
 
 from .kernels._validation import batched_selection_inputs, token_id
-from .scheduling import DensityPolicy
+from .scheduling import DensityPolicy, native_policy
 
 KINDS = {0: "correction", 1: "bonus", 2: "fallback"}
 _ROW_ERRORS = {
@@ -35,7 +35,11 @@ _ROW_ERRORS = {
 
 @dataclass(frozen=True, slots=True)
 class VerifiedToken:
-    """One target-confirmed choice, before request-level termination handling."""
+    """An event of a verified round: ``token_id`` and how the target confirmed it ("accepted"
+    draft token, "correction" at the first mismatch, "bonus" after a fully accepted draft, or
+    "fallback" for an empty draft).  Same fields and kinds as the reference's type
+    (decoding/verification.py:10-15), so its request loops consume these events unchanged; EOS,
+    length limits and grammar termination are the caller's business."""
 
     token_id: int
     kind: Literal["accepted", "correction", "bonus", "fallback"]
@@ -104,7 +108,7 @@ def verify_batch(logits, masks, proposals, lengths, *, policy=None, mask_rows=No
     if mask_rows is None:
         batched_selection_inputs(logits, masks)
     policy = DensityPolicy() if policy is None else policy
-    out = load_extension().verify_batch(logits, masks, proposals, lengths, policy.native(), mask_rows=mask_rows)
+    out = load_extension().verify_batch(logits, masks, proposals, lengths, native_policy(policy), mask_rows=mask_rows)
     return BatchVerification(**out)
 
 

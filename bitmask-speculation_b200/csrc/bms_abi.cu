@@ -504,7 +504,8 @@ __global__ void __launch_bounds__(128) shard_merge_kernel(
 // Merge of a peer-memory exchange step (argmax partials), one warp per row (grid-stride) over
 // this rank's area: waits (bounded) until every rank published the step, merges exactly like
 // shard_merge_kernel, then the last CTA tells every rank that this rank's slot of the step is
-// free again.  A wait that gives up reports status 7 for the CTA's rows.
+// free again.  A wait that gives up reports status 7 for the CTA's rows, and so does a row whose
+// partial from some rank carries another step's epoch tag (ranks that passed different row counts).
 __global__ void __launch_bounds__(128) exchange_merge_kernel(ExchangeAreas areas, int32_t ranks, int32_t rank,
                                                              int64_t rows_cap, uint32_t epoch, int64_t rows,
                                                              int64_t* __restrict__ tokens, int64_t* __restrict__ counts,
@@ -527,17 +528,21 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(ExchangeAreas areas
         }
         const bool in = lane < ranks;
         GatherSlot g{0u, 0u, 0u, 0u, 0.0, 0.0};
+        uint32_t tag = epoch;
         if (in) {  // written by peer GPUs: read through L2
-            const uint4 x = __ldcg(reinterpret_cast<const uint4*>(exchange_slot(areas.a[rank], ranks, rows_cap, epoch, lane) + row));
+            const uint4* src = reinterpret_cast<const uint4*>(exchange_slot(areas.a[rank], ranks, rows_cap, epoch, lane) + row);
+            const uint4 x = __ldcg(src), y = __ldcg(src + 1);
             g.a = x.x;
             g.b = x.y;
             g.c = x.z;
             g.d = x.w;
+            tag = y.z;  // low word of the slot's epoch tag (GatherSlot::pad)
         }
+        const bool stale = __any_sync(0xFFFFFFFFu, tag != epoch);
         const uint32_t hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
         const uint32_t lo = __reduce_max_sync(0xFFFFFFFFu, (in && g.a == hi) ? g.b : 0u);
         const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, g.c);
-        const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, g.d);
+        const uint32_t fl = __reduce_or_sync(0xFFFFFFFFu, g.d) | (stale ? kFlagAbort : 0u);
         if (lane == 0) {
             const int32_t code = argmax_status(fl, total);
             status[row] = code;

@@ -43,6 +43,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cstddef>
 #include <cstdint>
 #include <type_traits>
 
@@ -263,8 +264,9 @@ __device__ __forceinline__ float lane_mass_fast(const uint32_t (&q16)[kVecsPerLa
 struct alignas(16) GatherSlot {
     uint32_t a, b, c, d;
     double s;
-    double pad;
+    double pad;  // peer-memory exchange: the step's epoch (low word), read back by the merge
 };
+static_assert(sizeof(GatherSlot) == 32 && offsetof(GatherSlot, pad) == 24, "exchange merge reads the tag at byte 24");
 
 struct SelectParams {
     const void* logits;      // [rows, logit_stride] elements
@@ -1171,7 +1173,11 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - static_cast<uint32_t>(p.token_offset + lo);
                 uint32_t total = cnt, fl = flags;
                 if (p.partials != nullptr) {  // vocabulary shard: the row's partial is the output
-                    const GatherSlot rec{hi, lo, total, fl, 0.0, 0.0};
+                    GatherSlot rec{hi, lo, total, fl, 0.0, 0.0};
+                    // An exchange step tags each partial with its epoch, so that a merge finding
+                    // another tag in a rank's slot (that rank's step had fewer rows) fails the row
+                    // instead of merging a partial left there by an earlier step.
+                    if (p.xranks > 0) rec.pad = __longlong_as_double(static_cast<long long>(p.xepoch));
                     if (lane == 0) p.partials[row] = rec;
                     // Peer-memory exchange: the same record in every other rank's area (NVLink
                     // stores overlapping the streaming of the next rows).

@@ -208,7 +208,10 @@ BMS_API int bms_shard_merge(const bms_partial *partials, int32_t shards, int32_t
  * bms_shard_partials_exchange and one bms_shard_merge_exchange per rank on the same stream; the
  * selection kernel stores each row's partial into every area while it streams, the merge waits
  * (bounded, about one second) until every rank's partials of the step arrived.  A wait that gives
- * up reports status 7 (BMS_STATUS_TIMEOUT) for the affected rows. */
+ * up reports status 7 (BMS_STATUS_TIMEOUT) for the affected rows.  Every rank passes the same
+ * `rows` in a step: each partial carries its step's epoch, and a row whose partial from some rank
+ * has another epoch (that rank's step had fewer rows) also reports status 7.  Callers must check
+ * the statuses for 7; the ranks' results are then undefined for those rows. */
 typedef struct bms_ipc_handle {
     unsigned char bytes[64]; /* cudaIpcMemHandle_t */
 } bms_ipc_handle;

@@ -182,6 +182,41 @@ def widen(logits, dtype: str) -> np.ndarray:
     return out
 
 
+def cdf_interval(row_f32: np.ndarray, mask_row: np.ndarray, temperature: float, token: int):
+    """Normalised CDF interval [F(token-), F(token)] of the reference sampler's weights
+    exp((x - max) / T) over the valid finite logits of one float32 row (fp64, exact sums)."""
+    import math
+    vocab = row_f32.size
+    words = np.ascontiguousarray(mask_row, dtype=np.int32).view(np.uint32)
+    t = np.arange(vocab)
+    valid = ((words[t >> 5] >> (t & 31).astype(np.uint32)) & 1).astype(bool)
+    x = row_f32.astype(np.float64)
+    finite = valid & np.isfinite(x)
+    m = x[valid].max()
+    w = np.zeros(vocab)
+    with np.errstate(over="ignore", invalid="ignore"):
+        w[finite] = np.exp((x[finite] - m) / temperature)
+    total = math.fsum(w[valid])
+    cum = np.cumsum(w)
+    hi = cum[token] / total
+    lo = (cum[token] - w[token]) / total
+    return lo, hi
+
+
+def sample_matches(row_f32, mask_row, temperature, uniform, gpu_token, ref_token, tol=1e-6) -> bool:
+    """The sampler's parity rule: the GPU's token equals the reference's for the same uniform, or
+    u lies within ``tol`` (normalised CDF) of a boundary of the GPU's token's interval."""
+    if gpu_token == ref_token:
+        return True
+    if gpu_token < 0:
+        return False
+    lo, hi = cdf_interval(row_f32, mask_row, temperature, gpu_token)
+    if hi <= lo:  # a token of zero weight is never drawn
+        return False
+    dist = 0.0 if lo <= uniform < hi else min(abs(uniform - lo), abs(uniform - hi))
+    return dist <= tol
+
+
 def grammar_choices(draft, rows, grammar, *, dtype: str | None = None):
     """The reference's grammar-constrained verification loop (models/transformers.py:181-201:
     ``_choices`` + ``constrained_choices`` over decoding/verification.py:18-48 ``verify_prefix``),

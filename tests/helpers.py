@@ -2,8 +2,6 @@
 
 from __future__ import annotations
 
-import math
-
 import numpy as np
 
 TORCH_DTYPE_NAMES = ("float32", "bfloat16", "float16")
@@ -34,33 +32,12 @@ def widened(values: np.ndarray, dtype: str) -> np.ndarray:
     return oracle.widen(values, dtype)
 
 
-def cdf_interval(row_f32: np.ndarray, mask_row: np.ndarray, temperature: float, token: int):
-    """Normalised CDF interval [F(token-), F(token)] of the reference sampler (fp64)."""
-    vocab = row_f32.size
-    words = np.ascontiguousarray(mask_row, dtype=np.int32).view(np.uint32)
-    t = np.arange(vocab)
-    valid = ((words[t >> 5] >> (t & 31).astype(np.uint32)) & 1).astype(bool)
-    x = row_f32.astype(np.float64)
-    finite = valid & np.isfinite(x)
-    m = x[valid].max()
-    w = np.zeros(vocab)
-    with np.errstate(over="ignore", invalid="ignore"):
-        w[finite] = np.exp((x[finite] - m) / temperature)
-    total = math.fsum(w[valid])
-    cum = np.cumsum(w)
-    hi = cum[token] / total
-    lo = (cum[token] - w[token]) / total
-    return lo, hi
+def cdf_interval(row_f32, mask_row, temperature, token):
+    import oracle
+    return oracle.cdf_interval(row_f32, mask_row, temperature, token)
 
 
 def sample_matches(row_f32, mask_row, temperature, uniform, gpu_token, ref_token, tol=1e-6) -> bool:
     """Identical, or u within ``tol`` (normalised) of a CDF boundary of the GPU's token."""
-    if gpu_token == ref_token:
-        return True
-    if gpu_token < 0:
-        return False
-    lo, hi = cdf_interval(row_f32, mask_row, temperature, gpu_token)
-    if hi <= lo:  # zero-weight token can never be drawn
-        return False
-    dist = 0.0 if lo <= uniform < hi else min(abs(uniform - lo), abs(uniform - hi))
-    return dist <= tol
+    import oracle
+    return oracle.sample_matches(row_f32, mask_row, temperature, uniform, gpu_token, ref_token, tol)

@@ -81,6 +81,38 @@ def test_unpublished_step_times_out_then_recovers(cuda_module):
             PeerExchange.destroy(dev, a)
 
 
+def test_rows_a_peer_did_not_publish_fail_with_status_7(cuda_module):
+    """Ranks must pass the same rows.  If one rank's step has fewer rows, the slots past its batch
+    still hold partials of the step two earlier (same slot parity); their epoch tag fails those
+    rows with status 7 instead of merging stale partials, and ``check_statuses`` raises."""
+    from bitmask_speculation_b200.sharding import PeerExchange, shard_bounds
+    dev = torch.device("cuda", 0)
+    areas = [PeerExchange.create(dev, 2, 64)[0] for _ in range(2)]
+    bounds = shard_bounds(wl.VOCAB, 2)
+    try:
+        ex = [PeerExchange(64, areas=areas, rank=q, device=dev) for q in range(2)]
+        for step, rows1 in ((1, 40), (2, 40), (3, 30)):
+            logits, masks = wl.scale_rows_torch(40, seed=80 + step, device=dev)
+            want = _reference(cuda_module, logits, masks)
+            for q, (off, size) in enumerate(bounds):
+                n = 40 if q == 0 else rows1
+                ex[q].partials(logits[:n, off:off + size].contiguous(), masks[:n].contiguous(), off, step)
+            tokens, counts, status = (t.cpu() for t in ex[0].merge(40, step))
+            if step < 3:
+                assert torch.equal(tokens, want[0]) and torch.equal(status, want[2])
+                ex[1].merge(40, step)
+                continue
+            assert torch.equal(tokens[:30], want[0][:30]) and torch.equal(counts[:30], want[1][:30])
+            assert torch.all(status[30:] == STATUS_TIMEOUT) and torch.all(tokens[30:] == -1)
+            with pytest.raises(RuntimeError, match="did not arrive"):
+                PeerExchange.check_statuses(status)
+            ex[1].merge(30, step)
+    finally:
+        torch.cuda.synchronize(dev)
+        for a in areas:
+            PeerExchange.destroy(dev, a)
+
+
 def test_exchange_rejects_bad_arguments(cuda_module):
     from bitmask_speculation_b200 import _native
     from bitmask_speculation_b200.sharding import PeerExchange

@@ -1,10 +1,13 @@
 """bms_masked_reduce_batch_noalloc: the argmax + count kernel on the dynamic schedule with its
-workspace in a file-scope device array.  Two consecutive calls on different batches must equal
-bms_masked_reduce_batch (fixed schedule, no workspace) on the same inputs, bit for bit."""
+workspace in a file-scope device array, for callers that cannot allocate device memory.  Two
+consecutive calls on different batches must equal the oracle (the reference's torch_reduce
+restated) and bms_masked_reduce_batch (fixed schedule, no workspace) on the same inputs, bit for
+bit."""
 
 import numpy as np
 import pytest
 
+import oracle
 from bitmask_speculation_b200 import _native
 from bitmask_speculation_b200 import workloads as wl
 from helpers import as_dtype_bits, to_device
@@ -21,7 +24,8 @@ def _batch(rng, rows, vocab, dtype):
     dens = rng.choice([1.0, 0.3, 0.01, 1e-4], size=rows)
     valid = rng.random((rows, vocab)) < dens[:, None]
     valid[1, :] = False  # a row without a valid token
-    return to_device(as_dtype_bits(values, dtype), dtype), torch.from_numpy(wl.pack_bits_np(valid)).cuda()
+    bits, masks = as_dtype_bits(values, dtype), wl.pack_bits_np(valid)
+    return (to_device(bits, dtype), torch.from_numpy(masks).cuda()), (bits, masks)
 
 
 def _run(fn, logits, masks, dtype, extra):
@@ -40,13 +44,15 @@ def _run(fn, logits, masks, dtype, extra):
 def test_two_consecutive_calls_match_the_workspace_free_entry_point(cuda_module, dtype, rows, vocab):
     lib = _native.library()
     rng = np.random.default_rng(rows + vocab)
-    first = _batch(rng, rows, vocab, dtype)
-    second = _batch(rng, rows, vocab, dtype)
+    first, first_host = _batch(rng, rows, vocab, dtype)
+    second, second_host = _batch(rng, rows, vocab, dtype)
     got_first = _run(lib.bms_masked_reduce_batch_noalloc, *first, dtype, [])
     got_second = _run(lib.bms_masked_reduce_batch_noalloc, *second, dtype, [])
-    for got, batch in ((got_first, first), (got_second, second)):
+    for got, batch, (bits, masks) in ((got_first, first, first_host), (got_second, second, second_host)):
+        expect = oracle.reduce_rows(bits, masks, dtype=None if dtype == "float32" else dtype)
         want = _run(lib.bms_masked_reduce_batch, *batch, dtype, [None, 0])
-        for g, w in zip(got, want):
+        for g, e, w in zip(got, expect, want):
+            assert np.array_equal(g, e)
             assert np.array_equal(g, w)
 
 
