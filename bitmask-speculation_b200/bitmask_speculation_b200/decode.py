@@ -165,34 +165,21 @@ def _rotate(x, cos, sin):
 
 # ---------------------------------------------------------------- selection
 class _Selector:
-    """Masked argmax of one row under a grammar's current mask (the reference's _select_token:
-    select without advancing, then advance; NaN or an empty mask raise).  ``seconds`` accumulates
-    the host time spent selecting (a synchronizing call, so it covers the device work)."""
+    """Masked argmax of one row under a grammar's current mask (the reference's _select_token,
+    models/transformers.py:131-145: ``dispatch.select_token`` without advancing, then advance; NaN or
+    an empty mask raise).  With ``table`` the state masks are read on the device.  ``seconds``
+    accumulates the host time spent selecting (a synchronizing call, so it covers the device work)."""
 
     seconds = 0.0
 
     def __init__(self, vocab: int, device, table: DeviceMaskTable | None = None):
-        torch = _torch()
-        from .kernels._extension import load_extension
-        self.native = load_extension()
-        self.words = (vocab + 31) // 32
-        self.host = torch.zeros(self.words, dtype=torch.int32).pin_memory()
-        self.dev = torch.empty(self.words, dtype=torch.int32, device=device)
-        self._np = self.host.numpy()
         self.table = table
 
     def __call__(self, row, grammar) -> int:
         import time
-        from .kernels.cuda import masked_argmax
+        from .dispatch import select_token
         t0 = time.perf_counter()
-        if self.table is not None:  # the state's mask is already on the device: a view of the table
-            idx = grammar.state_index()
-            mask = self.table.table[idx if idx >= 0 else self.table.empty]
-        else:
-            self._np[:] = grammar.packed_mask_np()
-            self.dev.copy_(self.host, non_blocking=True)
-            mask = self.dev
-        token = int(masked_argmax(row, mask).item())
+        token = select_token(row, grammar, "cuda", table=self.table)
         self.seconds += time.perf_counter() - t0
         if not grammar.accept_token(token):
             raise ValueError("grammar rejected its selected token")

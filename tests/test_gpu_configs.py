@@ -107,8 +107,12 @@ def test_configuration_5_sampler_matches_oracle(configuration_5, cuda_module):
             assert sample_matches(widened, m[r], temperature, uniforms[r0 + r], int(tokens[r0 + r]), int(et[r])), \
                 (r0 + r, tokens[r0 + r], et[r])
             mismatched += 1
-    # Boundary cases are rare: a systematic error would show in many rows.
-    assert mismatched <= 3
+    # Every differing row passed the tolerance rule above.  How many differ depends on how many
+    # boundaries lie near u: with n positive-weight tokens in a row, u falls within d of some
+    # boundary with probability 2 d n, and rows here hold ~27,000 valid tokens on average, so a few
+    # rows in 65,536 (d ~ 1e-9 of fp32 partial sums) are expected; a systematic error would show in
+    # a large fraction of the rows.
+    assert mismatched <= 65536 // 1000, mismatched
 
 
 def test_configuration_1_exact(cuda_module):

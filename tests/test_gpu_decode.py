@@ -6,6 +6,9 @@ fp32 models keep the target's logits independent of the forward length to well b
 between the best and second-best valid logit, so greedy and speculative runs see the same choices.
 """
 
+import json
+from pathlib import Path
+
 import pytest
 
 from bitmask_speculation_b200 import workloads as wl
@@ -100,3 +103,34 @@ def test_speculative_c4_with_graphs_equals_eager(models):
         c = constrained_greedy(g_target, prompt, g0.fork(), max_new_tokens=48, eos=(0,))
         assert a == b, i
         assert b.token_ids == c.token_ids, i
+
+
+def _decode_golden():
+    return json.loads((Path(__file__).resolve().parent / "golden" / "decode_golden.json").read_text())["sets"]
+
+
+@pytest.mark.parametrize("name", ["small", "tiny_eos", "tiny_grammar_stop", "config4_fp32"])
+def test_decodes_match_the_reference_engine(cuda_module, name):
+    """Token streams, stop reasons and proposal accounting of the reference's own DecodingEngine
+    (``target_constrained`` = greedy_decode, ``c4`` = speculative_decode with DensityPolicy budgets;
+    decoding/greedy.py:46-92, decoding/speculative.py:98-210), recorded on CPU in fp32 by
+    tests/golden/make_decode_golden.py, reproduced by this library's constrained_greedy and
+    speculative_c4 on the same fp32 models and grammars on the GPU."""
+    from bitmask_speculation_b200.decode import build_decoder, constrained_greedy, speculative_c4
+    spec = next(s for s in _decode_golden() if s["name"] == name)
+    vocab, new, eos = spec["vocab"], spec["new_tokens"], tuple(spec["eos"])
+    target = build_decoder(vocab, dtype=torch.float32, **spec["target"])
+    draft = build_decoder(vocab, dtype=torch.float32, **spec["draft"])
+    for i, req in enumerate(spec["requests"]):
+        base = wl.SyntheticDFAGrammar(vocab, states=64, seed=req["grammar_seed"])
+        prompt = tuple(req["prompt"])
+        greedy = constrained_greedy(target, prompt, base.fork(), max_new_tokens=new, eos=eos)
+        want = req["target_constrained"]
+        assert (list(greedy.token_ids), greedy.stop_reason, greedy.eos_token_id) == (
+            want["token_ids"], want["stop_reason"], want["eos_token_id"]), (name, i, "greedy")
+        c4 = speculative_c4(target, draft, prompt, base.fork(), max_new_tokens=new, eos=eos)
+        want = req["c4"]
+        assert (list(c4.token_ids), c4.stop_reason, c4.eos_token_id) == (
+            want["token_ids"], want["stop_reason"], want["eos_token_id"]), (name, i, "c4")
+        assert (c4.rounds, c4.proposed, c4.accepted) == (want["rounds"], want["proposed"], want["accepted"]), \
+            (name, i, "accounting")
