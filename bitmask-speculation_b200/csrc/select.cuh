@@ -299,6 +299,7 @@ struct SelectParams {
     int32_t block;             // chunks per block of the split rows
     uint32_t epoch;            // this launch's tag, never 0
     int32_t dynamic_always;    // host only: take the dynamic schedule for any batch size
+    int32_t publish_only;      // split pieces only publish (a separate merge kernel merges the rows)
     // mask table (nullable): row r's mask is row mask_rows[r] of `masks` ([mask_table_rows, W]);
     // an index outside [0, mask_table_rows) fails the row with status 8
     const int32_t* mask_rows;
@@ -812,48 +813,23 @@ __device__ __forceinline__ double* ws_granules(const SelectParams& p, int64_t t)
 }
 
 // ----------------------------------------------------------------- the kernel
-// Finalizer (one warp) of a split unit: the piece's partial (argmax: key, first region holding
-// it, count, flags; sampler: max, count, flags, mass) and, for the sampler, its granules scaled
-// to the piece's max go to the workspace.  The CTA whose piece completes the row's chunk count
-// merges the row's pieces in chunk order -- the same merge as cluster ranks and vocabulary
-// shards -- and writes the row's outputs: the argmax index is recovered from the winning region
-// only, the sampler walks the owning piece.  Sampler: `granules` (shared memory) holds the
-// piece's granules, lanes w < 8 pass warp w's factor to the piece max; the buffer is then reused
-// for the row's granules; `uniform` is the row's uniform.
+// Merge of one split row (one warp): the row's pieces of this launch (epoch), read from the
+// workspace and merged in chunk order -- the same merge as cluster ranks and vocabulary shards --
+// then the row's outputs: the argmax index is recovered from the winning region only, the sampler
+// walks the owning piece.  `granules` is a shared-memory table [warp][kMaxChunksSampler] that the
+// row's granules are copied into (sampler); `piece_c0` / `piece_part` hold up to 32 pieces.  A
+// row without pieces of this launch (handed out whole) is left alone.  `reset` returns the row's
+// chunk counter to zero for the next launch (in-kernel merges only).
 template <typename T, bool kSample>
-__device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row_chunks, const GatherSlot& part, double wf,
-                                   double* granules, double uniform, Shared& sh, SamplerShared& ss, const uint8_t* lrow,
-                                   const int32_t* mrow, int lane) {
+__device__ void merge_split_row(const SelectParams& p, int64_t row, int64_t t, int row_chunks, double* granules,
+                                double uniform, uint32_t abort_flag, int32_t* piece_c0, GatherSlot* piece_part,
+                                float (*walk)[33], double* fac, const uint8_t* lrow, const int32_t* mrow, int lane,
+                                bool reset) {
     using E = Elem<T>;
     constexpr int kTPC = Layout<T>::kTokensPerChunk;
     constexpr int kTPW = Layout<T>::kTokensPerWarp;
     constexpr int kFinPer = kTPW / 32;
-    const int64_t t = d.row - p.whole_rows;
-    const int nch = d.c1 - d.c0;
-    WsPiece* pc = ws_piece(p, t, d.c0);
-    if (lane == 0) {
-        pc->epoch = p.epoch;
-        pc->c1 = d.c1;
-        pc->part = part;
-    }
-    if constexpr (kSample) {
-        if (lane < kConsumerWarps) ss.fac[lane] = wf;
-        __syncwarp();
-        double* g = ws_granules(p, t) + d.c0;
-        for (int i = lane; i < nch * kConsumerWarps; i += 32) {
-            const int w = i / nch, c = i - w * nch;
-            g[w * kWsChunks + c] = granules[w * kMaxChunksSampler + c] * ss.fac[w];
-        }
-    }
-    // Publish the piece and count its chunks in with one acquire-release add: the add that
-    // reaches the row's total identifies the merging CTA, which then sees every piece.
-    __syncwarp();
-    unsigned long long before = 0;
-    if (lane == 0) before = ptx::atom_add_acq_rel_gpu(ws_row_counter(p, t), static_cast<uint64_t>(nch));
-    before = __shfl_sync(0xFFFFFFFFu, before, 0);
-    if (before + static_cast<unsigned long long>(nch) != static_cast<unsigned long long>(row_chunks)) return;
-    __syncwarp();
-
+    __syncwarp();  // every lane is done with the scratch of the warp's previous row
     // One round trip: the sampler's row granules stream into shared memory (no registers) while
     // the piece records at chunks c = lane and lane + 32 load; records of this launch (epoch) are
     // compacted in chunk order (at most 32 pieces: rows of <= 64 chunks in blocks of >= 4 chunks,
@@ -888,20 +864,19 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
     const uint32_t below = (1u << lane) - 1u;
     const int na = __popc(ba);
     if (va) {
-        sh.piece_c0[__popc(ba & below)] = lane;
-        sh.piece_part[__popc(ba & below)] = ga;
+        piece_c0[__popc(ba & below)] = lane;
+        piece_part[__popc(ba & below)] = ga;
     }
     if (vb && na + __popc(bb & below) < 32) {
-        sh.piece_c0[na + __popc(bb & below)] = lane + 32;
-        sh.piece_part[na + __popc(bb & below)] = gb;
+        piece_c0[na + __popc(bb & below)] = lane + 32;
+        piece_part[na + __popc(bb & below)] = gb;
     }
     const int npieces = min(na + __popc(bb), 32);
     if constexpr (kSample) ptx::cp_async_wait_all();
+    if (npieces == 0) return;  // handed out whole: the selection launch wrote the row
     __syncwarp();
     const bool in = lane < npieces;
-    const GatherSlot e = in ? sh.piece_part[lane] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
-    const int64_t row = d.row;
-    const uint32_t abort_flag = sh.abort ? kFlagAbort : 0u;
+    const GatherSlot e = in ? piece_part[lane] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
     if constexpr (!kSample) {
         const uint32_t hi = __reduce_max_sync(0xFFFFFFFFu, e.a);
         const uint32_t region = __reduce_min_sync(0xFFFFFFFFu, (in && hi != 0u && e.a == hi) ? e.b : 0xFFFFFFFFu);
@@ -933,15 +908,15 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
         int64_t chosen = -1;
         if (mg.code == kOk) {
             const int q = mg.owner;
-            const int oc0 = sh.piece_c0[q];
-            const int oc1 = q + 1 < npieces ? sh.piece_c0[q + 1] : row_chunks;
+            const int oc0 = piece_c0[q];
+            const int oc1 = q + 1 < npieces ? piece_c0[q + 1] : row_chunks;
             // The owner's granules are already relative to its max: every warp factor is the
             // owner's rank factor.
             const int64_t b0 = static_cast<int64_t>(oc0) * kTPC;
             const int64_t b1 = static_cast<int64_t>(oc1) * kTPC < p.vocab ? static_cast<int64_t>(oc1) * kTPC : p.vocab;
             chosen = sampler_owner_walk<T>(granules + oc0, 1, kMaxChunksSampler, (oc1 - oc0) * kConsumerWarps, 1.0, 1.0,
                                            lane < kConsumerWarps, mg, p.temperature, p.inv_temperature, p.scale2, b0, b1,
-                                           lrow, mrow, ss.walk, ss.fac, lane);
+                                           lrow, mrow, walk, fac, lane);
         }
         if (lane == 0) {
             p.status[row] = mg.code != kOk ? mg.code : chosen >= 0 ? kOk : kNoMass;
@@ -950,7 +925,49 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
         }
     }
     // The next launch (or graph replay) counts this row from zero.
-    if (lane == 0) atomicExch(ws_row_counter(p, t), 0ull);
+    if (reset && lane == 0) atomicExch(ws_row_counter(p, t), 0ull);
+}
+
+// Finalizer (one warp) of a split unit: the piece's partial (argmax: key, first region holding
+// it, count, flags; sampler: max, count, flags, mass) and, for the sampler, its granules scaled
+// to the piece's max go to the workspace.  In the one-launch form the CTA whose piece completes
+// the row's chunk count merges the row (merge_split_row); with `publish_only` the merge kernel
+// does it after the launch.  Sampler: `granules` (shared memory) holds the piece's granules, lanes
+// w < 8 pass warp w's factor to the piece max; the buffer is then reused for the row's granules;
+// `uniform` is the row's uniform.
+template <typename T, bool kSample>
+__device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row_chunks, const GatherSlot& part, double wf,
+                                   double* granules, double uniform, Shared& sh, SamplerShared& ss, const uint8_t* lrow,
+                                   const int32_t* mrow, int lane) {
+    const int64_t t = d.row - p.whole_rows;
+    const int nch = d.c1 - d.c0;
+    WsPiece* pc = ws_piece(p, t, d.c0);
+    if (lane == 0) {
+        pc->epoch = p.epoch;
+        pc->c1 = d.c1;
+        pc->part = part;
+    }
+    if constexpr (kSample) {
+        if (lane < kConsumerWarps) ss.fac[lane] = wf;
+        __syncwarp();
+        double* g = ws_granules(p, t) + d.c0;
+        for (int i = lane; i < nch * kConsumerWarps; i += 32) {
+            const int w = i / nch, c = i - w * nch;
+            g[w * kWsChunks + c] = granules[w * kMaxChunksSampler + c] * ss.fac[w];
+        }
+    }
+    // Publish the piece and count its chunks in with one acquire-release add: the add that
+    // reaches the row's total identifies the merging CTA, which then sees every piece.
+    __syncwarp();
+    if (p.publish_only) return;
+    unsigned long long before = 0;
+    if (lane == 0) before = ptx::atom_add_acq_rel_gpu(ws_row_counter(p, t), static_cast<uint64_t>(nch));
+    before = __shfl_sync(0xFFFFFFFFu, before, 0);
+    if (before + static_cast<unsigned long long>(nch) != static_cast<unsigned long long>(row_chunks)) return;
+    __syncwarp();
+
+    merge_split_row<T, kSample>(p, d.row, t, row_chunks, granules, uniform, sh.abort ? kFlagAbort : 0u, sh.piece_c0,
+                                sh.piece_part, ss.walk, ss.fac, lrow, mrow, lane, true);
 }
 
 // Programmatic dependent launch: a dependent grid (the next selection launch, the verification
@@ -1090,9 +1107,11 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 // remaining (split) rows' chunks in row-major order.
                 const int64_t split_chunks = (p.rows - p.whole_rows) * nchunks;
                 unsigned long long* tickets = &ws_header(p)->tickets;
-                while (!stop) {
-                    // One atomic per ticket (the counter starts every launch at 0).
-                    const int64_t tk = static_cast<int64_t>(atomicAdd(tickets, 1ull));
+                for (bool first = true; !stop; first = false) {
+                    // CTA b's first ticket is b; later ones come from the counter (one atomic per
+                    // ticket, the counter starting every launch at 0).
+                    const int64_t tk = first ? static_cast<int64_t>(blockIdx.x)
+                                             : static_cast<int64_t>(gridDim.x) + static_cast<int64_t>(atomicAdd(tickets, 1ull));
                     if (tk >= p.tickets) break;
                     if (tk < p.whole_rows) {
                         run(tk, 0, nchunks, kUnitWhole);
@@ -1597,6 +1616,46 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             atomicExch(&hd->tickets, 0ull);
             atomicExch(&hd->done, 0ull);
         }
+    }
+}
+
+// Scratch of one merging warp of merge_pieces_kernel.
+struct MergeScratch {
+    double granules[kMaxChunksSampler * kConsumerWarps];  // the row's granules [warp][chunk] (sampler)
+    float walk[32][33];
+    double fac[kConsumerWarps];
+    int32_t piece_c0[32];
+    GatherSlot piece_part[32];
+};
+constexpr int kMergeWarps = 4;
+
+// Second launch of the two-launch schedule of small batches: the selection launch streamed every
+// row as pieces (publish_only) and left their partials and granules in the workspace; one warp per
+// row merges them (merge_split_row) and writes the outputs.  Launched as a programmatic dependent
+// of the selection launch; lets its own dependents start at once (they wait for its completion).
+template <typename T, bool kSample>
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_pieces_kernel(const SelectParams p) {
+    __shared__ MergeScratch ms[kMergeWarps];
+    launch_dependents();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    using E = Elem<T>;
+    constexpr int kTPC = Layout<T>::kTokensPerChunk;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int row_chunks = static_cast<int>((p.vocab + kTPC - 1) / kTPC);
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kMergeWarps;
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; row < p.rows; row += nwarps) {
+        const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                              static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+        int64_t mr = row;
+        if (p.mask_rows != nullptr) {  // a bad index failed the row in the selection launch
+            mr = p.mask_rows[row];
+            if (mr < 0 || mr >= p.mask_table_rows) mr = 0;
+        }
+        const int32_t* mrow = p.masks + static_cast<size_t>(mr) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
+        const double u = (kSample && p.uniforms != nullptr) ? p.uniforms[row] : 0.0;
+        MergeScratch& m = ms[wib];
+        merge_split_row<T, kSample>(p, row, row - p.whole_rows, row_chunks, m.granules, u, 0u, m.piece_c0, m.piece_part,
+                                    m.walk, m.fac, lrow, mrow, lane, false);
     }
 }
 
