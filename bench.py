@@ -468,13 +468,17 @@ class EndToEnd:
             self.h2d_masks = w.rows * w.words * 4 + s * k * 8 + s * 4
             self.d2h = w.rows * (8 + 8 + 4 + 4) + s * (4 + 8 + 4 + 4)
         elif w.kind == "verify":
-            self.h_masks = w.masks.cpu().pin_memory()
+            from bitmask_speculation_b200.compressed_masks import CompressedMasks
+            # The round's masks in their compact transfer form: rows with few valid tokens (the
+            # enumeration rows) as token-ID lists, the others as bitmaps, expanded on the device
+            # into a mask table that the verification reads through per-row indices.
+            self.cm = CompressedMasks.from_bitmaps(w.masks.cpu().numpy(), w.vocab)
+            self.tables = [self.cm.allocate(w.device) for _ in range(2)]
             self.h_prop = w.proposals.cpu().pin_memory()
             self.h_len = w.lengths.cpu().pin_memory()
             # Two device input sets and a copy stream: step i's inputs upload while step i-1's
             # kernels run (an engine prefetching the next round's masks); every step still copies
             # its own inputs and reads its own results.
-            self.d_masks = [torch.empty_like(w.masks) for _ in range(2)]
             self.d_prop = [torch.empty_like(w.proposals) for _ in range(2)]
             self.d_len = [torch.empty_like(w.lengths) for _ in range(2)]
             self.copy_stream = torch.cuda.Stream(w.device)
@@ -491,7 +495,8 @@ class EndToEnd:
                 "seq_status": torch.empty(s, dtype=torch.int32).pin_memory(),
                 "row_budget": torch.empty(w.rows, dtype=torch.int32).pin_memory(),
             }
-            self.h2d = self.h_masks.numel() * 4 + self.h_prop.numel() * 8 + self.h_len.numel() * 4
+            self.h2d = self.cm.h2d_bytes + self.h_prop.numel() * 8 + self.h_len.numel() * 4
+            self.h2d_bitmaps = w.masks.numel() * 4 + self.h_prop.numel() * 8 + self.h_len.numel() * 4
             self.d2h = sum(t.numel() * t.element_size() for t in self.h_out.values())
         else:
             logits, masks = w._batch()
@@ -519,12 +524,11 @@ class EndToEnd:
             compute = torch.cuda.current_stream(w.device)
             with torch.cuda.stream(self.copy_stream):
                 self.copy_stream.wait_event(self.consumed[b])  # the kernels that read buffer b are done
-                self.d_masks[b].copy_(self.h_masks, non_blocking=True)
                 self.d_prop[b].copy_(self.h_prop, non_blocking=True)
                 self.d_len[b].copy_(self.h_len, non_blocking=True)
-                self.ready[b].record(self.copy_stream)
-            compute.wait_event(self.ready[b])
-            out = verify_batch(w.logits, self.d_masks[b], self.d_prop[b], self.d_len[b])
+            # Mask bitmaps and ID lists on the copy stream; the list expansion on the compute stream.
+            table, mask_rows = self.cm.upload(w.device, self.tables[b], copy_stream=self.copy_stream)
+            out = verify_batch(w.logits, table, self.d_prop[b], self.d_len[b], mask_rows=mask_rows)
             self.consumed[b].record(compute)
             for k, h in self.h_out.items():
                 h.copy_(getattr(out, k), non_blocking=True)
@@ -794,28 +798,35 @@ def run_b200_arm(args):
             torch.cuda.synchronize(device)
             if dist is not None:
                 dist.barrier()
+            # At least 50 end-to-end steps (about a millisecond each): host-link timings vary more
+            # than kernel timings.
+            esteps = max(args.steps, 50)
             t0 = time.perf_counter()
-            etime = timed_loop(e.step, args.steps, device, dist)
+            etime = timed_loop(e.step, esteps, device, dist)
             wall = time.perf_counter() - t0
             if w.kind == "grammar":  # the same round uploading every row's mask words instead
                 e.use_table = False
                 e.step()
-                mtime = timed_loop(e.step, args.steps, device, dist)
+                mtime = timed_loop(e.step, esteps, device, dist)
                 e.use_table = True
-                uploaded = {"value": w.rows * world * args.steps / mtime, "unit": "rows/s",
+                uploaded = {"value": w.rows * world * esteps / mtime, "unit": "rows/s",
                             "h2d_bytes_per_step": e.h2d_masks, "d2h_bytes_per_step": e.d2h,
                             "path": "verify_with_grammars with fork masks filled on the host and uploaded"}
-            e2e = {"value": w.rows * world * args.steps / etime, "unit": "rows/s",
+            e2e = {"value": w.rows * world * esteps / etime, "unit": "rows/s", "steps": esteps,
                    "h2d_bytes_per_step": e.h2d, "d2h_bytes_per_step": e.d2h,
-                   "wall_value": w.rows * world * args.steps / wall,
+                   "h2d_bytes_as_bitmaps": getattr(e, "h2d_bitmaps", None),
+                   "wall_value": w.rows * world * esteps / wall,
                    "path": {
                        "grammar": ("grammar_verification.verify_with_grammars (public API) with a device-resident "
                                    "mask table: fork state indices computed on the host, one H2D of 4 bytes per "
                                    "row, one launch pair, one sync, events replayed on the sequences' grammars "
                                    "every step"),
-                       "verify": ("verification.verify_batch (public API): pinned host masks/drafts/lengths H2D, "
-                                  "device-resident logits, results D2H every step; each step's upload on a copy "
-                                  "stream overlaps the previous step's kernels (two input buffers)"),
+                       "verify": ("compressed_masks.CompressedMasks.upload + verification.verify_batch (public API): "
+                                  "every step the round's masks go host->device in compact form (rows with at most "
+                                  "970 valid tokens as token-ID lists, expanded on the device by "
+                                  "bms_expand_token_lists; the others as bitmaps) with the drafts and lengths, "
+                                  "device-resident logits, results D2H; each step's upload on a copy stream "
+                                  "overlaps the previous step's kernels (two input buffers)"),
                        "sample": ("kernels.cuda.batched_masked_sample (public API): pinned host masks H2D, "
                                   "device-resident logits, uniforms drawn on the device, tokens and status D2H "
                                   "every step"),

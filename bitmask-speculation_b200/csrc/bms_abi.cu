@@ -435,6 +435,33 @@ __global__ void __launch_bounds__(256) count_rows_kernel(const int32_t* __restri
     }
 }
 
+// Token-ID lists to packed mask rows, one CTA per list (grid-stride): the row is cleared, then the
+// listed tokens' bits are set (atomicOr: a list may repeat IDs or be unsorted).  List l is
+// ids[offsets[l], offsets[l + 1]), clamped to [0, n_ids) so that no offsets can reach outside
+// `ids`; IDs outside [0, vocab) set nothing and flag the list in `bad` (nullable).
+__global__ void __launch_bounds__(256) expand_lists_kernel(const int32_t* __restrict__ ids, int64_t n_ids,
+                                                           const int32_t* __restrict__ offsets, int64_t lists,
+                                                           int64_t vocab, int32_t* __restrict__ out,
+                                                           int32_t* __restrict__ bad) {
+    const int64_t words = (vocab + 31) / 32;
+    for (int64_t l = blockIdx.x; l < lists; l += gridDim.x) {
+        uint32_t* row = reinterpret_cast<uint32_t*>(out) + l * words;
+        for (int64_t w = threadIdx.x; w < words; w += blockDim.x) row[w] = 0u;
+        __syncthreads();  // the cleared words before any bit of this CTA is set
+        int64_t b = offsets[l], e = offsets[l + 1];
+        b = b < 0 ? 0 : b > n_ids ? n_ids : b;
+        e = e < b ? b : e > n_ids ? n_ids : e;
+        int flag = 0;
+        for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+            const int64_t t = ids[i];
+            if (t >= 0 && t < vocab) atomicOr(row + (t >> 5), 1u << (t & 31));
+            else flag = 1;
+        }
+        flag = __syncthreads_or(flag);
+        if (bad != nullptr && threadIdx.x == 0) bad[l] = flag;
+    }
+}
+
 // Longest-prefix acceptance, one warp per sequence: lane i looks at row i of a 32-row window,
 // a ballot finds the first row where the reference stops (a failed status, a draft mismatch,
 // or the bonus row), and per-row budgets follow.  Launched as a programmatic dependent of
@@ -866,6 +893,25 @@ int bms_mask_budget(const int32_t* masks, int64_t rows, int64_t vocab, const bms
     const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
     count_rows_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(masks, rows, vocab, P, counts, density, budget);
     BMS_CUDA(cudaGetLastError(), "popcount launch");
+    return BMS_SUCCESS;
+}
+
+int bms_expand_token_lists(const int32_t* ids, int64_t n_ids, const int32_t* offsets, int64_t lists, int64_t vocab,
+                           int32_t* out, int32_t* bad, int32_t device, void* stream) {
+    BMS_CHECK(check_vocab(vocab));
+    if (lists < 0 || n_ids < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "lists and n_ids must be nonnegative");
+    BMS_CHECK(check_device(device));
+    if (lists == 0) return BMS_SUCCESS;
+    if (n_ids > 0) BMS_CHECK(check_ptr(ids, device, "ids", 4));
+    BMS_CHECK(check_ptr(offsets, device, "offsets", 4));
+    BMS_CHECK(check_ptr(out, device, "out", 4));
+    if (bad) BMS_CHECK(check_ptr(bad, device, "bad", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
+    const unsigned grid = static_cast<unsigned>(lists < cap ? lists : cap);
+    expand_lists_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(ids, n_ids, offsets, lists, vocab, out, bad);
+    BMS_CUDA(cudaGetLastError(), "token-list expansion launch");
     return BMS_SUCCESS;
 }
 

@@ -139,6 +139,17 @@ BMS_API int bms_masked_sample_batch(const void *logits, int32_t dtype, const int
 BMS_API int bms_mask_budget(const int32_t *masks, int64_t rows, int64_t vocab, const bms_policy *policy,
                     int64_t *counts, double *density, int32_t *budget, int32_t device, void *stream);
 
+/* Compact upload form of mask rows (no reference counterpart; the reference copied every 31 KB
+ * bitmap row to the device, kernels/dispatch.py:95).  Writes `lists` packed mask rows to `out`
+ * (row l at out + l * ceil(vocab / 32), bits of the listed tokens set, every other bit clear) from
+ * token-ID lists: list l is ids[offsets[l], offsets[l + 1]) (int32 device arrays; `offsets` has
+ * lists + 1 entries; entries are clamped to [0, n_ids], so no offsets reach outside `ids`).  IDs may
+ * repeat or come unsorted; an ID outside [0, vocab) sets nothing and sets bad[l] to 1 (else 0;
+ * `bad` may be NULL).  Sparse rows sent this way plus dense rows sent as bitmaps form a mask table
+ * for bms_verify_batch's `mask_rows`. */
+BMS_API int bms_expand_token_lists(const int32_t *ids, int64_t n_ids, const int32_t *offsets, int64_t lists,
+                                   int64_t vocab, int32_t *out, int32_t *bad, int32_t device, void *stream);
+
 /* One batched verification round (decoding/verification.py:18-48 verify_prefix
  * over the rows models/transformers.py:181-201 selects from).  Sequence s owns
  * rows [s*rows_per_seq, (s+1)*rows_per_seq); row s*rows_per_seq + i is the
