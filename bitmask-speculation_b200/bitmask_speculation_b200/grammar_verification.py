@@ -42,6 +42,16 @@ def _mask_row(grammar, vocab: int) -> np.ndarray:
     return row.view(np.int32)
 
 
+def _write_mask_row(grammar, vocab: int, out: np.ndarray, row: int) -> None:
+    """The grammar's mask into ``out[row]``: written in place by grammars that can
+    (``fill_mask_row``, e.g. ``xgrammar_state.XGrammarState``), else copied from ``_mask_row``."""
+    fill = getattr(grammar, "fill_mask_row", None)
+    if fill is not None:
+        fill(out, row)
+    else:
+        out[row] = _mask_row(grammar, vocab)
+
+
 def fork_masks(grammar, draft: Sequence[int], vocab: int, out: np.ndarray) -> int:
     """Write into ``out[: len(draft) + 1]`` the packed masks of the committed state and of the
     state after each draft prefix (rows a fork cannot reach -- after a proposal it rejects, or
@@ -50,11 +60,14 @@ def fork_masks(grammar, draft: Sequence[int], vocab: int, out: np.ndarray) -> in
     if rows > out.shape[0]:
         raise ValueError("draft longer than the buffer")
     fork = grammar.fork()
-    out[0] = _mask_row(fork, vocab)
+    _write_mask_row(fork, vocab, out, 0)
     live = not fork.is_terminated()
     for i, proposal in enumerate(draft):
         live = live and fork.accept_token(proposal) and not fork.is_terminated()
-        out[i + 1] = _mask_row(fork, vocab) if live else 0
+        if live:
+            _write_mask_row(fork, vocab, out, i + 1)
+        else:
+            out[i + 1] = 0
     return rows
 
 
