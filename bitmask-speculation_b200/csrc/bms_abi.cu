@@ -462,6 +462,181 @@ __global__ void __launch_bounds__(256) expand_lists_kernel(const int32_t* __rest
     }
 }
 
+// ---------------------------------------------------------------- stochastic speculative acceptance
+// Row normaliser of a sampler partial (one rank covering the whole row): the partial's reference
+// max M and the row's mass S relative to it, or a status code for rows that cannot be sampled
+// (the sampler's codes and priority, merge_sampler_ranks).
+struct RowNorm {
+    float M;
+    double S;
+    int32_t code;
+};
+
+__device__ __forceinline__ RowNorm row_norm(const GatherSlot& g) {
+    const float kInf = __int_as_float(0x7F800000);
+    RowNorm r{__uint_as_float(g.a), g.s, kOk};
+    r.code = (g.c & kFlagAbort) ? kTimeout : (g.c & kFlagNaN) ? kNaN : (r.M == kInf) ? kPosInf : (g.b == 0u) ? kEmpty
+             : (r.M == -kInf || !(r.S > 0.0)) ? kNoMass : kOk;
+    return r;
+}
+
+// Weight of logit x relative to a row normaliser: 2^((x - M) log2(e) / T) / S (fp32 exponential,
+// fp64 quotient).  x == M gives exactly 1 / S whatever the scale.
+__device__ __forceinline__ double spec_weight(float x, const RowNorm& n, float sc) {
+    const float d = x - n.M;
+    const float t = d == 0.0f ? 0.0f : fminf(d * sc, 126.0f);
+    return static_cast<double>(ptx::ex2(t)) / n.S;
+}
+
+// Speculative sampling for S sequences, one CTA each.  Sequence s has lengths[s] = L drafts
+// proposals[s, i] drawn from the draft's masked softmax q_i (draft row s * (R - 1) + i), and target
+// rows s * R + i giving p_i (R = rows per sequence, both under mask row s * R + i).  Draft i is
+// accepted iff u_i q_i(d_i) < p_i(d_i) (probability min(1, p / q)); at the first rejection j the
+// replacement is drawn by inverse CDF with v_s from max(0, p_j - q_j) normalised, and after L
+// acceptances the bonus from p_L -- so every emitted token is distributed as the target's masked
+// softmax.  A replacement distribution that rounds to zero mass falls back to p_j.  Outputs: the
+// accepted length, the drawn token, its kind (0 replacement, 1 bonus, 2 fallback for L = 0) and a
+// status, nonzero when a row the procedure consumed cannot be sampled.
+template <typename T>
+__global__ void __launch_bounds__(256) speculative_accept_kernel(
+    const T* __restrict__ target, const T* __restrict__ draft, const int32_t* __restrict__ masks, int64_t seqs,
+    int64_t rows_per_seq, int64_t vocab, const int64_t* __restrict__ proposals, const int32_t* __restrict__ lengths,
+    const GatherSlot* __restrict__ tpart, const GatherSlot* __restrict__ qpart, const double* __restrict__ u_accept,
+    const double* __restrict__ u_resample, float sc, int32_t* __restrict__ accept_len, int64_t* __restrict__ token,
+    int32_t* __restrict__ kind, int32_t* __restrict__ status) {
+    using E = Elem<T>;
+    __shared__ double sums[256];
+    __shared__ int32_t s_j, s_code, s_residual, s_last;
+    __shared__ int64_t s_token;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int64_t K = rows_per_seq - 1, words = (vocab + 31) / 32;
+    for (int64_t seq = blockIdx.x; seq < seqs; seq += gridDim.x) {
+        const int32_t L = lengths[seq];
+        if (tid < 32) {
+            // Acceptance, 32 drafts per pass: the first rejected position (or L) and its status.
+            int32_t j = -1, code = kOk;
+            if (L < 0 || L > K) {
+                j = 0;
+                code = kBadLength;
+            }
+            for (int64_t i0 = 0; j < 0 && i0 < L; i0 += 32) {
+                const int64_t i = i0 + lane;
+                bool stop = false;
+                int32_t c = kOk;
+                if (i < L) {
+                    const int64_t trow = seq * rows_per_seq + i, qrow = seq * K + i;
+                    const RowNorm tn = row_norm(tpart[trow]), qn = row_norm(qpart[qrow]);
+                    c = tn.code != kOk ? tn.code : qn.code;
+                    const int64_t d = proposals[seq * K + i];
+                    bool ok = false;
+                    if (c == kOk && d >= 0 && d < vocab &&
+                        ((static_cast<uint32_t>(masks[trow * words + (d >> 5)]) >> (d & 31)) & 1u)) {
+                        const double p = spec_weight(E::load(target, trow * vocab + d), tn, sc);
+                        const double q = spec_weight(E::load(draft, qrow * vocab + d), qn, sc);
+                        ok = q > 0.0 && u_accept[seq * K + i] * q < p;
+                    }
+                    stop = c != kOk || !ok;
+                }
+                const uint32_t ballot = __ballot_sync(0xFFFFFFFFu, stop);
+                if (ballot) {
+                    const int f = __ffs(ballot) - 1;
+                    j = static_cast<int32_t>(i0 + f);
+                    code = __shfl_sync(0xFFFFFFFFu, c, f);
+                }
+            }
+            if (j < 0) j = L;
+            if (lane == 0) {
+                s_j = j;
+                s_code = code;
+                s_residual = (code == kOk && j < L) ? 1 : 0;
+            }
+        }
+        __syncthreads();
+        const int32_t j = s_j;
+        int32_t code = s_code;
+        const int64_t trow = seq * rows_per_seq + j;
+        RowNorm tn{0.0f, 1.0, kOk}, qn{0.0f, 1.0, kOk};
+        if (code == kOk) {
+            tn = row_norm(tpart[trow]);
+            code = tn.code;
+            if (s_residual) qn = row_norm(qpart[seq * K + j]);  // usable: its acceptance test ran
+        }
+        int64_t chosen = -1;
+        if (code == kOk) {
+            // Inverse CDF over the row's valid tokens, each thread owning one contiguous segment.
+            const int64_t per = (vocab + 255) / 256, t0 = tid * per, t1 = t0 + per < vocab ? t0 + per : vocab;
+            const T* trow_p = target + trow * vocab;
+            const T* qrow_p = draft + (seq * K + j) * vocab;
+            const int32_t* mrow = masks + trow * words;
+            for (int pass = 0; pass < 2 && chosen < 0; ++pass) {
+                const bool residual = s_residual && pass == 0;
+                auto weight = [&](int64_t t) -> double {
+                    if (!((static_cast<uint32_t>(mrow[t >> 5]) >> (t & 31)) & 1u)) return 0.0;
+                    const double w = spec_weight(E::load(trow_p, t), tn, sc);
+                    return residual ? fmax(0.0, w - spec_weight(E::load(qrow_p, t), qn, sc)) : w;
+                };
+                double local = 0.0;
+                for (int64_t t = t0; t < t1; ++t) local += weight(t);
+                // Inclusive scan of the 256 segment sums: warp scans, then the 8 warp totals.
+                double v = local;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const double n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                    if (lane >= o) v += n;
+                }
+                if (lane == 31) sums[tid >> 5] = v;
+                if (tid == 0) {
+                    s_token = -1;
+                    s_last = -1;
+                }
+                __syncthreads();
+                double before = 0.0, total = 0.0;
+                for (int w = 0; w < 8; ++w) {
+                    if (w < (tid >> 5)) before += sums[w];
+                    total += sums[w];
+                }
+                const double incl = before + v, start = incl - local;
+                const double cut = u_resample[seq] * total;
+                if (total > 0.0 && local > 0.0) {
+                    atomicMax(&s_last, tid);
+                    if (cut >= start && cut < incl) {  // this segment holds the crossing: walk it
+                        double acc = start;
+                        int64_t pick = -1;
+                        for (int64_t t = t0; t < t1; ++t) {
+                            const double w = weight(t);
+                            if (w > 0.0) {
+                                pick = t;
+                                if (cut < acc + w) break;
+                                acc += w;
+                            }
+                        }
+                        s_token = pick;
+                    }
+                }
+                __syncthreads();
+                if (s_token < 0 && s_last == tid) {
+                    // Rounding put the cut past the last positive weight: its token is taken.
+                    int64_t pick = -1;
+                    for (int64_t t = t0; t < t1; ++t)
+                        if (weight(t) > 0.0) pick = t;
+                    s_token = pick;
+                }
+                __syncthreads();
+                chosen = s_token;
+                __syncthreads();
+            }
+            if (chosen < 0) code = kNoMass;
+        }
+        if (tid == 0) {
+            accept_len[seq] = j;
+            status[seq] = code;
+            token[seq] = code == kOk ? chosen : -1;
+            kind[seq] = j < L ? 0 : (L > 0 ? 1 : 2);
+        }
+        __syncthreads();
+    }
+}
+
 // Longest-prefix acceptance, one warp per sequence: lane i looks at row i of a 32-row window,
 // a ballot finds the first row where the reference stops (a failed status, a draft mismatch,
 // or the bonus row), and per-row budgets follow.  Launched as a programmatic dependent of
@@ -893,6 +1068,55 @@ int bms_mask_budget(const int32_t* masks, int64_t rows, int64_t vocab, const bms
     const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
     count_rows_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(masks, rows, vocab, P, counts, density, budget);
     BMS_CUDA(cudaGetLastError(), "popcount launch");
+    return BMS_SUCCESS;
+}
+
+int bms_speculative_accept(const void* target_logits, const void* draft_logits, int32_t dtype, const int32_t* masks,
+                           int64_t seqs, int64_t rows_per_seq, int64_t vocab, const int64_t* proposals,
+                           const int32_t* lengths, const bms_partial* target_partials, const bms_partial* draft_partials,
+                           double temperature, const double* accept_uniforms, const double* resample_uniforms,
+                           int32_t* accept_len, int64_t* token, int32_t* kind, int32_t* status, int32_t device,
+                           void* stream) {
+    if (!std::isfinite(temperature) || !(temperature > 0))
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "temperature must be finite and positive");
+    if (seqs < 0 || rows_per_seq < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "invalid sequence shape");
+    BMS_CHECK(check_dtype(dtype));
+    BMS_CHECK(check_vocab(vocab));
+    BMS_CHECK(check_device(device));
+    if (seqs == 0) return BMS_SUCCESS;
+    const size_t eb = static_cast<size_t>(elem_bytes(dtype));
+    BMS_CHECK(check_ptr(target_logits, device, "target_logits", eb));
+    BMS_CHECK(check_ptr(masks, device, "masks", 4));
+    BMS_CHECK(check_ptr(lengths, device, "lengths", 4));
+    BMS_CHECK(check_ptr(target_partials, device, "target_partials", 16));
+    BMS_CHECK(check_ptr(resample_uniforms, device, "resample_uniforms", 8));
+    if (rows_per_seq > 1) {
+        BMS_CHECK(check_ptr(draft_logits, device, "draft_logits", eb));
+        BMS_CHECK(check_ptr(proposals, device, "proposals", 8));
+        BMS_CHECK(check_ptr(draft_partials, device, "draft_partials", 16));
+        BMS_CHECK(check_ptr(accept_uniforms, device, "accept_uniforms", 8));
+    }
+    BMS_CHECK(check_ptr(accept_len, device, "accept_len", 4));
+    BMS_CHECK(check_ptr(token, device, "token", 8));
+    BMS_CHECK(check_ptr(kind, device, "kind", 4));
+    BMS_CHECK(check_ptr(status, device, "status", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    const float sc = static_cast<float>(1.4426950408889634 / temperature);
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
+    const unsigned grid = static_cast<unsigned>(seqs < cap ? seqs : cap);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto tp = reinterpret_cast<const GatherSlot*>(target_partials);
+    auto qp = reinterpret_cast<const GatherSlot*>(draft_partials);
+#define BMS_SPEC(T)                                                                                                  \
+    speculative_accept_kernel<T><<<grid, 256, 0, st>>>(                                                              \
+        static_cast<const T*>(target_logits), static_cast<const T*>(draft_logits), masks, seqs, rows_per_seq, vocab, \
+        proposals, lengths, tp, qp, accept_uniforms, resample_uniforms, sc, accept_len, token, kind, status)
+    if (dtype == BMS_FLOAT32) BMS_SPEC(float);
+    else if (dtype == BMS_BFLOAT16) BMS_SPEC(__nv_bfloat16);
+    else BMS_SPEC(__half);
+#undef BMS_SPEC
+    BMS_CUDA(cudaGetLastError(), "speculative acceptance launch");
     return BMS_SUCCESS;
 }
 

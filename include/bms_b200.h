@@ -210,6 +210,27 @@ BMS_API int bms_shard_merge(const bms_partial *partials, int32_t shards, int32_t
                             const void *granules, int64_t granule_stride, int64_t *tokens, int64_t *counts,
                             int32_t *status, int32_t device, void *stream);
 
+/* Stochastic speculative acceptance (speculative sampling; no counterpart in the reference, whose
+ * correctness contract is greedy, docs/design.md:5-11).  Sequence s has lengths[s] = L <= K drafts
+ * proposals[s, i] ([seqs, K] int64, K = rows_per_seq - 1) that were drawn from the draft model's
+ * masked softmax q_i at `temperature` (draft logits row s * K + i); target logits row
+ * s * rows_per_seq + i gives p_i; both use mask row s * rows_per_seq + i.  The partials are
+ * bms_shard_partials outputs (whole rows, token_offset 0, the same temperature) of the target rows
+ * and of the draft rows.  Draft i is accepted iff accept_uniforms[s, i] * q_i(d_i) < p_i(d_i); at the
+ * first rejection j the token is drawn by inverse CDF with resample_uniforms[s] from
+ * max(0, p_j - q_j) normalised (from p_j if that rounds to zero mass), after L acceptances from p_L:
+ * every emitted token is distributed as the target's masked softmax.  Outputs per sequence: accepted
+ * length, token (-1 on error), kind (0 replacement, 1 bonus, 2 fallback for L = 0) and status
+ * (BMS_STATUS_* of the first consumed row that cannot be sampled; 6 for L outside [0, K]).  Uniforms
+ * are float64 in [0, 1).  temperature must be positive (temperature 0 is bms_verify_batch). */
+BMS_API int bms_speculative_accept(const void *target_logits, const void *draft_logits, int32_t dtype,
+                                   const int32_t *masks, int64_t seqs, int64_t rows_per_seq, int64_t vocab,
+                                   const int64_t *proposals, const int32_t *lengths,
+                                   const bms_partial *target_partials, const bms_partial *draft_partials,
+                                   double temperature, const double *accept_uniforms, const double *resample_uniforms,
+                                   int32_t *accept_len, int64_t *token, int32_t *kind, int32_t *status,
+                                   int32_t device, void *stream);
+
 /* ---- Peer-memory exchange of argmax shard partials (no reference counterpart: it replaces the
  * NCCL all-gather between bms_shard_partials and bms_shard_merge with stores over NVLink).
  * Each rank of a group of `ranks` (<= 8, one GPU each) creates one exchange area in its device

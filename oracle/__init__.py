@@ -217,6 +217,57 @@ def sample_matches(row_f32, mask_row, temperature, uniform, gpu_token, ref_token
     return dist <= tol
 
 
+def masked_softmax(row_f32, mask_row, temperature: float) -> np.ndarray:
+    """fp64 probabilities exp((x - max) / T) / sum over the valid finite logits of one row (zero
+    elsewhere)."""
+    vocab = row_f32.size
+    words = np.ascontiguousarray(mask_row, dtype=np.int32).view(np.uint32)
+    t = np.arange(vocab)
+    valid = ((words[t >> 5] >> (t & 31).astype(np.uint32)) & 1).astype(bool) & np.isfinite(row_f32)
+    x = row_f32.astype(np.float64)
+    w = np.zeros(vocab)
+    w[valid] = np.exp((x[valid] - x[valid].max()) / temperature)
+    return w / w.sum()
+
+
+def speculative_accept(target_f32, draft_f32, masks, proposals, lengths, temperature, u_accept, u_resample):
+    """The speculative-sampling rule, restated in fp64 as the checker of this library's stochastic
+    acceptance (an extension: the reference has no stochastic acceptance, so parity is unpinned).
+    Draft i is accepted iff u_i q_i(d_i) < p_i(d_i); at the first rejection j the token is drawn by
+    inverse CDF from max(0, p_j - q_j) normalised, after L acceptances from p_L.  Rows are the
+    target's [S*(K+1), V] and the draft's [S*K, V] float32 values; every row is assumed sampleable.
+    Returns per sequence (accept_len, token, kind, the margin min |u q - p| / p over its tests, the
+    sampled distribution)."""
+    seqs, k = np.asarray(proposals).shape
+    out = []
+    for s in range(seqs):
+        L = int(lengths[s])
+        j, margin = L, np.inf
+        for i in range(L):
+            r = s * (k + 1) + i
+            p = masked_softmax(target_f32[r], masks[r], temperature)
+            q = masked_softmax(draft_f32[s * k + i], masks[r], temperature)
+            d = int(proposals[s, i])
+            if p[d] > 0:
+                margin = min(margin, abs(u_accept[s, i] * q[d] - p[d]) / p[d])
+            if not (q[d] > 0 and u_accept[s, i] * q[d] < p[d]):
+                j = i
+                break
+        r = s * (k + 1) + j
+        p = masked_softmax(target_f32[r], masks[r], temperature)
+        dist = p
+        if j < L:
+            res = np.maximum(0.0, p - masked_softmax(draft_f32[s * k + j], masks[r], temperature))
+            if res.sum() > 0:
+                dist = res / res.sum()
+        cum = np.cumsum(dist)
+        cut = u_resample[s] * cum[-1]
+        token = int(np.searchsorted(cum, cut, side="right"))
+        token = min(token, int(np.flatnonzero(dist > 0)[-1]))
+        out.append((j, token, 0 if j < L else (1 if L > 0 else 2), margin, dist))
+    return out
+
+
 def grammar_choices(draft, rows, grammar, *, dtype: str | None = None):
     """The reference's grammar-constrained verification loop (models/transformers.py:181-201:
     ``_choices`` + ``constrained_choices`` over decoding/verification.py:18-48 ``verify_prefix``),

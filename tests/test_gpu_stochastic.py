@@ -1,0 +1,136 @@
+"""Stochastic speculative acceptance (``stochastic.speculative_accept``; an extension: the reference
+decodes greedily, docs/design.md:5-11, so there is no reference output to pin it to).  The proof is
+distributional: with drafts drawn from the draft model's masked softmax q, the first emitted token
+must follow the target's masked softmax p (chi-square), and the acceptance rate must be
+sum_x min(p(x), q(x)).  At full vocabulary the GPU must also agree with the rule restated in fp64
+(``oracle.speculative_accept``) except where a uniform sits within rounding of a decision: 1e-5
+relative for the acceptance tests, and 1e-5 of a CDF boundary for the drawn token (fp32 weights, and
+the replacement distribution p - q cancels leading digits where p and q are close)."""
+
+import numpy as np
+import pytest
+
+import oracle
+from bitmask_speculation_b200 import workloads as wl
+
+torch = pytest.importorskip("torch")
+scipy_stats = pytest.importorskip("scipy.stats")
+pytestmark = pytest.mark.gpu
+
+
+def _bf16(values):
+    return torch.from_numpy(wl.to_bf16_bits(values).view(np.int16)).view(torch.bfloat16)
+
+
+def _widen(t):
+    return (t.cpu().view(torch.int16).numpy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_first_token_follows_the_target_distribution():
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rng = np.random.default_rng(4)
+    vocab, n, temp = 1024, 200_000, 0.9
+    valid = rng.random(vocab) < 0.3
+    mask = wl.pack_bits_np(valid[None, :])
+    tvals = _bf16(rng.standard_normal((2, vocab), dtype=np.float32) * np.float32(1.2))
+    dvals = _bf16(rng.standard_normal((1, vocab), dtype=np.float32) * np.float32(1.2))
+    p = oracle.masked_softmax(_widen(tvals[0]), mask[0], temp)
+    q = oracle.masked_softmax(_widen(dvals[0]), mask[0], temp)
+    drafts = rng.choice(vocab, size=n, p=q)  # the draft model's samples
+    dev = torch.device("cuda")
+    target = tvals.to(dev).repeat(n, 1)                     # [2n, V]: position 0 and the bonus row
+    draft = dvals.to(dev).repeat(n, 1)                      # [n, V]
+    masks = torch.from_numpy(mask).to(dev).repeat(2 * n, 1)
+    out = speculative_accept(target, draft, masks, torch.from_numpy(drafts[:, None]).to(dev),
+                             torch.ones(n, dtype=torch.int32, device=dev), temperature=temp,
+                             generator=torch.Generator(device=dev).manual_seed(1))
+    acc, tok, st = out.accept_len.cpu().numpy(), out.token.cpu().numpy(), out.status.cpu().numpy()
+    assert (st == 0).all()
+    first = np.where(acc >= 1, drafts, tok)
+    # acceptance rate: sum_x min(p, q)
+    rate = np.minimum(p, q).sum()
+    assert abs(acc.mean() - rate) < 4 * np.sqrt(rate * (1 - rate) / n)
+    # chi-square of the first emitted token against p (bins with expected count >= 5)
+    counts = np.bincount(first, minlength=vocab)
+    expected = p * n
+    big = expected >= 5
+    obs = np.append(counts[big], counts[~big].sum())
+    exp = np.append(expected[big], expected[~big].sum())
+    keep = exp > 0
+    assert counts[~valid].sum() == 0
+    assert scipy_stats.chisquare(obs[keep], exp[keep] * obs.sum() / exp[keep].sum()).pvalue > 1e-4
+
+
+def test_fallback_token_without_drafts_follows_the_target_distribution():
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rng = np.random.default_rng(8)
+    vocab, n, temp = 512, 100_000, 0.7
+    valid = rng.random(vocab) < 0.5
+    mask = torch.from_numpy(wl.pack_bits_np(valid[None, :])).cuda()
+    row = _bf16(rng.standard_normal((1, vocab), dtype=np.float32))
+    p = oracle.masked_softmax(_widen(row[0]), mask.cpu().numpy()[0], temp)
+    out = speculative_accept(row.cuda().repeat(n, 1), torch.empty((0, vocab), dtype=torch.bfloat16, device="cuda"),
+                             mask.repeat(n, 1), torch.zeros((n, 0), dtype=torch.int64, device="cuda"),
+                             torch.zeros(n, dtype=torch.int32, device="cuda"), temperature=temp)
+    tok = out.token.cpu().numpy()
+    assert (out.kind.cpu().numpy() == 2).all() and (out.accept_len.cpu().numpy() == 0).all()
+    counts = np.bincount(tok, minlength=vocab)
+    big = p * n >= 5
+    obs = np.append(counts[big], counts[~big].sum())
+    exp = np.append(p[big] * n, p[~big].sum() * n)
+    assert scipy_stats.chisquare(obs, exp * obs.sum() / exp.sum()).pvalue > 1e-4
+
+
+def test_full_vocabulary_rounds_agree_with_the_restated_rule():
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rng = np.random.default_rng(12)
+    seqs, k, vocab, temp = 48, 8, wl.VOCAB, 0.8
+    rows = seqs * (k + 1)
+    valid = wl.verify_masks_np(rng, rows, vocab)
+    masks = wl.pack_bits_np(valid)
+    tvals = _bf16(rng.standard_normal((rows, vocab), dtype=np.float32) * np.float32(2))
+    dvals_np = _widen(tvals).reshape(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab).copy()
+    dvals_np += rng.standard_normal(dvals_np.shape, dtype=np.float32) * np.float32(0.7)  # a similar draft model
+    dvals = _bf16(dvals_np)
+    tf, df = _widen(tvals), _widen(dvals)
+    proposals = np.zeros((seqs, k), dtype=np.int64)
+    lengths = rng.integers(0, k + 1, size=seqs).astype(np.int32)
+    for s in range(seqs):
+        for i in range(lengths[s]):
+            r = s * (k + 1) + i
+            proposals[s, i] = rng.choice(vocab, p=oracle.masked_softmax(df[s * k + i], masks[r], temp))
+    ua = rng.random((seqs, k))
+    ur = rng.random(seqs)
+    out = speculative_accept(tvals.cuda(), dvals.cuda(), torch.from_numpy(masks).cuda(), torch.from_numpy(proposals).cuda(),
+                             torch.from_numpy(lengths).cuda(), temperature=temp,
+                             accept_uniforms=torch.from_numpy(ua).cuda(), resample_uniforms=torch.from_numpy(ur).cuda())
+    acc, tok, kind, st = (t.cpu().numpy() for t in (out.accept_len, out.token, out.kind, out.status))
+    assert (st == 0).all()
+    want = oracle.speculative_accept(tf, df, masks, proposals, lengths, temp, ua, ur)
+    checked = 0
+    for s, (j, t, kd, margin, dist) in enumerate(want):
+        if margin < 1e-5:
+            continue  # a uniform within rounding of an acceptance threshold
+        assert acc[s] == j and kind[s] == kd, s
+        if tok[s] != t:
+            cum = np.cumsum(dist)
+            lo, hi = cum[tok[s]] - dist[tok[s]], cum[tok[s]]
+            assert dist[tok[s]] > 0 and min(abs(ur[s] - lo), abs(ur[s] - hi)) <= 1e-5, (s, tok[s], t)
+        checked += 1
+    assert checked >= seqs - 2 and (acc > 0).any() and (acc < lengths).any()
+
+
+def test_failed_and_invalid_rows_report_statuses():
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    vocab, k = 256, 2
+    tvals = torch.zeros((3 * (k + 1), vocab), device="cuda")
+    dvals = torch.zeros((3 * k, vocab), device="cuda")
+    masks = torch.full((3 * (k + 1), vocab // 32), -1, dtype=torch.int32, device="cuda")
+    tvals[0, 5] = float("nan")          # sequence 0: its first target row is consumed -> NaN
+    masks[3 * 1 + 0].zero_()            # sequence 1: the first row has no valid token
+    lengths = torch.tensor([2, 1, 3], dtype=torch.int32, device="cuda")  # sequence 2: L > K
+    out = speculative_accept(tvals, dvals, masks, torch.zeros((3, k), dtype=torch.int64, device="cuda"), lengths,
+                             temperature=1.0)
+    assert out.status.cpu().tolist() == [2, 1, 6]
+    with pytest.raises(ValueError, match="NaN"):
+        out.events(0, [0, 0])
