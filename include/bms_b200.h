@@ -108,8 +108,9 @@ BMS_API int bms_masked_reduce_batch(const void *logits, int32_t dtype, const int
                             void *workspace, int64_t workspace_bytes, int32_t device, void *stream);
 
 /* bms_masked_reduce_batch on the dynamic schedule with a workspace that is a file-scope device
- * array (about 1.8 MB per device) instead of caller memory: the call allocates nothing.  No
- * reference counterpart.  Rows of at most 64 chunks (524,288 16-bit or 262,144 float32 tokens;
+ * array (about 1.8 MB per device, held until the process exits) instead of caller memory: the call
+ * allocates nothing, for callers that may not allocate device memory (an engine whose allocator
+ * owns the free HBM, a binding without a device allocator).  No reference counterpart.  Rows of at most 64 chunks (524,288 16-bit or 262,144 float32 tokens;
  * longer rows fail with BMS_ERROR_UNSUPPORTED).  Calls that overlap in time on one device (other
  * streams or threads) share the array and race: serialize them.  The first call on a device
  * resolves the array's address and clears its counters; make it before any stream capture. */
