@@ -802,7 +802,9 @@ def run_b200_arm(args):
             # than kernel timings.
             esteps = max(args.steps, 50)
             t0 = time.perf_counter()
+            torch.cuda.nvtx.range_push("e2e")
             etime = timed_loop(e.step, esteps, device, dist)
+            torch.cuda.nvtx.range_pop()
             wall = time.perf_counter() - t0
             if w.kind == "grammar":  # the same round uploading every row's mask words instead
                 e.use_table = False
