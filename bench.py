@@ -469,9 +469,9 @@ class EndToEnd:
             self.d2h = w.rows * (8 + 8 + 4 + 4) + s * (4 + 8 + 4 + 4)
         elif w.kind == "verify":
             from bitmask_speculation_b200.compressed_masks import CompressedMasks
-            # The round's masks in their compact transfer form: rows with few valid tokens (the
-            # enumeration rows) as token-ID lists, the others as bitmaps, expanded on the device
-            # into a mask table that the verification reads through per-row indices.
+            # The round's masks in their compact transfer form: each row as the smallest of a bitmap,
+            # a token-ID list (the enumeration rows) or a byte-coded gap stream (the 5 % rows),
+            # expanded on the device into a mask table read through per-row indices.
             self.cm = CompressedMasks.from_bitmaps(w.masks.cpu().numpy(), w.vocab)
             self.tables = [self.cm.allocate(w.device) for _ in range(2)]
             self.h_prop = w.proposals.cpu().pin_memory()
@@ -824,9 +824,10 @@ def run_b200_arm(args):
                                    "row, one launch pair, one sync, events replayed on the sequences' grammars "
                                    "every step"),
                        "verify": ("compressed_masks.CompressedMasks.upload + verification.verify_batch (public API): "
-                                  "every step the round's masks go host->device in compact form (rows with at most "
-                                  "970 valid tokens as token-ID lists, expanded on the device by "
-                                  "bms_expand_token_lists; the others as bitmaps) with the drafts and lengths, "
+                                  "every step the round's masks go host->device in compact form (each row as the "
+                                  "smallest of a bitmap, a token-ID list or a byte-coded gap stream, lists and streams "
+                                  "expanded on the device by bms_expand_token_lists / bms_expand_token_gaps) with the "
+                                  "drafts and lengths, "
                                   "device-resident logits, results D2H; each step's upload on a copy stream "
                                   "overlaps the previous step's kernels (two input buffers)"),
                        "sample": ("kernels.cuda.batched_masked_sample (public API): pinned host masks H2D, "

@@ -33,7 +33,7 @@ class Policy(ctypes.Structure):
 EXPORTS = (
     "bms_last_error", "bms_runtime_version", "bms_mask_count", "bms_masked_argmax",
     "bms_masked_reduce_batch", "bms_masked_sample", "bms_masked_sample_batch",
-    "bms_mask_budget", "bms_expand_token_lists", "bms_speculative_accept", "bms_verify_batch", "bms_set_launch_override", "bms_shard_granule_bytes",
+    "bms_mask_budget", "bms_expand_token_lists", "bms_expand_token_gaps", "bms_speculative_accept", "bms_verify_batch", "bms_set_launch_override", "bms_shard_granule_bytes",
     "bms_shard_partials", "bms_shard_merge", "bms_workspace_bytes", "bms_masked_reduce_batch_noalloc",
     "bms_exchange_bytes", "bms_exchange_create", "bms_exchange_open", "bms_exchange_close", "bms_exchange_destroy",
     "bms_shard_partials_exchange", "bms_shard_merge_exchange",
@@ -60,6 +60,7 @@ def _declare(lib) -> None:
         "bms_masked_sample_batch": [p, i32, p, i64, i64, f64, p, p, p, p, p, i64, i32, p],
         "bms_mask_budget": [p, i64, i64, ctypes.POINTER(Policy), p, p, p, i32, p],
         "bms_expand_token_lists": [p, i64, p, i64, i64, p, p, i32, p],
+        "bms_expand_token_gaps": [p, i64, p, i64, i64, p, p, i32, p],
         "bms_speculative_accept": [p, p, i32, p, i64, i64, i64, p, p, p, p, f64, p, p, p, p, p, p, i32, p],
         "bms_verify_batch": [p, i32, p, i64, i64, i64, p, p, ctypes.POINTER(Policy), p, p, p, p,
                              p, p, p, p, p, i64, p, i64, i32, p],

@@ -462,6 +462,57 @@ __global__ void __launch_bounds__(256) expand_lists_kernel(const int32_t* __rest
     }
 }
 
+// Byte-coded gap streams to packed mask rows, one CTA per row (grid-stride).  Row l's stream is
+// bytes[offsets[l], offsets[l + 1]) (clamped to [0, n_bytes]); starting before token 0, a byte b > 0
+// advances b tokens and allows the token reached, a byte 0 advances 255 tokens and allows nothing.
+// Each thread decodes one contiguous segment of the stream: segment advances are summed, a block
+// scan gives every segment's starting token, then each segment sets its bits (atomicOr after the
+// row is cleared).  Tokens at or past `vocab` set nothing and flag the row in `bad` (nullable).
+__global__ void __launch_bounds__(256) expand_gaps_kernel(const uint8_t* __restrict__ bytes, int64_t n_bytes,
+                                                          const int32_t* __restrict__ offsets, int64_t rows,
+                                                          int64_t vocab, int32_t* __restrict__ out,
+                                                          int32_t* __restrict__ bad) {
+    __shared__ long long warp_sums[8];
+    const int64_t words = (vocab + 31) / 32;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    for (int64_t l = blockIdx.x; l < rows; l += gridDim.x) {
+        uint32_t* row = reinterpret_cast<uint32_t*>(out) + l * words;
+        for (int64_t w = tid; w < words; w += blockDim.x) row[w] = 0u;
+        int64_t b = offsets[l], e = offsets[l + 1];
+        b = b < 0 ? 0 : b > n_bytes ? n_bytes : b;
+        e = e < b ? b : e > n_bytes ? n_bytes : e;
+        const int64_t per = (e - b + blockDim.x - 1) / blockDim.x;
+        const int64_t s0 = b + tid * per < e ? b + tid * per : e;
+        const int64_t s1 = s0 + per < e ? s0 + per : e;
+        long long local = 0;
+        for (int64_t i = s0; i < s1; ++i) {
+            const uint32_t c = bytes[i];
+            local += c ? c : 255u;
+        }
+        long long v = local;  // inclusive scan: warps, then the 8 warp totals
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+            if (lane >= o) v += n;
+        }
+        if (lane == 31) warp_sums[wid] = v;
+        __syncthreads();  // also orders the cleared words before any bit is set
+        long long pos = -1 + v - local;
+        for (int w = 0; w < wid; ++w) pos += warp_sums[w];
+        int flag = 0;
+        for (int64_t i = s0; i < s1; ++i) {
+            const uint32_t c = bytes[i];
+            pos += c ? c : 255u;
+            if (c) {
+                if (pos < vocab) atomicOr(row + (pos >> 5), 1u << (pos & 31));
+                else flag = 1;
+            }
+        }
+        flag = __syncthreads_or(flag);
+        if (bad != nullptr && tid == 0) bad[l] = flag;
+    }
+}
+
 // ---------------------------------------------------------------- stochastic speculative acceptance
 // Row normaliser of a sampler partial (one rank covering the whole row): the partial's reference
 // max M and the row's mass S relative to it, or a status code for rows that cannot be sampled
@@ -1136,6 +1187,25 @@ int bms_expand_token_lists(const int32_t* ids, int64_t n_ids, const int32_t* off
     const unsigned grid = static_cast<unsigned>(lists < cap ? lists : cap);
     expand_lists_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(ids, n_ids, offsets, lists, vocab, out, bad);
     BMS_CUDA(cudaGetLastError(), "token-list expansion launch");
+    return BMS_SUCCESS;
+}
+
+int bms_expand_token_gaps(const uint8_t* bytes, int64_t n_bytes, const int32_t* offsets, int64_t rows, int64_t vocab,
+                          int32_t* out, int32_t* bad, int32_t device, void* stream) {
+    BMS_CHECK(check_vocab(vocab));
+    if (rows < 0 || n_bytes < 0) return fail(BMS_ERROR_INVALID_ARGUMENT, "rows and n_bytes must be nonnegative");
+    BMS_CHECK(check_device(device));
+    if (rows == 0) return BMS_SUCCESS;
+    if (n_bytes > 0) BMS_CHECK(check_ptr(bytes, device, "bytes", 1));
+    BMS_CHECK(check_ptr(offsets, device, "offsets", 4));
+    BMS_CHECK(check_ptr(out, device, "out", 4));
+    if (bad) BMS_CHECK(check_ptr(bad, device, "bad", 4));
+    DeviceGuard guard;
+    BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
+    const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+    expand_gaps_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(bytes, n_bytes, offsets, rows, vocab, out, bad);
+    BMS_CUDA(cudaGetLastError(), "gap-stream expansion launch");
     return BMS_SUCCESS;
 }
 
