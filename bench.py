@@ -48,7 +48,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["verify", "grammar", "argmax", "sample", "scale", "vocab", "decode"],
+    ap.add_argument("--workload", choices=["verify", "grammar", "argmax", "sample", "scale", "vocab", "decode",
+                                           "stochastic"],
                     default="verify")
     ap.add_argument("--prompts", type=int, default=32, help="prompts for the decode workload")
     ap.add_argument("--new-tokens", type=int, default=256, help="tokens generated per prompt (decode workload)")
@@ -974,8 +975,99 @@ def run_decode(args):
     print(json.dumps(line), flush=True)
 
 
+def run_stochastic(args):
+    """Stochastic speculative acceptance at the verification round's shape: 256 sequences x K = 8
+    drafts (``--seqs``), target rows bf16 N(0, 3^2) with the round's masks, draft rows = the target's
+    first K rows of each sequence plus N(0, 0.7^2) noise (a close draft model), drafts sampled from
+    the draft's masked softmax at T = 0.8 with the batched sampler.  One step = the target and draft
+    rows' sampler partials (two selection launches) and the acceptance kernel, on device-resident
+    inputs; rows/s counts target rows.  No reference implementation exists (the reference's
+    contract is greedy), so there is no reference arm; the CPU figure is this rule restated in fp64
+    (``oracle.speculative_accept``) on a few sequences."""
+    import numpy as np
+    import torch
+    import oracle
+    from bitmask_speculation_b200 import workloads as wl
+    from bitmask_speculation_b200.kernels._extension import load_extension
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    temp, k = 0.8, wl.DRAFT_K
+    logits, masks, _, _ = wl.verify_batch_torch(args.seqs, seed=3, device=device)
+    seqs, vocab = args.seqs, wl.VOCAB
+    words = masks.shape[1]
+    g = torch.Generator(device=device).manual_seed(7)
+    first_k = logits.view(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab)
+    draft = (first_k.float() + 0.7 * torch.randn(first_k.shape, generator=g, device=device)).to(torch.bfloat16)
+    del first_k
+    dmasks = masks.view(seqs, k + 1, words)[:, :k].reshape(seqs * k, words).contiguous()
+    native = load_extension()
+    u = torch.rand(seqs * k, dtype=torch.float64, generator=g, device=device)
+    proposals = native.masked_sample_batch(draft, dmasks, temp, u)[0].view(seqs, k).contiguous()
+    lengths = torch.full((seqs,), k, dtype=torch.int32, device=device)
+    ua = torch.rand((seqs, k), dtype=torch.float64, generator=g, device=device)
+    ur = torch.rand(seqs, dtype=torch.float64, generator=g, device=device)
+
+    def step():
+        return speculative_accept(logits, draft, masks, proposals, lengths, temperature=temp, accept_uniforms=ua,
+                                  resample_uniforms=ur)
+    out = step()
+    # Untimed check against the fp64 restatement on the first sequences.
+    n_chk = 6
+    tf = (logits[: n_chk * (k + 1)].cpu().view(torch.int16).numpy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    df = (draft[: n_chk * k].cpu().view(torch.int16).numpy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    want = oracle.speculative_accept(tf, df, masks[: n_chk * (k + 1)].cpu().numpy(), proposals[:n_chk].cpu().numpy(),
+                                     lengths[:n_chk].cpu().numpy(), temp, ua[:n_chk].cpu().numpy(), ur[:n_chk].cpu().numpy())
+    acc = out.accept_len.cpu().numpy()
+    for s_, (j, _, _, margin, _) in enumerate(want):
+        if margin > 1e-5 and acc[s_] != j:
+            raise SystemExit("stochastic acceptance differs from the restated rule")
+    with ClockSampler(local) as clocks:
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.nvtx.range_push("timed")
+        seconds = timed_loop(step, args.steps, device)
+        torch.cuda.nvtx.range_pop()
+    per_step = seconds / args.steps
+    rows = seqs * (k + 1)
+    algorithmic = (rows + seqs * k) * (vocab * 2 + words * 4 + 32) + seqs * 2 * vocab * 2
+    t0 = time.perf_counter()
+    oracle.speculative_accept(tf, df, masks[: n_chk * (k + 1)].cpu().numpy(), proposals[:n_chk].cpu().numpy(),
+                              lengths[:n_chk].cpu().numpy(), temp, ua[:n_chk].cpu().numpy(), ur[:n_chk].cpu().numpy())
+    cpu_rows = n_chk * (k + 1) / (time.perf_counter() - t0)
+    peak, peak_kind = measured_peak()
+    line = {
+        "metric": "rows/s", "value": rows / per_step, "unit": "rows/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": (f"stochastic: {seqs} sequences x K={k} drafts sampled from a draft model at T={temp}, "
+                                f"V={vocab} bf16, verification-round masks; target rows/s"),
+                   "rows_per_gpu": rows, "draft_rows": seqs * k},
+        "roofline": {"bound": "hbm", "achieved": algorithmic / per_step / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": algorithmic / per_step / 1e9 / peak, "peak_kind": peak_kind,
+                     "kernel": "whole step (two sampler-partials launches + acceptance kernel)",
+                     "bytes_per_step": algorithmic},
+        "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
+        "acceptance_rate": float(out.accept_len.double().mean().item()) / k,
+        "cpu_baseline": {"value": cpu_rows, "unit": "rows/s", "cores": 1, "kind": "port",
+                         "sample": f"{n_chk} sequences through oracle.speculative_accept (fp64 numpy restatement of "
+                                   "this library's rule; the reference has no stochastic acceptance)"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.workload == "stochastic":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no stochastic speculative "
+                              "acceptance (its correctness contract is greedy, docs/design.md:5-11)"}), flush=True)
+        else:
+            run_stochastic(args)
+        return
     if args.workload == "decode":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference's engine (Transformers models, "

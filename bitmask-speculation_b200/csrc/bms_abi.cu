@@ -521,11 +521,12 @@ struct RowNorm {
     float M;
     double S;
     int32_t code;
+    double invS;  // 1 / S, so that each weight costs a multiply, not a division
 };
 
 __device__ __forceinline__ RowNorm row_norm(const GatherSlot& g) {
     const float kInf = __int_as_float(0x7F800000);
-    RowNorm r{__uint_as_float(g.a), g.s, kOk};
+    RowNorm r{__uint_as_float(g.a), g.s, kOk, g.s > 0.0 ? 1.0 / g.s : 0.0};
     r.code = (g.c & kFlagAbort) ? kTimeout : (g.c & kFlagNaN) ? kNaN : (r.M == kInf) ? kPosInf : (g.b == 0u) ? kEmpty
              : (r.M == -kInf || !(r.S > 0.0)) ? kNoMass : kOk;
     return r;
@@ -536,7 +537,34 @@ __device__ __forceinline__ RowNorm row_norm(const GatherSlot& g) {
 __device__ __forceinline__ double spec_weight(float x, const RowNorm& n, float sc) {
     const float d = x - n.M;
     const float t = d == 0.0f ? 0.0f : fminf(d * sc, 126.0f);
-    return static_cast<double>(ptx::ex2(t)) / n.S;
+    return static_cast<double>(ptx::ex2(t)) * n.invS;
+}
+
+// Tokens [a, a + 8) of a row as floats (0 past `vocab`): one or two 16-byte loads when the row is
+// 16-byte aligned (`vec`), else scalar loads.  No branch on the mask, so the loads of several
+// calls can be in flight together.
+template <typename T>
+__device__ __forceinline__ void load8(const T* row, int64_t a, int64_t vocab, bool vec, float (&x)[8]) {
+    using E = Elem<T>;
+    if (vec && a + 8 <= vocab) {
+        if constexpr (E::kBytes == 2) {
+            const uint4 r = __ldg(reinterpret_cast<const uint4*>(row + a));
+            const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                x[2 * i] = E::lo(w[i]);
+                x[2 * i + 1] = E::hi(w[i]);
+            }
+        } else {
+            const float4 p0 = __ldg(reinterpret_cast<const float4*>(row + a));
+            const float4 p1 = __ldg(reinterpret_cast<const float4*>(row + a) + 1);
+            x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
+            x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = a + i < vocab ? E::load(row, a + i) : 0.0f;
+    }
 }
 
 // Speculative sampling for S sequences, one CTA each.  Sequence s has lengths[s] = L drafts
@@ -557,10 +585,16 @@ __global__ void __launch_bounds__(256) speculative_accept_kernel(
     int32_t* __restrict__ kind, int32_t* __restrict__ status) {
     using E = Elem<T>;
     __shared__ double sums[256];
-    __shared__ int32_t s_j, s_code, s_residual, s_last;
-    __shared__ int64_t s_token;
-    const int tid = threadIdx.x, lane = tid & 31;
+    extern __shared__ double tile_sums[];  // one per 256 tokens of the vocabulary
+    __shared__ int32_t s_j, s_code, s_residual, s_last, s_cut_past, s_claim;
+    __shared__ int64_t s_token, s_tile;
+    __shared__ double s_prefix;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int64_t K = rows_per_seq - 1, words = (vocab + 31) / 32;
+    if (tid == 0) {
+        s_last = -1;
+        s_cut_past = 0;
+    }
     for (int64_t seq = blockIdx.x; seq < seqs; seq += gridDim.x) {
         const int32_t L = lengths[seq];
         if (tid < 32) {
@@ -614,50 +648,138 @@ __global__ void __launch_bounds__(256) speculative_accept_kernel(
         }
         int64_t chosen = -1;
         if (code == kOk) {
-            // Inverse CDF over the row's valid tokens, each thread owning one contiguous segment.
-            const int64_t per = (vocab + 255) / 256, t0 = tid * per, t1 = t0 + per < vocab ? t0 + per : vocab;
+            // Inverse CDF over the row's valid tokens in tiles of 256: a warp per tile, 8
+            // consecutive tokens per lane (coalesced), tile sums in shared memory; then a scan of
+            // the tile sums finds the tile holding v * total and one warp walks it.
             const T* trow_p = target + trow * vocab;
             const T* qrow_p = draft + (seq * K + j) * vocab;
             const int32_t* mrow = masks + trow * words;
+            const int64_t ntiles = (vocab + 255) / 256;
+            // 16-byte loads need 16-byte aligned rows (row starts at multiples of vocab elements).
+            const bool vec = (reinterpret_cast<uintptr_t>(target) % 16 == 0) &&
+                             (reinterpret_cast<uintptr_t>(draft) % 16 == 0) && ((vocab * sizeof(T)) % 16 == 0);
             for (int pass = 0; pass < 2 && chosen < 0; ++pass) {
                 const bool residual = s_residual && pass == 0;
-                auto weight = [&](int64_t t) -> double {
-                    if (!((static_cast<uint32_t>(mrow[t >> 5]) >> (t & 31)) & 1u)) return 0.0;
-                    const double w = spec_weight(E::load(trow_p, t), tn, sc);
-                    return residual ? fmax(0.0, w - spec_weight(E::load(qrow_p, t), qn, sc)) : w;
+                // Lane sum of tokens [t0 + 8 lane, +8) of the tile starting at t0.
+                auto lane_sum = [&](int64_t t0) -> double {
+                    const int64_t a = t0 + 8 * lane;
+                    if (a >= vocab) return 0.0;
+                    const uint32_t bits = (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu;
+                    float xt[8], xq[8];
+                    load8<T>(trow_p, a, vocab, vec, xt);
+                    if (residual) load8<T>(qrow_p, a, vocab, vec, xq);
+                    double acc = 0.0;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        if (!((bits >> i) & 1u) || a + i >= vocab) continue;
+                        const double w = spec_weight(xt[i], tn, sc);
+                        acc += residual ? fmax(0.0, w - spec_weight(xq[i], qn, sc)) : w;
+                    }
+                    return acc;
                 };
+                // Four tiles per warp and iteration (their loads overlap), 32 tiles apart.
+                for (int64_t tile = wid; tile < ntiles; tile += 32) {
+                    double v[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) v[q] = tile + 8 * q < ntiles ? lane_sum((tile + 8 * q) * 256) : 0.0;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                        for (int o = 16; o >= 1; o >>= 1) v[q] += __shfl_xor_sync(0xFFFFFFFFu, v[q], o);
+                        if (lane == 0 && tile + 8 * q < ntiles) tile_sums[tile + 8 * q] = v[q];
+                    }
+                }
+                if (tid == 0) {
+                    s_tile = -1;
+                    s_token = -1;
+                    s_last = -1;
+                    s_claim = 0;
+                }
+                __syncthreads();
+                // Scan of the tile sums in order: thread tid owns tiles [tid * per, (tid + 1) * per).
+                const int64_t per = (ntiles + 255) / 256;
+                const int64_t a0 = tid * per < ntiles ? tid * per : ntiles;
+                const int64_t a1 = a0 + per < ntiles ? a0 + per : ntiles;
                 double local = 0.0;
-                for (int64_t t = t0; t < t1; ++t) local += weight(t);
-                // Inclusive scan of the 256 segment sums: warp scans, then the 8 warp totals.
+                for (int64_t t = a0; t < a1; ++t) local += tile_sums[t];
                 double v = local;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
                     const double n = __shfl_up_sync(0xFFFFFFFFu, v, o);
                     if (lane >= o) v += n;
                 }
-                if (lane == 31) sums[tid >> 5] = v;
-                if (tid == 0) {
-                    s_token = -1;
-                    s_last = -1;
-                }
+                if (lane == 31) sums[wid] = v;
                 __syncthreads();
                 double before = 0.0, total = 0.0;
                 for (int w = 0; w < 8; ++w) {
-                    if (w < (tid >> 5)) before += sums[w];
+                    if (w < wid) before += sums[w];
                     total += sums[w];
                 }
-                const double incl = before + v, start = incl - local;
+                const double incl = before + v;
                 const double cut = u_resample[seq] * total;
                 if (total > 0.0 && local > 0.0) {
-                    atomicMax(&s_last, tid);
-                    if (cut >= start && cut < incl) {  // this segment holds the crossing: walk it
-                        double acc = start;
+                    atomicMax(&s_last, static_cast<int>(tid));
+                    if (cut >= incl - local && cut < incl) {
+                        double acc = incl - local;
                         int64_t pick = -1;
-                        for (int64_t t = t0; t < t1; ++t) {
-                            const double w = weight(t);
-                            if (w > 0.0) {
+                        double pick_prefix = 0.0;
+                        for (int64_t t = a0; t < a1; ++t) {
+                            if (tile_sums[t] > 0.0) {
                                 pick = t;
-                                if (cut < acc + w) break;
+                                pick_prefix = acc;
+                                if (cut < acc + tile_sums[t]) break;
+                                acc += tile_sums[t];
+                            }
+                        }
+                        if (atomicExch(&s_claim, 1) == 0) {  // rounding may let two segments claim
+                            s_tile = pick;
+                            s_prefix = pick_prefix;
+                        }
+                    }
+                }
+                __syncthreads();
+                if (s_tile < 0 && tid == s_last) {
+                    // Rounding put the cut past the last positive tile sum: that tile is walked,
+                    // and its last positive token taken.
+                    int64_t pick = -1;
+                    double acc = incl - local;
+                    double pick_prefix = 0.0;
+                    for (int64_t t = a0; t < a1; ++t)
+                        if (tile_sums[t] > 0.0) {
+                            pick = t;
+                            pick_prefix = acc;
+                            acc += tile_sums[t];
+                        }
+                    s_tile = pick;
+                    s_prefix = pick_prefix;
+                    s_cut_past = 1;
+                }
+                __syncthreads();
+                if (wid == 0 && s_tile >= 0) {
+                    const int64_t t0 = s_tile * 256;
+                    const double ls = lane_sum(t0);
+                    double li = ls;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const double n = __shfl_up_sync(0xFFFFFFFFu, li, o);
+                        if (lane >= o) li += n;
+                    }
+                    const bool past = s_cut_past != 0;
+                    const uint32_t pos = __ballot_sync(0xFFFFFFFFu, ls > 0.0);
+                    const uint32_t hit = __ballot_sync(0xFFFFFFFFu, !past && ls > 0.0 && cut < s_prefix + li);
+                    const int L = hit ? __ffs(hit) - 1 : (pos ? 31 - __clz(pos) : -1);
+                    if (lane == L) {
+                        const int64_t a = t0 + 8 * lane;
+                        const uint32_t bits = (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu;
+                        double acc = s_prefix + li - ls;
+                        int64_t pick = -1;
+                        for (int i = 0; i < 8; ++i) {
+                            if (!((bits >> i) & 1u) || a + i >= vocab) continue;
+                            double w = spec_weight(E::load(trow_p, a + i), tn, sc);
+                            if (residual) w = fmax(0.0, w - spec_weight(E::load(qrow_p, a + i), qn, sc));
+                            if (w > 0.0) {
+                                pick = a + i;
+                                if (hit && cut < acc + w) break;
                                 acc += w;
                             }
                         }
@@ -665,15 +787,8 @@ __global__ void __launch_bounds__(256) speculative_accept_kernel(
                     }
                 }
                 __syncthreads();
-                if (s_token < 0 && s_last == tid) {
-                    // Rounding put the cut past the last positive weight: its token is taken.
-                    int64_t pick = -1;
-                    for (int64_t t = t0; t < t1; ++t)
-                        if (weight(t) > 0.0) pick = t;
-                    s_token = pick;
-                }
-                __syncthreads();
                 chosen = s_token;
+                if (tid == 0) s_cut_past = 0;
                 __syncthreads();
             }
             if (chosen < 0) code = kNoMass;
@@ -1154,13 +1269,25 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
     const float sc = static_cast<float>(1.4426950408889634 / temperature);
+    // One double per 256 tokens of shared memory (7.8 KB at V = 248,320).
+    const size_t smem = static_cast<size_t>((vocab + 255) / 256) * sizeof(double);
+    if (smem > 200 * 1024) return fail(BMS_ERROR_UNSUPPORTED, "vocabulary too large for the acceptance kernel");
+    if (smem > 48 * 1024) {
+        BMS_CUDA(cudaFuncSetAttribute(speculative_accept_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)), "cudaFuncSetAttribute(smem)");
+        BMS_CUDA(cudaFuncSetAttribute(speculative_accept_kernel<__nv_bfloat16>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                 "cudaFuncSetAttribute(smem)");
+        BMS_CUDA(cudaFuncSetAttribute(speculative_accept_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)), "cudaFuncSetAttribute(smem)");
+    }
     const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
     const unsigned grid = static_cast<unsigned>(seqs < cap ? seqs : cap);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto tp = reinterpret_cast<const GatherSlot*>(target_partials);
     auto qp = reinterpret_cast<const GatherSlot*>(draft_partials);
 #define BMS_SPEC(T)                                                                                                  \
-    speculative_accept_kernel<T><<<grid, 256, 0, st>>>(                                                              \
+    speculative_accept_kernel<T><<<grid, 256, smem, st>>>(                                                           \
         static_cast<const T*>(target_logits), static_cast<const T*>(draft_logits), masks, seqs, rows_per_seq, vocab, \
         proposals, lengths, tp, qp, accept_uniforms, resample_uniforms, sc, accept_len, token, kind, status)
     if (dtype == BMS_FLOAT32) BMS_SPEC(float);
