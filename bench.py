@@ -655,9 +655,11 @@ def bench_config(w: Workload, world: int) -> dict:
                             else f"row-sharded x{world}, no collective")}
 
 
-def sampler_roofline(args, device, peak, peak_kind, rows_list=(256, 2304)):
+def sampler_roofline(args, device, peak, peak_kind, rows_list=(64, 256, 2304)):
     """The masked sampler alone at small and large batches (configuration-2 rows tiled, fp16,
-    T = 0.7, fresh uniforms; buffers rotated beyond L2): per-launch time and HBM fraction."""
+    T = 0.7, fresh uniforms; buffers rotated beyond L2): per-launch time and HBM fraction.  At 64
+    rows the library takes the flat schedule (two launches), at 256 the fixed one, at 2,304 the
+    dynamic one."""
     import copy
     out = {}
     for rows in rows_list:

@@ -95,7 +95,7 @@ class BatchedMaskedReduction:
 def batched_masked_reduce(logits, mask):
     """Masked argmax, valid-token count and status of every row of a [B, V] batch under its
     [B, ceil(V/32)] masks, as new [B] tensors on the device.  The whole batch is one selection
-    launch (two on the two-launch schedule); the host does not wait."""
+    launch; the host does not wait."""
     batched_selection_inputs(logits, mask)
     tokens, counts, status = load_extension().masked_reduce_batch(logits, mask)
     return BatchedMaskedReduction(tokens, counts, status)

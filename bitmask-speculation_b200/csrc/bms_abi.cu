@@ -117,6 +117,7 @@ struct KernelInfo {
     bool ready = false;
     int sms = 0;
     int max_clusters[5] = {0, 0, 0, 0, 0};  // resident clusters for each cluster size
+    int flat_ctas = 0;                      // resident CTAs of the flat-schedule variant (sampler, bulk)
 };
 
 std::mutex g_mutex;
@@ -134,6 +135,14 @@ int kernel_info(int device, KernelInfo*& out) {
         BMS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
                  "cudaFuncSetAttribute(cluster)");
         BMS_CUDA(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+        if constexpr (kSample && kBulk) {
+            auto flat = select_rows_kernel<T, true, true, kStages, true>;
+            BMS_CUDA(cudaFuncSetAttribute(flat, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                     "cudaFuncSetAttribute(smem)");
+            int per_sm = 0;
+            BMS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, flat, kThreads, smem), "flat occupancy");
+            info.flat_ctas = per_sm * info.sms;
+        }
         for (int i = 0; i < 5; ++i) {
             cudaLaunchConfig_t cfg = {};
             cudaLaunchAttribute attr[1];
@@ -255,38 +264,65 @@ bool launch_dynamic(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t&
     return true;
 }
 
-// Two-launch schedule of sampler batches with more rows than resident CTAs but fewer than 1.5 per
-// CTA (a workspace is given, rows of at most kWsChunks chunks, no forced launch shape).  There the
-// fixed schedule gives some CTAs two rows and others one, and merging the pieces of split rows
-// inside the launch puts a chain of global round trips and fp64 work (about 5 us per row) on the
-// finalizer warp, which then holds up its consumers.  Instead every row is cut into blocks of
-// chunks that the CTAs take as tickets (about four per CTA, so that fast CTAs take more), each
-// piece only publishes its partial and granules, and a second launch merges every row in
-// parallel, one warp per row (merge_pieces_kernel).  Measured on B200 (configuration-2 rows, fp16):
-// 600 rows 76 us against 88 us on the fixed schedule; at 256 and 444 rows the fixed schedule wins
-// (39 / 51 us against 44 / 62 us): each piece costs its consumers about 1.2 us of hand-off and
-// waits, and the second launch adds a kernel boundary (about 2.3 us) and the merge (about 5 us).
+// Flat schedule of sampler batches with fewer than 1.5 rows per resident CTA (a workspace with
+// the flat-record area is given, rows of at most kWsChunks chunks, no forced launch shape).  The
+// batch's chunks, in row-major order, are taken as tickets by one-CTA clusters filling every
+// resident slot, every ticket from the counter (a CTA that starts late owns no block); tickets
+// shrink by tier -- one block per CTA of about 60 % of its even share, one of about 20 %, then
+// blocks of two chunks (single chunks when the batch has no more chunks than CTAs) -- so that
+// most chunks stream in long pieces and SMs streaming at different speeds still finish together.
+// Consumer warps store one record per (chunk, warp) granule to the workspace and hand nothing over
+// at a piece boundary; a second launch (flat_merge_kernel) merges and walks every row in parallel.
+//
+// Measured on B200 (configuration-2 rows, fp16, 31 chunks per row, CUDA events, back to back):
+// 16 / 32 / 48 / 74 / 100 / 120 rows 16.4 / 18.7 / 20.3 / 22.4 / 25.3 / 27.5 us against 18.7 /
+// 24.9 / 28.5 / 28.7 / 28.9 / 29.1 us on the fixed schedule; 200 rows 36.2 against 38.9; 480 /
+// 560 / 665 rows 61.8 / 69.1 / 78.3 against 63.9 / 73.0 / 82.6 on the former two-launch split
+// schedule.  Batches that fill the SMs' row slots evenly stream faster on the fixed schedule
+// (148 / 256 / 444 rows 29.3 / 39.2 / 50.6 us against 30.7 / 41.6 / 58.6 us): up to one row per
+// resident CTA the flat schedule runs only where its cost, about 14.8 us + 0.47 us x chunks / SMs,
+// undercuts the fixed schedule's, about 18.6 us + 0.34 us x chunks per row x ceil(rows / SMs), by
+// more than 1.5 us.
+constexpr int64_t kFlatTierPct[2] = {60, 20};
+constexpr int64_t kFlatSmallBlock = 2;
+
 template <typename T, bool kSample, bool kBulk, int kStages>
-bool launch_two_phase(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t& cfg) {
+bool launch_flat(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t& cfg) {
     constexpr int kTPC = Layout<T>::kTokensPerChunk;
     const int64_t n = (p.vocab + kTPC - 1) / kTPC;
-    const int64_t grid = info.max_clusters[0];
-    if (p.ws == nullptr || p.partials != nullptr || p.dynamic_always || g_force_cluster != 0 || g_force_clusters != 0 ||
-        !kSample || n > kWsChunks || p.rows <= grid || 2 * p.rows >= 3 * grid || p.rows > p.ws_rows)
+    const int64_t grid = info.flat_ctas;
+    if (!kSample || !kBulk || grid <= 0 || p.ws == nullptr || !p.ws_flat || p.partials != nullptr || p.dynamic_always ||
+        g_force_cluster != 0 || g_force_clusters != 0 || n > kWsChunks || p.rows > p.ws_rows || 2 * p.rows >= 3 * grid)
         return false;
-    // About four blocks per CTA, at least 4 chunks each (at most 17 pieces per row).
     const int64_t chunks = p.rows * n;
-    int64_t block = (chunks + 4 * grid - 1) / (4 * grid);
-    block = block < 4 ? 4 : block > kWsChunks ? kWsChunks : block;
-    p.publish_only = 1;
+    const int64_t sms = info.sms;
+    if (p.rows <= grid && 2 * p.rows >= sms) {
+        const double flat_us = 14.8 + 0.47 * static_cast<double>(chunks) / static_cast<double>(sms);
+        const double fixed_us = 18.6 + 0.34 * static_cast<double>(n) * static_cast<double>((p.rows + sms - 1) / sms);
+        if (fixed_us <= flat_us + 1.5) return false;
+    }
+    const int64_t small = chunks <= grid ? 1 : kFlatSmallBlock;
+    int64_t rem = chunks, tickets = 0;
+    for (int i = 0; i < 2; ++i) {
+        int64_t b = chunks * kFlatTierPct[i] / (100 * grid);
+        if (b < small) b = small;
+        int64_t t = rem / b;
+        if (t > grid) t = grid;
+        p.tier_block[i] = static_cast<int32_t>(b);
+        p.tier_tickets[i] = t;
+        rem -= t * b;
+        tickets += t;
+    }
+    tickets += (rem + small - 1) / small;
+    p.flat = 1;
     p.whole_rows = 0;
-    p.block = static_cast<int32_t>(block);
-    p.tickets = (chunks + block - 1) / block;
+    p.block = static_cast<int32_t>(small);
+    p.tickets = tickets;
     p.segment = (p.vocab + 31) / 32 * 32;
     uint32_t e = ++g_epoch;
     if (e == 0) e = ++g_epoch;
     p.epoch = e;
-    cfg.gridDim = dim3(static_cast<unsigned>(p.tickets < grid ? p.tickets : grid));
+    cfg.gridDim = dim3(static_cast<unsigned>(tickets < grid ? tickets : grid));
     return true;
 }
 
@@ -299,24 +335,25 @@ int launch_select_t(SelectParams p, int device, cudaStream_t stream) {
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
     {
         cudaLaunchConfig_t cfg = {};
-        if (launch_two_phase<T, kSample, kBulk, kStages>(p, *info, cfg)) {
-            cfg.blockDim = dim3(kThreads);
-            cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
-            cfg.stream = stream;
-            const bool full = static_cast<int>(cfg.gridDim.x) >= info->max_clusters[0];
-            cfg.attrs = pdl;
-            cfg.numAttrs = full ? 1 : 0;
-            BMS_CUDA(cudaLaunchKernelEx(&cfg, select_rows_kernel<T, kSample, kBulk, kStages>, p), "selection launch");
-            cudaLaunchConfig_t mcfg = {};
-            const int64_t need = (p.rows + kMergeWarps - 1) / kMergeWarps;
-            const int64_t cap = static_cast<int64_t>(info->sms) * 4;
-            mcfg.gridDim = dim3(static_cast<unsigned>(need < cap ? need : cap));
-            mcfg.blockDim = dim3(kMergeWarps * 32);
-            mcfg.stream = stream;
-            mcfg.attrs = pdl;
-            mcfg.numAttrs = 1;
-            BMS_CUDA(cudaLaunchKernelEx(&mcfg, merge_pieces_kernel<T, kSample>, p), "piece merge launch");
-            return BMS_SUCCESS;
+        if (launch_flat<T, kSample, kBulk, kStages>(p, *info, cfg)) {
+            if constexpr (kSample && kBulk) {
+                cfg.blockDim = dim3(kThreads);
+                cfg.dynamicSmemBytes = select_smem_bytes<T, kSample>(kStages);
+                cfg.stream = stream;
+                const bool full = static_cast<int>(cfg.gridDim.x) >= info->flat_ctas;
+                cfg.attrs = pdl;
+                cfg.numAttrs = full ? 1 : 0;
+                BMS_CUDA(cudaLaunchKernelEx(&cfg, select_rows_kernel<T, true, true, kStages, true>, p), "selection launch");
+                cudaLaunchConfig_t mcfg = {};
+                const int64_t cap = static_cast<int64_t>(info->sms) * 8;
+                mcfg.gridDim = dim3(static_cast<unsigned>(p.rows < cap ? p.rows : cap));
+                mcfg.blockDim = dim3(kFlatMergeWarps * 32);
+                mcfg.stream = stream;
+                mcfg.attrs = pdl;
+                mcfg.numAttrs = 1;
+                BMS_CUDA(cudaLaunchKernelEx(&mcfg, flat_merge_kernel<T>, p), "flat merge launch");
+                return BMS_SUCCESS;
+            }
         }
     }
     {
@@ -1039,8 +1076,8 @@ int select_common(int dtype, const void* logits, const int32_t* masks, int64_t r
     return BMS_SUCCESS;
 }
 
-// Split-row capacity of a device's workspace: every row of a batch on the two-launch schedule
-// (fewer than 1.5 rows per resident CTA, at most 3 CTAs per SM).
+// Split-row capacity of a device's workspace: every row of a batch on the flat schedule (fewer
+// than 1.5 rows per resident CTA, at most 3 CTAs per SM).
 int64_t workspace_rows(int device) { return 5ll * sm_count(device); }
 
 int attach_workspace(SelectParams& p, void* ws, int64_t bytes, int device) {
@@ -1054,6 +1091,7 @@ int attach_workspace(SelectParams& p, void* ws, int64_t bytes, int device) {
     BMS_CHECK(check_ptr(ws, device, "workspace", 256));
     p.ws = static_cast<uint8_t*>(ws);
     p.ws_rows = workspace_rows(device);
+    p.ws_flat = 1;
     return BMS_SUCCESS;
 }
 
@@ -1061,7 +1099,7 @@ int attach_workspace(SelectParams& p, void* ws, int64_t bytes, int device) {
 // device), so that entry point allocates nothing.  Split-row capacity kStaticWsRows (the dynamic
 // schedule splits at most that many rows), about 1.8 MB.
 constexpr int64_t kStaticWsRows = 256;
-constexpr int64_t kStaticWsBytes = ws_bytes(kStaticWsRows);
+constexpr int64_t kStaticWsBytes = ws_split_bytes(kStaticWsRows);
 static __device__ __align__(256) uint8_t g_static_ws[kStaticWsBytes];
 void* g_static_ws_ptr[kMaxDevices] = {};  // guarded by g_mutex
 

@@ -295,11 +295,14 @@ struct SelectParams {
     uint8_t* ws;               // workspace (layout above)
     int64_t ws_rows;           // its split-row capacity
     int64_t whole_rows;        // tickets [0, whole_rows) are rows 0.. handed out whole
-    int64_t tickets;           // then ceil((rows - whole_rows) * row_chunks / block) blocks of chunks
-    int32_t block;             // chunks per block of the split rows
+    int64_t tickets;           // then blocks of chunks over the split rows' chunks (row-major):
+    int64_t tier_tickets[2];   //   tier_tickets[i] blocks of tier_block[i] chunks (i = 0, 1), then
+    int32_t tier_block[2];     //   blocks of `block` chunks
+    int32_t block;
     uint32_t epoch;            // this launch's tag, never 0
     int32_t dynamic_always;    // host only: take the dynamic schedule for any batch size
-    int32_t publish_only;      // split pieces only publish (a separate merge kernel merges the rows)
+    int32_t flat;              // sampler: consumers store granule records to the workspace (flat schedule)
+    int32_t ws_flat;           // host only: the workspace has the flat-record area
     // mask table (nullable): row r's mask is row mask_rows[r] of `masks` ([mask_table_rows, W]);
     // an index outside [0, mask_table_rows) fails the row with status 8
     const int32_t* mask_rows;
@@ -418,6 +421,10 @@ struct alignas(16) Shared {
     WarpPartial part[2][kConsumerWarps];
     int32_t piece_c0[32];             // finalizer: first chunks of a split row's pieces, in order
     GatherSlot piece_part[32];        // finalizer: their partials
+    // Flat schedule: each consumer warp's last granule record and its destination (nullptr: none),
+    // stored one chunk later, after the next stage's release, so that no release waits for it.
+    uint4 flat_rec[kConsumerWarps];
+    uint4* flat_dst[kConsumerWarps];
     volatile int32_t abort;
 };
 
@@ -452,8 +459,16 @@ __host__ __device__ constexpr int64_t ws_pieces_offset(int64_t rows_cap) {
 __host__ __device__ constexpr int64_t ws_granules_offset(int64_t rows_cap) {
     return ws_pieces_offset(rows_cap) + static_cast<int64_t>(sizeof(WsPiece)) * kWsChunks * rows_cap;
 }
+// Flat schedule: one 16-byte record per (row, chunk, warp) granule, [rows_cap][kWsChunks][warp]:
+// (reference max, mass relative to it as fp32 bits, valid tokens, flags), stored by the consumer
+// warp that streamed the granule.  A separate area, so that no record can pass for a piece.
+__host__ __device__ constexpr int64_t ws_flat_offset(int64_t rows_cap) {
+    return (ws_granules_offset(rows_cap) + 8ll * kConsumerWarps * kWsChunks * rows_cap + 255) / 256 * 256;
+}
+// Workspace without the flat-record area (argmax-only callers).
+__host__ __device__ constexpr int64_t ws_split_bytes(int64_t rows_cap) { return ws_flat_offset(rows_cap); }
 __host__ __device__ constexpr int64_t ws_bytes(int64_t rows_cap) {
-    return ws_granules_offset(rows_cap) + 8ll * kConsumerWarps * kWsChunks * rows_cap;
+    return ws_flat_offset(rows_cap) + 16ll * kConsumerWarps * kWsChunks * rows_cap;
 }
 
 // Sampler-only shared memory after the control block.
@@ -769,9 +784,17 @@ __device__ int64_t sampler_owner_walk(const double* granules, int cstride, int w
             lsum += ((bits >> i) & 1u) ? w : 0.0f;
         }
     }
-    const double lsum_d = lsum;
+    double lsum_d = lsum;
+    // Every fp32 weight of the granule underflowed (tiny temperatures: its mass comes from weights
+    // below 2^-149 relative to M): the lane is located with the exact fp64 weights instead.
+    if (__ballot_sync(0xFFFFFFFFu, lsum > 0.0f) == 0u) {
+        lsum_d = 0.0;
+#pragma unroll 1
+        for (int i = 0; i < kFinPer; ++i)
+            if ((bits >> i) & 1u) lsum_d += exact_weight(walk[lane][i], M, temp, inv);
+    }
     const double lincl = warp_inclusive_scan(lsum_d, lane);
-    const bool positive = lsum > 0.0f;
+    const bool positive = lsum_d > 0.0;
     const uint32_t pos_mask = __ballot_sync(0xFFFFFFFFu, positive);
     const uint32_t cross_mask = __ballot_sync(0xFFFFFFFFu, !walk_fallback && positive && cutoff < gprefix + lincl);
     const bool lane_fallback = cross_mask == 0u;
@@ -810,6 +833,10 @@ __device__ __forceinline__ WsPiece* ws_piece(const SelectParams& p, int64_t t, i
 // Split row t's granule block, [warp][chunk] with kWsChunks chunks per warp.
 __device__ __forceinline__ double* ws_granules(const SelectParams& p, int64_t t) {
     return reinterpret_cast<double*>(p.ws + ws_granules_offset(p.ws_rows)) + t * kWsChunks * kConsumerWarps;
+}
+// Flat schedule: row t's granule records, [chunk][warp].
+__device__ __forceinline__ uint4* ws_flat_records(const SelectParams& p, int64_t t) {
+    return reinterpret_cast<uint4*>(p.ws + ws_flat_offset(p.ws_rows)) + t * kWsChunks * kConsumerWarps;
 }
 
 // ----------------------------------------------------------------- the kernel
@@ -930,9 +957,8 @@ __device__ void merge_split_row(const SelectParams& p, int64_t row, int64_t t, i
 
 // Finalizer (one warp) of a split unit: the piece's partial (argmax: key, first region holding
 // it, count, flags; sampler: max, count, flags, mass) and, for the sampler, its granules scaled
-// to the piece's max go to the workspace.  In the one-launch form the CTA whose piece completes
-// the row's chunk count merges the row (merge_split_row); with `publish_only` the merge kernel
-// does it after the launch.  Sampler: `granules` (shared memory) holds the piece's granules, lanes
+// to the piece's max go to the workspace; the CTA whose piece completes the row's chunk count
+// merges the row (merge_split_row).  Sampler: `granules` (shared memory) holds the piece's granules, lanes
 // w < 8 pass warp w's factor to the piece max; the buffer is then reused for the row's granules;
 // `uniform` is the row's uniform.
 template <typename T, bool kSample>
@@ -959,7 +985,6 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
     // Publish the piece and count its chunks in with one acquire-release add: the add that
     // reaches the row's total identifies the merging CTA, which then sees every piece.
     __syncwarp();
-    if (p.publish_only) return;
     unsigned long long before = 0;
     if (lane == 0) before = ptx::atom_add_acq_rel_gpu(ws_row_counter(p, t), static_cast<uint64_t>(nch));
     before = __shfl_sync(0xFFFFFFFFu, before, 0);
@@ -977,8 +1002,9 @@ __device__ void finish_split_piece(const SelectParams& p, const Unit& d, int row
 // rows; the dependent still waits for this grid's completion before touching memory.
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-template <typename T, bool kSample, bool kBulk, int kStages>
+template <typename T, bool kSample, bool kBulk, int kStages, bool kFlat = false>
 __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectParams p) {
+    static_assert(!kFlat || (kSample && kBulk), "the flat schedule is a sampler schedule of bulk-copied rows");
     using E = Elem<T>;
     using L = Layout<T>;
     constexpr int kVec = E::kVec;
@@ -1000,6 +1026,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     const uint32_t cid = ptx::cluster_id_x();
     const uint32_t nclusters = ptx::ncluster_x();
     const bool dynamic = p.ws != nullptr;  // tickets from the workspace (one-CTA clusters only)
+    constexpr bool flat = kFlat;  // granule records to the workspace (dynamic schedule, sampler)
 
     // Fixed schedule: a contiguous, remainder-balanced block of rows per cluster (neighbouring
     // rows, often of different mask densities, hence cost, land on the same cluster).
@@ -1025,6 +1052,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             ptx::mbar_init(ptx::smem_addr(&sh.unit_full[s]), 1);
             ptx::mbar_init(ptx::smem_addr(&sh.unit_empty[s]), kConsumerWarps);
         }
+        for (int w = 0; w < kConsumerWarps; ++w) sh.flat_dst[w] = nullptr;
         sh.abort = 0;
         ptx::fence_mbarrier_init();
     }
@@ -1103,22 +1131,32 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             if (!dynamic) {
                 for (int64_t row = row_begin; row < row_end && !stop; ++row) run(row, 0, nchunks, kUnitWhole);
             } else {
-                // Tickets: rows [0, whole_rows) whole, then blocks of `block` chunks over the
-                // remaining (split) rows' chunks in row-major order.
+                // Tickets: rows [0, whole_rows) whole, then blocks over the remaining (split)
+                // rows' chunks in row-major order, shrinking by tier (tier_tickets / tier_block,
+                // then `block`).
                 const int64_t split_chunks = (p.rows - p.whole_rows) * nchunks;
                 unsigned long long* tickets = &ws_header(p)->tickets;
                 for (bool first = true; !stop; first = false) {
                     // CTA b's first ticket is b; later ones come from the counter (one atomic per
                     // ticket, the counter starting every launch at 0).
-                    const int64_t tk = first ? static_cast<int64_t>(blockIdx.x)
-                                             : static_cast<int64_t>(gridDim.x) + static_cast<int64_t>(atomicAdd(tickets, 1ull));
+                    // The flat schedule takes every ticket from the counter, so that a CTA starting
+                    // late holds no block of its own.
+                    const int64_t tk = flat    ? static_cast<int64_t>(atomicAdd(tickets, 1ull))
+                                       : first ? static_cast<int64_t>(blockIdx.x)
+                                               : static_cast<int64_t>(gridDim.x) + static_cast<int64_t>(atomicAdd(tickets, 1ull));
                     if (tk >= p.tickets) break;
                     if (tk < p.whole_rows) {
                         run(tk, 0, nchunks, kUnitWhole);
                         continue;
                     }
-                    const int64_t g0 = (tk - p.whole_rows) * p.block;
-                    const int64_t g1 = (g0 + p.block) < split_chunks ? (g0 + p.block) : split_chunks;
+                    const int64_t sk = tk - p.whole_rows;
+                    const int64_t n0 = p.tier_tickets[0], n1 = p.tier_tickets[1];
+                    const int64_t b0 = p.tier_block[0], b1 = p.tier_block[1];
+                    const int64_t g0 = sk < n0        ? sk * b0
+                                       : sk < n0 + n1 ? n0 * b0 + (sk - n0) * b1
+                                                      : n0 * b0 + n1 * b1 + (sk - n0 - n1) * p.block;
+                    const int64_t len = sk < n0 ? b0 : sk < n0 + n1 ? b1 : p.block;
+                    const int64_t g1 = (g0 + len) < split_chunks ? (g0 + len) : split_chunks;
                     for (int64_t r = g0 / nchunks; r <= (g1 - 1) / nchunks; ++r) {
                         const int c0 = static_cast<int>(g0 > r * nchunks ? g0 - r * nchunks : 0);
                         const int c1 = static_cast<int>(g1 < (r + 1) * nchunks ? g1 - r * nchunks : nchunks);
@@ -1143,143 +1181,147 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     } else if (warp == kFinalizerWarp) {
         // ------------------------------------------------------------ finalizer warp
         launch_dependents();
-        for (uint32_t k = 0;; ++k) {
-            const uint32_t slot = k & 1u;
-            if (!wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort)) break;
-            const Unit d = sh.part_unit[slot];
-            if (d.kind == kUnitEnd) break;
-            const int64_t row = d.row;
-            const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
-                                  static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-            const int32_t* mrow =
-                p.masks + static_cast<size_t>(d.mask_row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
-            const int nch = d.c1 - d.c0;
-            const bool in = lane < kConsumerWarps;
-            const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u, 0.0, 0.0};
-            const uint32_t cnt = __reduce_add_sync(0xFFFFFFFFu, wp.count);
-            const uint32_t flags = __reduce_or_sync(0xFFFFFFFFu, wp.flags) | (sh.abort ? kFlagAbort : 0u) |
-                                   (d.mask_bad ? kFlagBadMaskRow : 0u);
-            const uint32_t ckey = __reduce_max_sync(0xFFFFFFFFu, wp.key);
+        if constexpr (kFlat) {
+            // Flat schedule: the rows are merged by the merge launch that follows this one.
+        } else {
+            for (uint32_t k = 0;; ++k) {
+                const uint32_t slot = k & 1u;
+                if (!wait_bounded(ptx::smem_addr(&sh.part_full[slot]), (k >> 1) & 1u, &sh.abort)) break;
+                const Unit d = sh.part_unit[slot];
+                if (d.kind == kUnitEnd) break;
+                const int64_t row = d.row;
+                const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                                      static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+                const int32_t* mrow =
+                    p.masks + static_cast<size_t>(d.mask_row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
+                const int nch = d.c1 - d.c0;
+                const bool in = lane < kConsumerWarps;
+                const WarpPartial wp = in ? sh.part[slot][lane] : WarpPartial{0u, 0xFFFFFFFFu, 0u, 0u, 0.0, 0.0};
+                const uint32_t cnt = __reduce_add_sync(0xFFFFFFFFu, wp.count);
+                const uint32_t flags = __reduce_or_sync(0xFFFFFFFFu, wp.flags) | (sh.abort ? kFlagAbort : 0u) |
+                                       (d.mask_bad ? kFlagBadMaskRow : 0u);
+                const uint32_t ckey = __reduce_max_sync(0xFFFFFFFFu, wp.key);
 
-            if constexpr (!kSample) {
-                // First (chunk, warp) region holding the segment maximum; its lowest valid token
-                // equal to the maximum is the segment's argmax.
-                const uint32_t region = (in && ckey != 0u && wp.key == ckey) ? (wp.chunk * kConsumerWarps + lane)
-                                                                              : 0xFFFFFFFFu;
-                const uint32_t rmin = __reduce_min_sync(0xFFFFFFFFu, region);
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
-                if (d.kind == kUnitSplit && p.partials == nullptr) {
-                    // The index is recovered by the row's merge, from the winning piece only.
-                    finish_split_piece<T, false>(p, d, nchunks, GatherSlot{ckey, rmin, cnt, flags, 0.0, 0.0}, 0.0,
-                                                 nullptr, 0.0, sh, ss, lrow, mrow, lane);
-                    continue;
-                }
-                uint32_t found = 0xFFFFFFFFu;
-                if (rmin != 0xFFFFFFFFu) {
-                    const float target = ordered_to_float(ckey);
-                    const int64_t r0 = seg_begin + static_cast<int64_t>(rmin / kConsumerWarps) * kTPC +
-                                       static_cast<int64_t>(rmin % kConsumerWarps) * kTPW;
-                    const int64_t my0 = r0 + lane * kFinPer;
-                    Slice<E, kFinPer> sl;
-                    load_slice<E, kFinPer>(lrow, mrow, my0, seg_end, sl);
-#pragma unroll
-                    for (int i = kFinPer - 1; i >= 0; --i)
-                        if (((sl.bits >> i) & 1u) && sl.value(i) == target) found = static_cast<uint32_t>(my0 + i);
-                }
-                uint32_t hi = ckey;
-                uint32_t lo = __reduce_min_sync(0xFFFFFFFFu, found);
-                lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - static_cast<uint32_t>(p.token_offset + lo);
-                uint32_t total = cnt, fl = flags;
-                if (p.partials != nullptr) {  // vocabulary shard: the row's partial is the output
-                    GatherSlot rec{hi, lo, total, fl, 0.0, 0.0};
-                    // An exchange step tags each partial with its epoch, so that a merge finding
-                    // another tag in a rank's slot (that rank's step had fewer rows) fails the row
-                    // instead of merging a partial left there by an earlier step.
-                    if (p.xranks > 0) rec.pad = __longlong_as_double(static_cast<long long>(p.xepoch));
-                    if (lane == 0) p.partials[row] = rec;
-                    // Peer-memory exchange: the same record in every other rank's area (NVLink
-                    // stores overlapping the streaming of the next rows).
-                    if (lane < p.xranks && lane != p.xrank && !sh.abort) p.xpeer[lane][row] = rec;
-                    continue;
-                }
-                if (csize > 1) {
-                    if (lane == 0)
-                        cluster_allgather(sh, slot, crank, csize, GatherSlot{hi, lo, total, fl, 0.0, 0.0}, (k >> 1) & 1u);
+                if constexpr (!kSample) {
+                    // First (chunk, warp) region holding the segment maximum; its lowest valid token
+                    // equal to the maximum is the segment's argmax.
+                    const uint32_t region = (in && ckey != 0u && wp.key == ckey) ? (wp.chunk * kConsumerWarps + lane)
+                                                                                  : 0xFFFFFFFFu;
+                    const uint32_t rmin = __reduce_min_sync(0xFFFFFFFFu, region);
                     __syncwarp();
-                    const bool inr = lane < static_cast<int>(csize);
-                    const GatherSlot g = inr ? sh.slots[slot][lane] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
-                    hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
-                    lo = __reduce_max_sync(0xFFFFFFFFu, (inr && g.a == hi) ? g.b : 0u);
-                    total = __reduce_add_sync(0xFFFFFFFFu, g.c);
-                    fl = __reduce_or_sync(0xFFFFFFFFu, g.d) | (sh.abort ? kFlagAbort : 0u);
-                }
-                if (crank == 0 && lane == 0) {
-                    const int32_t code = argmax_status(fl, total);
-                    p.status[row] = code;
-                    p.tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
-                    if (p.counts) p.counts[row] = total;
-                }
-            } else {
-                // Segment maximum and mass relative to it: the consumer warps already folded their
-                // granules to their own maxima; combine the 8 warp masses in warp order.
-                double* granules = ss.granules[slot];
-                const int ngran = nch * kConsumerWarps;
-                const float seg_m = ckey ? ordered_to_float(ckey) : -kInf;
-                const bool seg_finite = seg_m > -kInf && seg_m < kInf;
-                const float wmax = in ? ordered_to_float(wp.key) : -kInf;
-                const double wf = (seg_finite && in && wp.mass > 0.0)
-                                      ? warp_factor(wmax, seg_m, p.temperature, p.inv_temperature)
-                                      : 0.0;
-                const double term = wp.mass * wf;
-                const double seg_s = warp_sum8(term);  // read on lane 0
-                if (p.partials != nullptr) {
-                    // Vocabulary shard: the row's partial and granule record are the output.
-                    if (lane == 0) p.partials[row] = GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
-                    uint8_t* rec = p.granule_out + row * p.granule_stride;
-                    if (in) {
-                        reinterpret_cast<float*>(rec + SamplerRecord::kWarpMaxOffset)[lane] = wmax;
-                        reinterpret_cast<double*>(rec + SamplerRecord::kWarpMassOffset)[lane] = wp.mass;
+                    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
+                    if (d.kind == kUnitSplit && p.partials == nullptr) {
+                        // The index is recovered by the row's merge, from the winning piece only.
+                        finish_split_piece<T, false>(p, d, nchunks, GatherSlot{ckey, rmin, cnt, flags, 0.0, 0.0}, 0.0,
+                                                     nullptr, 0.0, sh, ss, lrow, mrow, lane);
+                        continue;
                     }
-                    double* rg = reinterpret_cast<double*>(rec + SamplerRecord::kGranuleOffset);
-                    // The record is chunk-major ([chunk][warp]); the table warp-major.
-                    for (int i = lane; i < ngran; i += 32) {
-                        const int w = i / nch, c = i - w * nch;
-                        rg[c * kConsumerWarps + w] = granules[w * kMaxChunksSampler + c];
+                    uint32_t found = 0xFFFFFFFFu;
+                    if (rmin != 0xFFFFFFFFu) {
+                        const float target = ordered_to_float(ckey);
+                        const int64_t r0 = seg_begin + static_cast<int64_t>(rmin / kConsumerWarps) * kTPC +
+                                           static_cast<int64_t>(rmin % kConsumerWarps) * kTPW;
+                        const int64_t my0 = r0 + lane * kFinPer;
+                        Slice<E, kFinPer> sl;
+                        load_slice<E, kFinPer>(lrow, mrow, my0, seg_end, sl);
+    #pragma unroll
+                        for (int i = kFinPer - 1; i >= 0; --i)
+                            if (((sl.bits >> i) & 1u) && sl.value(i) == target) found = static_cast<uint32_t>(my0 + i);
                     }
-                } else if (d.kind == kUnitSplit) {
-                    finish_split_piece<T, true>(p, d, nchunks, GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0},
-                                                wf, granules, sh.part_uniform[slot], sh, ss, lrow, mrow, lane);
+                    uint32_t hi = ckey;
+                    uint32_t lo = __reduce_min_sync(0xFFFFFFFFu, found);
+                    lo = lo == 0xFFFFFFFFu ? 0u : 0xFFFFFFFFu - static_cast<uint32_t>(p.token_offset + lo);
+                    uint32_t total = cnt, fl = flags;
+                    if (p.partials != nullptr) {  // vocabulary shard: the row's partial is the output
+                        GatherSlot rec{hi, lo, total, fl, 0.0, 0.0};
+                        // An exchange step tags each partial with its epoch, so that a merge finding
+                        // another tag in a rank's slot (that rank's step had fewer rows) fails the row
+                        // instead of merging a partial left there by an earlier step.
+                        if (p.xranks > 0) rec.pad = __longlong_as_double(static_cast<long long>(p.xepoch));
+                        if (lane == 0) p.partials[row] = rec;
+                        // Peer-memory exchange: the same record in every other rank's area (NVLink
+                        // stores overlapping the streaming of the next rows).
+                        if (lane < p.xranks && lane != p.xrank && !sh.abort) p.xpeer[lane][row] = rec;
+                        continue;
+                    }
+                    if (csize > 1) {
+                        if (lane == 0)
+                            cluster_allgather(sh, slot, crank, csize, GatherSlot{hi, lo, total, fl, 0.0, 0.0}, (k >> 1) & 1u);
+                        __syncwarp();
+                        const bool inr = lane < static_cast<int>(csize);
+                        const GatherSlot g = inr ? sh.slots[slot][lane] : GatherSlot{0u, 0u, 0u, 0u, 0.0, 0.0};
+                        hi = __reduce_max_sync(0xFFFFFFFFu, g.a);
+                        lo = __reduce_max_sync(0xFFFFFFFFu, (inr && g.a == hi) ? g.b : 0u);
+                        total = __reduce_add_sync(0xFFFFFFFFu, g.c);
+                        fl = __reduce_or_sync(0xFFFFFFFFu, g.d) | (sh.abort ? kFlagAbort : 0u);
+                    }
+                    if (crank == 0 && lane == 0) {
+                        const int32_t code = argmax_status(fl, total);
+                        p.status[row] = code;
+                        p.tokens[row] = code == kOk ? static_cast<int64_t>(0xFFFFFFFFu - lo) : -1;
+                        if (p.counts) p.counts[row] = total;
+                    }
                 } else {
-                    // Rank partials, all-gathered in rank order, merged identically on every rank.
-                    if (lane == 0) {
-                        const GatherSlot mine{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
-                        if (csize > 1) cluster_allgather(sh, slot, crank, csize, mine, (k >> 1) & 1u);
-                        else sh.slots[slot][0] = mine;
+                    // Segment maximum and mass relative to it: the consumer warps already folded their
+                    // granules to their own maxima; combine the 8 warp masses in warp order.
+                    double* granules = ss.granules[slot];
+                    const int ngran = nch * kConsumerWarps;
+                    const float seg_m = ckey ? ordered_to_float(ckey) : -kInf;
+                    const bool seg_finite = seg_m > -kInf && seg_m < kInf;
+                    const float wmax = in ? ordered_to_float(wp.key) : -kInf;
+                    const double wf = (seg_finite && in && wp.mass > 0.0)
+                                          ? warp_factor(wmax, seg_m, p.temperature, p.inv_temperature)
+                                          : 0.0;
+                    const double term = wp.mass * wf;
+                    const double seg_s = warp_sum8(term);  // read on lane 0
+                    if (p.partials != nullptr) {
+                        // Vocabulary shard: the row's partial and granule record are the output.
+                        if (lane == 0) p.partials[row] = GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
+                        uint8_t* rec = p.granule_out + row * p.granule_stride;
+                        if (in) {
+                            reinterpret_cast<float*>(rec + SamplerRecord::kWarpMaxOffset)[lane] = wmax;
+                            reinterpret_cast<double*>(rec + SamplerRecord::kWarpMassOffset)[lane] = wp.mass;
+                        }
+                        double* rg = reinterpret_cast<double*>(rec + SamplerRecord::kGranuleOffset);
+                        // The record is chunk-major ([chunk][warp]); the table warp-major.
+                        for (int i = lane; i < ngran; i += 32) {
+                            const int w = i / nch, c = i - w * nch;
+                            rg[c * kConsumerWarps + w] = granules[w * kMaxChunksSampler + c];
+                        }
+                    } else if (d.kind == kUnitSplit) {
+                        finish_split_piece<T, true>(p, d, nchunks, GatherSlot{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0},
+                                                    wf, granules, sh.part_uniform[slot], sh, ss, lrow, mrow, lane);
+                    } else {
+                        // Rank partials, all-gathered in rank order, merged identically on every rank.
+                        if (lane == 0) {
+                            const GatherSlot mine{__float_as_uint(seg_m), cnt, flags, 0u, seg_s, 0.0};
+                            if (csize > 1) cluster_allgather(sh, slot, crank, csize, mine, (k >> 1) & 1u);
+                            else sh.slots[slot][0] = mine;
+                        }
+                        __syncwarp();
+                        const SampleMerge mg = merge_sampler_ranks(sh.slots[slot], 1, csize, sh.part_uniform[slot], p.temperature,
+                                                                   p.inv_temperature, sh.abort ? kFlagAbort : 0u, lane);
+                        if (mg.code != kOk) {
+                            if (crank == 0 && lane == 0) {
+                                p.status[row] = mg.code;
+                                p.tokens[row] = -1;
+                                if (p.counts) p.counts[row] = mg.total;
+                            }
+                        } else if (mg.owner == static_cast<int>(crank)) {
+                            const int64_t chosen =
+                                sampler_owner_walk<T>(granules, 1, kMaxChunksSampler, ngran, wf, wp.mass, in, mg, p.temperature,
+                                                      p.inv_temperature, p.scale2, seg_begin, seg_end, lrow, mrow, ss.walk,
+                                                      ss.fac, lane);
+                            if (lane == 0) {
+                                p.status[row] = chosen >= 0 ? kOk : kNoMass;
+                                p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
+                                if (p.counts) p.counts[row] = mg.total;
+                            }
+                        }
                     }
                     __syncwarp();
-                    const SampleMerge mg = merge_sampler_ranks(sh.slots[slot], 1, csize, sh.part_uniform[slot], p.temperature,
-                                                               p.inv_temperature, sh.abort ? kFlagAbort : 0u, lane);
-                    if (mg.code != kOk) {
-                        if (crank == 0 && lane == 0) {
-                            p.status[row] = mg.code;
-                            p.tokens[row] = -1;
-                            if (p.counts) p.counts[row] = mg.total;
-                        }
-                    } else if (mg.owner == static_cast<int>(crank)) {
-                        const int64_t chosen =
-                            sampler_owner_walk<T>(granules, 1, kMaxChunksSampler, ngran, wf, wp.mass, in, mg, p.temperature,
-                                                  p.inv_temperature, p.scale2, seg_begin, seg_end, lrow, mrow, ss.walk,
-                                                  ss.fac, lane);
-                        if (lane == 0) {
-                            p.status[row] = chosen >= 0 ? kOk : kNoMass;
-                            p.tokens[row] = chosen >= 0 ? p.token_offset + chosen : -1;
-                            if (p.counts) p.counts[row] = mg.total;
-                        }
-                    }
+                    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
                 }
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.part_empty[slot]));
             }
         }
     } else {
@@ -1297,19 +1339,29 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             __syncwarp();
             if (got && lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.unit_empty[us]));
             const uint32_t slot = k & 1u;
-            // The finalizer has released this partial slot (and granule table).
-            if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
-            if (d.kind == kUnitEnd) {
-                if (lane == 0) {
-                    if (warp == 0) sh.part_unit[slot] = d;
-                    ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
+            if (flat) {
+                if (d.kind == kUnitEnd) {
+                    // The warp's last record (its stores complete before the grid does).
+                    if (lane == 0 && sh.flat_dst[warp] != nullptr) *sh.flat_dst[warp] = sh.flat_rec[warp];
+                    launch_dependents();
+                    break;
                 }
-                launch_dependents();
-                break;
+            } else {
+                // The finalizer has released this partial slot (and granule table).
+                if (k >= 2) wait_bounded(ptx::smem_addr(&sh.part_empty[slot]), ((k >> 1) - 1u) & 1u, &sh.abort);
+                if (d.kind == kUnitEnd) {
+                    if (lane == 0) {
+                        if (warp == 0) sh.part_unit[slot] = d;
+                        ptx::mbar_arrive(ptx::smem_addr(&sh.part_full[slot]));
+                    }
+                    launch_dependents();
+                    break;
+                }
             }
             // Sampler: the row's uniform is copied to the partial slot while the row streams (the
             // finalizer needs it right after the last chunk).
-            const bool fetch_uniform = kSample && warp == 0 && lane == 0 && p.uniforms != nullptr && p.partials == nullptr;
+            const bool fetch_uniform =
+                kSample && !flat && warp == 0 && lane == 0 && p.uniforms != nullptr && p.partials == nullptr;
             if (fetch_uniform) ptx::cp_async_8(ptx::smem_addr(&sh.part_uniform[slot]), p.uniforms + d.row);
             const int64_t row = d.row;
             const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
@@ -1317,8 +1369,11 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             const int32_t* mrow =
                 p.masks + static_cast<size_t>(d.mask_row) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
             const int nch = d.c1 - d.c0;
-            double* granules = ss.granules[slot];
+            double* granules = ss.granules[slot & 1u];
             float2* granules_f = reinterpret_cast<float2*>(granules);
+            // Flat schedule: this warp's granule records of the unit's row, and the flags they carry.
+            uint4* frec = flat ? ws_flat_records(p, row) + warp : nullptr;
+            const uint32_t unit_flags = d.mask_bad ? kFlagBadMaskRow : 0u;
             typename E::NanAcc nan_acc = E::nan_init();
             uint32_t count = 0;
             // argmax: lane's running masked max and the chunk it came from
@@ -1333,6 +1388,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
 
             auto chunk = [&](auto full_tag, int c) {
                 constexpr bool kFull = decltype(full_tag)::value;
+                [[maybe_unused]] const uint32_t count_in = count;  // flat schedule: the chunk's own count
                 uint8_t* st = stages + (kBulk ? stage : 0u) * L::kStageBytes;
                 const uint32_t* smask;
                 int ntok = kTPC;
@@ -1396,7 +1452,14 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                 // Stage contents are in registers: release it to the producer.
                 if constexpr (kBulk) {
                     __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&sh.empty[stage]));
+                    if (lane == 0) {
+                        ptx::mbar_arrive(ptx::smem_addr(&sh.empty[stage]));
+                        // Flat schedule: the previous chunk's record, stored after the release.
+                        if (flat && sh.flat_dst[warp] != nullptr) {
+                            *sh.flat_dst[warp] = sh.flat_rec[warp];
+                            sh.flat_dst[warp] = nullptr;
+                        }
+                    }
                 } else {
                     ptx::named_sync(1, kConsumerThreads);  // stage 0 reusable
                 }
@@ -1528,7 +1591,19 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
                         for (int o = 16; o >= 1; o >>= 1) mass += __shfl_xor_sync(0xFFFFFFFFu, mass, o);
                         if (fast) mass *= corr;
                     }
-                    if (lane == 0) granules_f[warp * kMaxChunksSampler + (c - d.c0)] = make_float2(ref, mass);
+                    if (flat) {
+                        // The granule's record for the workspace: (reference, mass, valid tokens,
+                        // flags); NaN is flagged from the first chunk of the unit that met it on.
+                        const uint32_t ccount = __reduce_add_sync(0xFFFFFFFFu, count - count_in);
+                        const uint32_t cflags = (__any_sync(0xFFFFFFFFu, E::has_nan(nan_acc)) ? kFlagNaN : 0u) | unit_flags |
+                                                (sh.abort ? kFlagAbort : 0u);
+                        if (lane == 0) {
+                            sh.flat_rec[warp] = make_uint4(__float_as_uint(ref), __float_as_uint(mass), ccount, cflags);
+                            sh.flat_dst[warp] = frec + c * kConsumerWarps;
+                        }
+                    } else if (lane == 0) {
+                        granules_f[warp * kMaxChunksSampler + (c - d.c0)] = make_float2(ref, mass);
+                    }
                 }
                 if constexpr (kBulk) {
                     if (++stage == static_cast<uint32_t>(kStages)) {
@@ -1541,6 +1616,7 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
             for (int c = d.c0; c < cfull; ++c) chunk(std::true_type{}, c);
             for (int c = d.c0 > nfull ? d.c0 : nfull; c < d.c1; ++c) chunk(std::false_type{}, c);
 
+            if (flat) continue;  // nothing to hand over: the records carry the unit
             // ---------------------------------------------------- warp partial -> finalizer
             const bool nan_local = E::has_nan(nan_acc);
             const uint32_t wcount = __reduce_add_sync(0xFFFFFFFFu, count);
@@ -1619,43 +1695,132 @@ __global__ void __launch_bounds__(kThreads, 3) select_rows_kernel(const SelectPa
     }
 }
 
-// Scratch of one merging warp of merge_pieces_kernel.
-struct MergeScratch {
-    double granules[kMaxChunksSampler * kConsumerWarps];  // the row's granules [warp][chunk] (sampler)
+constexpr int kFlatMergeWarps = 4;
+
+// Shared memory of one flat_merge_kernel CTA.
+struct FlatMergeShared {
+    uint4 table[kMaxChunksSampler * kConsumerWarps];  // the row's granule records, then fp64 masses
     float walk[32][33];
     double fac[kConsumerWarps];
-    int32_t piece_c0[32];
-    GatherSlot piece_part[32];
+    uint32_t red[kFlatMergeWarps][3];                 // per-warp max key, count, flags
+    double uniform;
 };
-constexpr int kMergeWarps = 4;
 
-// Second launch of the two-launch schedule of small batches: the selection launch streamed every
-// row as pieces (publish_only) and left their partials and granules in the workspace; one warp per
-// row merges them (merge_split_row) and writes the outputs.  Launched as a programmatic dependent
-// of the selection launch; lets its own dependents start at once (they wait for its completion).
-template <typename T, bool kSample>
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_pieces_kernel(const SelectParams p) {
-    __shared__ MergeScratch ms[kMergeWarps];
+// Second launch of the flat schedule: the selection launch left one record per (row, chunk, warp)
+// granule in the workspace -- (reference max, mass relative to it as fp32 bits, valid tokens,
+// flags), from whichever CTAs streamed the row.  One CTA per row (grid-stride) copies the records
+// into shared memory, reduces them to the row's status, valid count and largest reference M,
+// rescales every granule to an fp64 mass relative to M (one exp per granule whose reference is
+// below M, spread over the CTA's threads), and warp 0 walks the row as one rank's partial (the
+// cutoff taken on the same lane-ordered sums as the walk's scan).  Launched as a programmatic
+// dependent of the selection launch; lets its own dependents start at once (they wait for its
+// completion before touching memory).
+template <typename T>
+__global__ void __launch_bounds__(kFlatMergeWarps * 32) flat_merge_kernel(const SelectParams p) {
+    __shared__ FlatMergeShared ms;
     launch_dependents();
     asm volatile("griddepcontrol.wait;" ::: "memory");
     using E = Elem<T>;
     constexpr int kTPC = Layout<T>::kTokensPerChunk;
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    constexpr int kN = kFlatMergeWarps * 32;
+    const float kInf = __int_as_float(0x7F800000);
+    const int tid = threadIdx.x, lane = tid & 31, wib = tid >> 5;
     const int row_chunks = static_cast<int>((p.vocab + kTPC - 1) / kTPC);
-    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kMergeWarps;
-    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; row < p.rows; row += nwarps) {
-        const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
-                              static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
-        int64_t mr = row;
-        if (p.mask_rows != nullptr) {  // a bad index failed the row in the selection launch
-            mr = p.mask_rows[row];
-            if (mr < 0 || mr >= p.mask_table_rows) mr = 0;
+    const int ngran = row_chunks * kConsumerWarps;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        __syncthreads();  // the previous row's tables are no longer read
+        const uint4* src = ws_flat_records(p, row);
+        const uint32_t dst = ptx::smem_addr(ms.table);
+        for (int g = tid; g < ngran; g += kN) ptx::cp_async_16(dst + 16u * static_cast<uint32_t>(g), src + g);
+        if (tid == 0) ms.uniform = p.uniforms != nullptr ? p.uniforms[row] : 0.0;
+        ptx::cp_async_wait_all();
+        __syncthreads();
+        uint32_t mkey = 0u, cnt = 0u, fl = 0u;
+        for (int g = tid; g < ngran; g += kN) {
+            const uint4 r = ms.table[g];
+            mkey = max(mkey, ordered_bits(__uint_as_float(r.x)));
+            cnt += r.z;
+            fl |= r.w;
         }
-        const int32_t* mrow = p.masks + static_cast<size_t>(mr) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
-        const double u = (kSample && p.uniforms != nullptr) ? p.uniforms[row] : 0.0;
-        MergeScratch& m = ms[wib];
-        merge_split_row<T, kSample>(p, row, row - p.whole_rows, row_chunks, m.granules, u, 0u, m.piece_c0, m.piece_part,
-                                    m.walk, m.fac, lrow, mrow, lane, false);
+        mkey = __reduce_max_sync(0xFFFFFFFFu, mkey);
+        cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+        fl = __reduce_or_sync(0xFFFFFFFFu, fl);
+        if (lane == 0) {
+            ms.red[wib][0] = mkey;
+            ms.red[wib][1] = cnt;
+            ms.red[wib][2] = fl;
+        }
+        __syncthreads();
+        mkey = 0u;
+        cnt = 0u;
+        fl = 0u;
+#pragma unroll
+        for (int w = 0; w < kFlatMergeWarps; ++w) {
+            mkey = max(mkey, ms.red[w][0]);
+            cnt += ms.red[w][1];
+            fl |= ms.red[w][2];
+        }
+        const float M = ordered_to_float(mkey);
+        const double u = ms.uniform;
+        SampleMerge mg;
+        mg.total = cnt;
+        mg.code = (fl & kFlagAbort) ? kTimeout
+                  : (fl & kFlagBadMaskRow) ? kBadMaskRow
+                  : (fl & kFlagNaN) ? kNaN
+                  : (M == kInf) ? kPosInf
+                  : (cnt == 0u) ? kEmpty
+                  : (M == -kInf) ? kNoMass
+                  : !(u >= 0.0 && u < 1.0) ? kBadUniform
+                                           : kOk;
+        mg.M = M;
+        mg.owner = 0;
+        mg.fallback = false;
+        mg.cutoff = 0.0;
+        mg.prefix = 0.0;
+        mg.rank_fac = 1.0;
+        // Granule g's fp64 mass relative to M replaces the first 8 bytes of its record.
+        double* gm = reinterpret_cast<double*>(ms.table);
+        if (mg.code == kOk) {
+            for (int g = tid; g < ngran; g += kN) {
+                const uint4 r = ms.table[g];
+                const float ref = __uint_as_float(r.x), mass = __uint_as_float(r.y);
+                gm[2 * g] = !(mass > 0.0f) ? 0.0
+                            : ref == M     ? static_cast<double>(mass)
+                                           : static_cast<double>(mass) *
+                                                 scaled_exp(static_cast<double>(ref) - static_cast<double>(M), p.temperature,
+                                                            p.inv_temperature);
+            }
+        }
+        __syncthreads();
+        if (wib != 0) continue;
+        int64_t chosen = -1;
+        if (mg.code == kOk) {
+            const int per = (ngran + 31) / 32;
+            const int g0 = lane * per, g1 = min(g0 + per, ngran);
+            double local = 0.0;
+            for (int g = g0; g < g1; ++g) local += gm[2 * g];
+            const double total = __shfl_sync(0xFFFFFFFFu, warp_inclusive_scan(local, lane), 31);
+            mg.cutoff = u * total;
+            mg.fallback = !(mg.cutoff < total);
+            if (total > 0.0) {
+                int64_t mr = row;
+                if (p.mask_rows != nullptr) {  // a bad index is flagged in the row's records
+                    mr = p.mask_rows[row];
+                    if (mr < 0 || mr >= p.mask_table_rows) mr = 0;
+                }
+                const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
+                                      static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
+                const int32_t* mrow = p.masks + static_cast<size_t>(mr) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
+                chosen = sampler_owner_walk<T>(gm, 2 * kConsumerWarps, 2, ngran, 1.0, 1.0, lane < kConsumerWarps, mg,
+                                               p.temperature, p.inv_temperature, p.scale2, 0, p.vocab, lrow, mrow, ms.walk,
+                                               ms.fac, lane);
+            }
+        }
+        if (lane == 0) {
+            p.status[row] = mg.code != kOk ? mg.code : chosen >= 0 ? kOk : kNoMass;
+            p.tokens[row] = mg.code == kOk && chosen >= 0 ? p.token_offset + chosen : -1;
+            if (p.counts) p.counts[row] = cnt;
+        }
     }
 }
 

@@ -89,13 +89,15 @@ BMS_API int bms_mask_count(const int32_t *mask, int64_t vocab, int64_t *count, i
 BMS_API int bms_masked_argmax(const void *logits, int32_t dtype, const int32_t *mask, int64_t vocab,
                       int64_t *token, int32_t *status, int32_t device, void *stream);
 
-/* Workspace of the batched entry points' dynamic schedule (no reference counterpart): bytes for
- * `device` (-1 if invalid).  A workspace is device memory of at least this size, 256-byte aligned,
- * zeroed once before its first use; every call leaves it ready for the next.  Calls that may run
- * concurrently (different streams) need different workspaces.  With a workspace, rows of at most
- * 64 chunks (8,192 tokens per chunk for 16-bit logits, 4,096 for float32) are handed to CTAs
- * dynamically and the last rows are split across CTAs; without one (NULL), each group of CTAs
- * owns a fixed block of rows. */
+/* Workspace of the batched entry points' dynamic and flat schedules (no reference counterpart):
+ * bytes for `device` (-1 if invalid; about 11 MB on a 148-SM B200).  A workspace is device memory
+ * of at least this size, 256-byte aligned, zeroed once before its first use; every call leaves it
+ * ready for the next.  Calls that may run concurrently (different streams) need different
+ * workspaces.  With a workspace, rows of at most 64 chunks (8,192 tokens per chunk for 16-bit
+ * logits, 4,096 for float32) are handed to CTAs dynamically and the last rows are split across
+ * CTAs; small sampler batches (fewer than 1.5 rows per resident CTA) stream as chunk blocks taken
+ * by every CTA, followed by a second launch that merges each row.  Without a workspace (NULL),
+ * each group of CTAs owns a fixed block of rows. */
 BMS_API int64_t bms_workspace_bytes(int32_t device);
 
 /* Replaces csrc/argmax.cu:127-137 masked_reduce_batch_cuda: per row of a
@@ -286,7 +288,8 @@ BMS_API int bms_shard_merge_exchange(void *const *areas, int32_t ranks, int32_t 
 /* Test hook: force the cluster size (1, 2, 4, 8 or 16) and the number of
  * clusters of the selection kernels' fixed schedule; 0 restores the automatic
  * choice.  With cluster 0 and a workspace, `clusters` caps the number of CTAs of
- * the dynamic schedule.  Process-wide; not for concurrent use with other calls. */
+ * the dynamic schedule.  Any override turns the flat sampler schedule off.
+ * Process-wide; not for concurrent use with other calls. */
 BMS_API int bms_set_launch_override(int32_t cluster, int32_t clusters);
 
 #ifdef __cplusplus

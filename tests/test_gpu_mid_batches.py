@@ -1,9 +1,9 @@
 """Mid-sized batches (one row per SM up to 1.5 rows per resident CTA) on every schedule they can
 take: the fixed one (no workspace), and with a workspace either the fixed one or -- for the sampler
-with more rows than resident CTAs -- the two-launch schedule (every row streamed as pieces taken as
-tickets, then a merge launch per row).  Results must equal the oracle (argmax, counts, statuses
-bit-exact; sampled tokens within the 1e-6 CDF-boundary rule) across dtypes, vocabularies
-(bulk-copy and plain-load rows, 16-bit and fp32 chunking), failing rows and mask tables."""
+-- the flat schedule (the batch's chunks streamed as blocks taken as tickets by every CTA, then a
+merge launch per row).  Results must equal the oracle (argmax, counts, statuses bit-exact; sampled
+tokens within the 1e-6 CDF-boundary rule) across dtypes, vocabularies (bulk-copy and plain-load
+rows, 16-bit and fp32 chunking), failing rows and mask tables."""
 
 import numpy as np
 import pytest
