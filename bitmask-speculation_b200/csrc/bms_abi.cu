@@ -499,13 +499,86 @@ __global__ void __launch_bounds__(256) expand_lists_kernel(const int32_t* __rest
     }
 }
 
-// Byte-coded gap streams to packed mask rows, one CTA per row (grid-stride).  Row l's stream is
+// Gap-stream expansion (bms_expand_token_gaps): row l of `out` ([rows, ceil(vocab / 32)] words)
+// becomes the packed mask of the token IDs coded by the byte stream
 // bytes[offsets[l], offsets[l + 1]) (clamped to [0, n_bytes]); starting before token 0, a byte b > 0
 // advances b tokens and allows the token reached, a byte 0 advances 255 tokens and allows nothing.
-// Each thread decodes one contiguous segment of the stream: segment advances are summed, a block
-// scan gives every segment's starting token, then each segment sets its bits (atomicOr after the
-// row is cleared).  Tokens at or past `vocab` set nothing and flag the row in `bad` (nullable).
-__global__ void __launch_bounds__(256) expand_gaps_kernel(const uint8_t* __restrict__ bytes, int64_t n_bytes,
+// Tokens at or past `vocab` set nothing and flag the row in `bad` (nullable).
+//
+// One CTA per row builds the row's bitmap in shared memory: the stream is read in tiles of 4,096
+// bytes (thread t takes bytes [16t, 16t + 16) of a tile, so that every warp load covers 512
+// contiguous bytes), a block scan of the threads' summed advances gives each thread its starting
+// token, and the bits go in with shared-memory atomicOr; the finished row is written out with
+// coalesced word stores.  Rows whose bitmap does not fit kGapSmemBytes use expand_gaps_atomic_kernel.
+constexpr int kGapThreads = 256;
+constexpr int kGapTile = 16 * kGapThreads;
+constexpr int64_t kGapSmemBytes = 160 * 1024;
+
+__global__ void __launch_bounds__(kGapThreads) expand_gaps_kernel(const uint8_t* __restrict__ bytes, int64_t n_bytes,
+                                                                  const int32_t* __restrict__ offsets, int64_t rows,
+                                                                  int64_t vocab, int32_t* __restrict__ out,
+                                                                  int32_t* __restrict__ bad) {
+    extern __shared__ uint32_t sbits[];
+    __shared__ long long warp_sums[kGapThreads / 32];
+    const int64_t words = (vocab + 31) / 32;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    for (int64_t l = blockIdx.x; l < rows; l += gridDim.x) {
+        for (int64_t w = tid; w < words; w += kGapThreads) sbits[w] = 0u;
+        int64_t b = offsets[l], e = offsets[l + 1];
+        b = b < 0 ? 0 : b > n_bytes ? n_bytes : b;
+        e = e < b ? b : e > n_bytes ? n_bytes : e;
+        __syncthreads();  // the cleared bitmap before any bit is set
+        long long base = -1;  // token reached before the tile
+        int flag = 0;
+        for (int64_t t0 = b; t0 < e; t0 += kGapTile) {
+            const int64_t s0 = t0 + 16 * static_cast<int64_t>(tid);
+            uint32_t c[16];
+            long long local = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const bool in = s0 + j < e;
+                c[j] = in ? static_cast<uint32_t>(bytes[s0 + j]) : 1u;
+                local += in ? (c[j] ? c[j] : 255u) : 0u;
+            }
+            long long v = local;  // block inclusive scan: warps, then the warp totals
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const long long n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                if (lane >= o) v += n;
+            }
+            if (lane == 31) warp_sums[wid] = v;
+            __syncthreads();
+            long long pos = base + v - local, total = 0;
+#pragma unroll
+            for (int w = 0; w < kGapThreads / 32; ++w) {
+                const long long ws = warp_sums[w];
+                if (w < wid) pos += ws;
+                total += ws;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                if (s0 + j >= e) break;
+                pos += c[j] ? c[j] : 255u;
+                if (c[j]) {
+                    if (pos < vocab) atomicOr(&sbits[pos >> 5], 1u << (pos & 31));
+                    else flag = 1;
+                }
+            }
+            base += total;
+            __syncthreads();  // every thread read warp_sums before the next tile writes it
+        }
+        flag = __syncthreads_or(flag);  // also: every bit is set
+        int32_t* row = out + l * words;
+        for (int64_t w = tid; w < words; w += kGapThreads) row[w] = static_cast<int32_t>(sbits[w]);
+        if (bad != nullptr && tid == 0) bad[l] = flag;
+        __syncthreads();  // the bitmap is read out before the next row clears it
+    }
+}
+
+// The same expansion for bitmaps larger than kGapSmemBytes: each thread decodes one contiguous
+// segment of the stream, a block scan of the segment advances gives every segment's starting
+// token, and the bits go into the cleared row with global atomicOr.
+__global__ void __launch_bounds__(256) expand_gaps_atomic_kernel(const uint8_t* __restrict__ bytes, int64_t n_bytes,
                                                           const int32_t* __restrict__ offsets, int64_t rows,
                                                           int64_t vocab, int32_t* __restrict__ out,
                                                           int32_t* __restrict__ bad) {
@@ -1369,7 +1442,18 @@ int bms_expand_token_gaps(const uint8_t* bytes, int64_t n_bytes, const int32_t* 
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
     const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
     const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
-    expand_gaps_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(bytes, n_bytes, offsets, rows, vocab, out, bad);
+    const int64_t smem = (vocab + 31) / 32 * 4;
+    if (smem <= kGapSmemBytes) {
+        if (smem > 48 * 1024)
+            BMS_CUDA(cudaFuncSetAttribute(expand_gaps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(kGapSmemBytes)),
+                     "cudaFuncSetAttribute(gap expansion smem)");
+        expand_gaps_kernel<<<grid, kGapThreads, static_cast<size_t>(smem), static_cast<cudaStream_t>(stream)>>>(
+            bytes, n_bytes, offsets, rows, vocab, out, bad);
+    } else {
+        expand_gaps_atomic_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(bytes, n_bytes, offsets, rows,
+                                                                                         vocab, out, bad);
+    }
     BMS_CUDA(cudaGetLastError(), "gap-stream expansion launch");
     return BMS_SUCCESS;
 }

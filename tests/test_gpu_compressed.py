@@ -68,8 +68,10 @@ def _expand_gaps(stream: np.ndarray, offsets, vocab):
     return out.cpu().numpy(), bad.cpu().numpy()
 
 
-@pytest.mark.parametrize("vocab", [248320, 50257, 700])
+@pytest.mark.parametrize("vocab", [248320, 50257, 700, 1_300_000, 1_400_000])
 def test_gap_expansion_sets_exactly_the_coded_tokens(cuda_module, vocab):
+    """Shared-memory row bitmaps (up to 160 KB: 1,300,000 tokens takes more than the default 48 KB)
+    and, past that, the global-atomic expansion (1,400,000 tokens)."""
     rng = np.random.default_rng(vocab + 1)
     sets = [np.flatnonzero(rng.random(vocab) < d) for d in (0.0, 0.0005, 0.004, 0.05, 0.12, 0.5)]
     sets.append(np.array([254, 509, 764, vocab - 1]) if vocab > 800 else np.array([254, 509, vocab - 1]))
