@@ -274,15 +274,13 @@ bool launch_dynamic(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t&
 // Consumer warps store one record per (chunk, warp) granule to the workspace and hand nothing over
 // at a piece boundary; a second launch (flat_merge_kernel) merges and walks every row in parallel.
 //
-// Measured on B200 (configuration-2 rows, fp16, 31 chunks per row, CUDA events, back to back):
-// 16 / 32 / 48 / 74 / 100 / 120 rows 16.4 / 18.7 / 20.3 / 22.4 / 25.3 / 27.5 us against 18.7 /
-// 24.9 / 28.5 / 28.7 / 28.9 / 29.1 us on the fixed schedule; 200 rows 36.2 against 38.9; 480 /
-// 560 / 665 rows 61.8 / 69.1 / 78.3 against 63.9 / 73.0 / 82.6 on the former two-launch split
-// schedule.  Batches that fill the SMs' row slots evenly stream faster on the fixed schedule
-// (148 / 256 / 444 rows 29.3 / 39.2 / 50.6 us against 30.7 / 41.6 / 58.6 us): up to one row per
-// resident CTA the flat schedule runs only where its cost, about 14.8 us + 0.47 us x chunks / SMs,
-// undercuts the fixed schedule's, about 18.6 us + 0.34 us x chunks per row x ceil(rows / SMs), by
-// more than 1.5 us.
+// Measured on B200 (configuration-2 rows, fp16, 31 chunks per row, CUDA events, back to back),
+// flat against the fixed schedule: 8 / 64 / 148 / 200 / 256 / 300 rows 12.8 / 19.1 / 28.2 / 33.3 /
+// 39.0 / 42.5 us against 15.9 / 28.7 / 29.5 / 38.9 / 39.2 / 50.1 us; 480 / 600 rows 58.6 / 69.2 us
+// against 64.5 / 76.4 us on a two-launch split schedule.  A batch of one row per resident CTA
+// streams faster on the fixed schedule (444 rows: 50.9 against 55.9 us): up to one row per
+// resident CTA the flat schedule runs where its cost, about 13.2 us + 0.47 us x chunks / SMs, is
+// below the fixed schedule's, about 18.6 us + 0.34 us x chunks per row x ceil(rows / SMs).
 constexpr int64_t kFlatTierPct[2] = {60, 20};
 constexpr int64_t kFlatSmallBlock = 2;
 
@@ -297,9 +295,9 @@ bool launch_flat(SelectParams& p, const KernelInfo& info, cudaLaunchConfig_t& cf
     const int64_t chunks = p.rows * n;
     const int64_t sms = info.sms;
     if (p.rows <= grid && 2 * p.rows >= sms) {
-        const double flat_us = 14.8 + 0.47 * static_cast<double>(chunks) / static_cast<double>(sms);
+        const double flat_us = 13.2 + 0.47 * static_cast<double>(chunks) / static_cast<double>(sms);
         const double fixed_us = 18.6 + 0.34 * static_cast<double>(n) * static_cast<double>((p.rows + sms - 1) / sms);
-        if (fixed_us <= flat_us + 1.5) return false;
+        if (fixed_us <= flat_us) return false;
     }
     const int64_t small = chunks <= grid ? 1 : kFlatSmallBlock;
     int64_t rem = chunks, tickets = 0;

@@ -705,6 +705,11 @@ __device__ __forceinline__ double warp_factor(float wmax, float seg_m, double te
     return wmax == seg_m ? 1.0 : scaled_exp(static_cast<double>(wmax) - static_cast<double>(seg_m), temp, inv);
 }
 
+template <typename T>
+__device__ int64_t walk_granule(int gsel, double gprefix, bool walk_fallback, double M, double cutoff, double temp,
+                                double inv, float scale2, int64_t seg_begin, int64_t seg_end, const uint8_t* lrow,
+                                const int32_t* mrow, float (*walk)[33], int lane);
+
 // The owning rank's walk (one warp): find the granule holding the crossing from the granule
 // masses (each relative to its warp's reference max; `fac` = warp factor x rank factor rescales
 // them to the row max), then the lane of that granule with fp32 weights, then the token with the
@@ -719,10 +724,6 @@ __device__ int64_t sampler_owner_walk(const double* granules, int cstride, int w
                                       const SampleMerge& mg, double temp, double inv, float scale2, int64_t seg_begin,
                                       int64_t seg_end, const uint8_t* lrow, const int32_t* mrow, float (*walk)[33],
                                       double* fac, int lane) {
-    using E = Elem<T>;
-    constexpr int kTPC = Layout<T>::kTokensPerChunk;
-    constexpr int kTPW = Layout<T>::kTokensPerWarp;
-    constexpr int kFinPer = kTPW / 32;
     const double M = mg.M, cutoff = mg.cutoff, prefix = mg.prefix;
     const bool fallback = mg.fallback;
     if (has_warp) fac[lane] = wmass > 0.0 ? wfac * mg.rank_fac : 0.0;
@@ -759,6 +760,23 @@ __device__ int64_t sampler_owner_walk(const double* granules, int cstride, int w
         gprefix = __shfl_sync(0xFFFFFFFFu, cand_prefix, owner_lane);
     }
     if (gsel < 0) return -1;
+    return walk_granule<T>(gsel, gprefix, walk_fallback, M, cutoff, temp, inv, scale2, seg_begin, seg_end, lrow, mrow,
+                           walk, lane);
+}
+
+// The walk of one granule (one warp): granule `gsel` (chunk gsel / 8, warp gsel % 8 of the segment
+// starting at token seg_begin) holds the crossing of `cutoff`, the masses before it summing to
+// `gprefix` (relative to M); `fallback` asks for its last positive weight instead.  The lane of the
+// crossing is found with fp32 weights (fp64 when every fp32 weight underflows), the token with the
+// reference's exact fp64 weights.  Returns the token's index within the row (-1 if none).
+template <typename T>
+__device__ int64_t walk_granule(int gsel, double gprefix, bool walk_fallback, double M, double cutoff, double temp,
+                                double inv, float scale2, int64_t seg_begin, int64_t seg_end, const uint8_t* lrow,
+                                const int32_t* mrow, float (*walk)[33], int lane) {
+    using E = Elem<T>;
+    constexpr int kTPC = Layout<T>::kTokensPerChunk;
+    constexpr int kTPW = Layout<T>::kTokensPerWarp;
+    constexpr int kFinPer = kTPW / 32;
     const int gc = gsel / kConsumerWarps, gw = gsel % kConsumerWarps;
     const int64_t gt0 = seg_begin + static_cast<int64_t>(gc) * kTPC + gw * kTPW;
     const int64_t gt1 = min(gt0 + kTPW, seg_end);
@@ -1699,22 +1717,24 @@ constexpr int kFlatMergeWarps = 4;
 
 // Shared memory of one flat_merge_kernel CTA.
 struct FlatMergeShared {
-    uint4 table[kMaxChunksSampler * kConsumerWarps];  // the row's granule records, then fp64 masses
+    uint4 table[kMaxChunksSampler * kConsumerWarps];  // the row's granule records
     float walk[32][33];
-    double fac[kConsumerWarps];
     uint32_t red[kFlatMergeWarps][3];                 // per-warp max key, count, flags
+    double wsum[kFlatMergeWarps];                     // per-warp mass sums (block scan)
+    double wprefix[kFlatMergeWarps];                  // per-warp first crossing: masses before it
+    int32_t wcand[kFlatMergeWarps];                   //   and its granule (0x7FFFFFFF: none)
+    int32_t wlast[kFlatMergeWarps];                   // per-warp last positive granule
     double uniform;
 };
 
 // Second launch of the flat schedule: the selection launch left one record per (row, chunk, warp)
 // granule in the workspace -- (reference max, mass relative to it as fp32 bits, valid tokens,
 // flags), from whichever CTAs streamed the row.  One CTA per row (grid-stride) copies the records
-// into shared memory, reduces them to the row's status, valid count and largest reference M,
-// rescales every granule to an fp64 mass relative to M (one exp per granule whose reference is
-// below M, spread over the CTA's threads), and warp 0 walks the row as one rank's partial (the
-// cutoff taken on the same lane-ordered sums as the walk's scan).  Launched as a programmatic
-// dependent of the selection launch; lets its own dependents start at once (they wait for its
-// completion before touching memory).
+// into shared memory and reduces them to the row's status, valid count and largest reference M;
+// each thread rescales its granules to fp64 masses relative to M (one exp per granule whose
+// reference is below M), a block scan in granule order locates the granule holding u * total, and
+// warp 0 walks it (walk_granule).  Launched as a programmatic dependent of the selection launch;
+// lets its own dependents start at once (they wait for its completion before touching memory).
 template <typename T>
 __global__ void __launch_bounds__(kFlatMergeWarps * 32) flat_merge_kernel(const SelectParams p) {
     __shared__ FlatMergeShared ms;
@@ -1762,47 +1782,87 @@ __global__ void __launch_bounds__(kFlatMergeWarps * 32) flat_merge_kernel(const 
         }
         const float M = ordered_to_float(mkey);
         const double u = ms.uniform;
-        SampleMerge mg;
-        mg.total = cnt;
-        mg.code = (fl & kFlagAbort) ? kTimeout
-                  : (fl & kFlagBadMaskRow) ? kBadMaskRow
-                  : (fl & kFlagNaN) ? kNaN
-                  : (M == kInf) ? kPosInf
-                  : (cnt == 0u) ? kEmpty
-                  : (M == -kInf) ? kNoMass
-                  : !(u >= 0.0 && u < 1.0) ? kBadUniform
-                                           : kOk;
-        mg.M = M;
-        mg.owner = 0;
-        mg.fallback = false;
-        mg.cutoff = 0.0;
-        mg.prefix = 0.0;
-        mg.rank_fac = 1.0;
-        // Granule g's fp64 mass relative to M replaces the first 8 bytes of its record.
-        double* gm = reinterpret_cast<double*>(ms.table);
-        if (mg.code == kOk) {
-            for (int g = tid; g < ngran; g += kN) {
+        const int32_t code = (fl & kFlagAbort) ? kTimeout
+                             : (fl & kFlagBadMaskRow) ? kBadMaskRow
+                             : (fl & kFlagNaN) ? kNaN
+                             : (M == kInf) ? kPosInf
+                             : (cnt == 0u) ? kEmpty
+                             : (M == -kInf) ? kNoMass
+                             : !(u >= 0.0 && u < 1.0) ? kBadUniform
+                                                      : kOk;
+        // Thread t owns granules [t * per, (t + 1) * per): their fp64 masses relative to M (one exp
+        // per granule whose reference is below M), a block scan of the owners' sums in granule
+        // order, and the first granule whose running mass passes u * total (or, after rounding,
+        // the last positive one) with the masses before it.
+        const int per = (ngran + kN - 1) / kN;  // <= 4
+        const int g0 = tid * per;
+        double m[4] = {0.0, 0.0, 0.0, 0.0};
+        double local = 0.0;
+        if (code == kOk) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int g = g0 + i;
+                if (i >= per || g >= ngran) break;
                 const uint4 r = ms.table[g];
                 const float ref = __uint_as_float(r.x), mass = __uint_as_float(r.y);
-                gm[2 * g] = !(mass > 0.0f) ? 0.0
-                            : ref == M     ? static_cast<double>(mass)
-                                           : static_cast<double>(mass) *
-                                                 scaled_exp(static_cast<double>(ref) - static_cast<double>(M), p.temperature,
-                                                            p.inv_temperature);
+                m[i] = !(mass > 0.0f) ? 0.0
+                       : ref == M     ? static_cast<double>(mass)
+                                      : static_cast<double>(mass) *
+                                            scaled_exp(static_cast<double>(ref) - static_cast<double>(M), p.temperature,
+                                                       p.inv_temperature);
+                local += m[i];
             }
+        }
+        const double incl = warp_inclusive_scan(local, lane);
+        if (lane == 31) ms.wsum[wib] = incl;
+        __syncthreads();
+        double before = incl - local, total = 0.0;
+#pragma unroll
+        for (int w = 0; w < kFlatMergeWarps; ++w) {
+            if (w < wib) before += ms.wsum[w];
+            total += ms.wsum[w];
+        }
+        const double cutoff = u * total;
+        const bool fallback = !(cutoff < total);
+        int cand = 0x7FFFFFFF, lastg = -1;
+        double cand_prefix = 0.0, acc = before;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (!(m[i] > 0.0)) continue;
+            lastg = g0 + i;
+            if (!fallback && cand == 0x7FFFFFFF && cutoff < acc + m[i]) {
+                cand = g0 + i;
+                cand_prefix = acc;
+            }
+            acc += m[i];
+        }
+        const int wc = __reduce_min_sync(0xFFFFFFFFu, cand);
+        const int wl = __reduce_max_sync(0xFFFFFFFFu, lastg);
+        if (cand == wc && wc != 0x7FFFFFFF) ms.wprefix[wib] = cand_prefix;  // one owner per warp
+        if (lane == 0) {
+            ms.wcand[wib] = wc;
+            ms.wlast[wib] = wl;
         }
         __syncthreads();
         if (wib != 0) continue;
         int64_t chosen = -1;
-        if (mg.code == kOk) {
-            const int per = (ngran + 31) / 32;
-            const int g0 = lane * per, g1 = min(g0 + per, ngran);
-            double local = 0.0;
-            for (int g = g0; g < g1; ++g) local += gm[2 * g];
-            const double total = __shfl_sync(0xFFFFFFFFu, warp_inclusive_scan(local, lane), 31);
-            mg.cutoff = u * total;
-            mg.fallback = !(mg.cutoff < total);
-            if (total > 0.0) {
+        if (code == kOk && total > 0.0) {
+            int gsel = 0x7FFFFFFF, glast = -1;
+            double gprefix = 0.0;
+#pragma unroll
+            for (int w = 0; w < kFlatMergeWarps; ++w) {
+                if (ms.wcand[w] < gsel) {
+                    gsel = ms.wcand[w];
+                    gprefix = ms.wprefix[w];
+                }
+                glast = max(glast, ms.wlast[w]);
+            }
+            const bool walk_fallback = gsel == 0x7FFFFFFF;
+            if (walk_fallback) {
+                gsel = glast;
+                gprefix = 0.0;
+            }
+            if (gsel >= 0) {
                 int64_t mr = row;
                 if (p.mask_rows != nullptr) {  // a bad index is flagged in the row's records
                     mr = p.mask_rows[row];
@@ -1811,14 +1871,13 @@ __global__ void __launch_bounds__(kFlatMergeWarps * 32) flat_merge_kernel(const 
                 const uint8_t* lrow = static_cast<const uint8_t*>(p.logits) +
                                       static_cast<size_t>(row) * static_cast<size_t>(p.logit_stride) * E::kBytes;
                 const int32_t* mrow = p.masks + static_cast<size_t>(mr) * static_cast<size_t>(p.mask_stride) + p.mask_word_offset;
-                chosen = sampler_owner_walk<T>(gm, 2 * kConsumerWarps, 2, ngran, 1.0, 1.0, lane < kConsumerWarps, mg,
-                                               p.temperature, p.inv_temperature, p.scale2, 0, p.vocab, lrow, mrow, ms.walk,
-                                               ms.fac, lane);
+                chosen = walk_granule<T>(gsel, gprefix, walk_fallback, static_cast<double>(M), cutoff, p.temperature,
+                                         p.inv_temperature, p.scale2, 0, p.vocab, lrow, mrow, ms.walk, lane);
             }
         }
         if (lane == 0) {
-            p.status[row] = mg.code != kOk ? mg.code : chosen >= 0 ? kOk : kNoMass;
-            p.tokens[row] = mg.code == kOk && chosen >= 0 ? p.token_offset + chosen : -1;
+            p.status[row] = code != kOk ? code : chosen >= 0 ? kOk : kNoMass;
+            p.tokens[row] = code == kOk && chosen >= 0 ? p.token_offset + chosen : -1;
             if (p.counts) p.counts[row] = cnt;
         }
     }
