@@ -36,6 +36,10 @@
 //    the finalizer merges ranks in fixed order in fp64, then re-reads only the
 //    granule that holds u * total and walks it with exact fp64 weights
 //    exp((x - M) / T).
+//  * With a caller workspace the work can also arrive as tickets: whole rows
+//    and split pieces merged through the workspace (dynamic schedule), or, for
+//    small sampler batches, blocks of chunks whose granule records go straight
+//    to the workspace for a second launch to merge (flat schedule, kFlat).
 //  * Every wait is bounded (about one second, %globaltimer); on expiry the CTA
 //    stops waiting, reports status 7 for its rows and still completes the
 //    cluster protocol, so no wait can hang the GPU.
