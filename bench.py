@@ -958,6 +958,7 @@ def run_decode(args):
                    "accepted": sum(o.accepted for o in spec), "tokens": tokens,
                    "stop_reasons": {r: sum(o.stop_reason == r for o in spec) for r in ("eos", "grammar", "length")}},
         "selection_share_of_wall": sum(o.select_seconds for o in spec) / spec_s,
+        "device_draft_share_of_wall": sum(o.draft_seconds for o in spec) / spec_s,
         "eager_tokens_per_s": sum(len(o.token_ids) for o in eager) / eager_s,
         "identical_to_eager": same(spec, eager),
         "lazy_verification_tokens_per_s": sum(len(o.token_ids) for o in lazy) / lazy_s,
@@ -969,7 +970,10 @@ def run_decode(args):
         "note": ("value: c4 with CUDA-graph model trunks; eager = the same without graphs (must be identical); "
                  "lazy verification = the reference's per-row loop on the same target rows, eager (must be "
                  "identical); greedy = target-only decoding, whose bf16 logits come from forwards of other lengths "
-                 "and may differ in near-ties"),
+                 "and may differ in near-ties; drafts run on the device (one CUDA graph per draft step: forward, "
+                 "masked argmax on the state's table row, DFA step; one read-back per round), so draft selections "
+                 "cost no host synchronization: selection_share_of_wall counts the verification calls, "
+                 "device_draft_share_of_wall the drafted rounds from launch to read-back"),
         "roofline": None, "clocks": clocks,
         "e2e": {"value": tokens / spec_s, "unit": "tokens/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
                 "path": "decode.speculative_c4 per prompt (host wall clock, model forwards included, graphs)"},

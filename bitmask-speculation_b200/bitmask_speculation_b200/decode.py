@@ -186,6 +186,129 @@ class _Selector:
         return token
 
 
+class _DraftStep:
+    """One greedy constrained draft step on the device, over static buffers so that it can be
+    replayed from a CUDA graph: the draft forward over ``ids`` (the round's padded length), norm and
+    LM head of row ``ctl[0]`` (the context's last position), the masked argmax of that row under
+    table row ``ctl[2] ? empty : ctl[1]`` (the state; ``select_indexed_into``), the token recorded
+    in ``rec[:, ctl[3]]`` (token, status, terminated before it) and written at ``ids[ctl[0] + 1]``,
+    and the grammar's transition (``device_advance``).  ``ctl`` = [position, state, terminated,
+    step] int64."""
+
+    def __init__(self, model, padded: int, table: DeviceMaskTable, grammar, max_steps: int):
+        torch = _torch()
+        from .kernels._extension import load_extension
+        self.native = load_extension()
+        dev = model.head.weight.device
+        self.model, self.table, self.grammar = model, table, grammar
+        self.ids = torch.zeros(padded, dtype=torch.long, device=dev)
+        self.cos, self.sin = model._rope(padded)
+        self.ctl = torch.zeros(4, dtype=torch.long, device=dev)
+        self.empty = torch.full((1,), table.empty, dtype=torch.long, device=dev)
+        self.idx = torch.empty(1, dtype=torch.int32, device=dev)
+        self.token = torch.empty(1, dtype=torch.long, device=dev)
+        self.status = torch.empty(1, dtype=torch.int32, device=dev)
+        self.scratch = torch.zeros(6, dtype=torch.int32, device=dev)
+        self.rec = torch.zeros((3, max_steps), dtype=torch.long, device=dev)
+        self.graph = None
+
+    def run(self):
+        torch = _torch()
+        m, ctl = self.model, self.ctl
+        pos, state, term, step = ctl[0:1], ctl[1:2], ctl[2:3], ctl[3:4]
+        x = m._trunk(self.ids, self.cos, self.sin)
+        row = m.head(m.norm(x.index_select(0, pos)))
+        self.idx.copy_(torch.where(term != 0, self.empty, state))
+        self.native.select_indexed_into(row, self.table.table, self.idx, self.token, self.status, self.scratch)
+        self.rec[0].index_copy_(0, step, self.token)
+        self.rec[1].index_copy_(0, step, self.status.long())
+        self.rec[2].index_copy_(0, step, term)
+        # A failed row (status != 0, token -1) is discarded by the host; the steps after it still
+        # need a valid token ID to embed.
+        token = self.token.clamp(min=0)
+        self.ids.index_copy_(0, pos + 1, token)
+        nxt, is_eos = self.grammar.device_advance(state, token)
+        ctl.copy_(torch.cat((pos + 1, nxt, term | is_eos.long(), step + 1)))
+
+    def capture(self, pool):
+        """Replay the step from a CUDA graph (after two eager runs on a side stream set up every
+        library handle and launch configuration)."""
+        torch = _torch()
+        dev = self.ids.device
+        side = torch.cuda.Stream(device=dev)
+        # The warm-up runs start from position 0, state 0, step 0 (a step object reused from eager
+        # rounds holds its last round's position and step, which the runs would carry past the
+        # buffers); every round uploads its own ids and control values.
+        self.ids.zero_()
+        self.ctl.zero_()
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self.run()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        # relaxed: the selection's C entry point queries pointer attributes while it is captured
+        with torch.cuda.graph(graph, pool=pool, capture_error_mode="relaxed"):
+            self.run()
+        self.ids.zero_()
+        self.ctl.zero_()
+        self.graph = graph
+        return self
+
+    def step(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.run()
+
+
+def _device_draft(model, prefix, steps: int, grammar, table: DeviceMaskTable, eos) -> tuple[list[int], float]:
+    """Greedy constrained drafting of up to ``steps`` tokens after ``prefix`` with the grammar's
+    states on the device (the draft loop of decoding/speculative.py:63-95, for grammars with a
+    finite state set and ``device_advance``).  Every step (``_DraftStep``: one CUDA-graph replay
+    when the model replays graphs) runs the draft forward over the round's padded length (the last
+    step's context rounded up to 64 tokens), the masked argmax of the context's last row under its
+    state's table row and the grammar's transition, all on the device; the host reads the round
+    back once and keeps the tokens up to where the per-step loop stops: a terminated fork, or before
+    a draft EOS.  A failed selection raises ``ValueError`` as the per-step loop does.  Returns the
+    proposals and the host time from the first step's launch to the read-back."""
+    torch = _torch()
+    from .dispatch import _STATUS_MESSAGES
+    import time
+    if steps <= 0:
+        return [], 0.0
+    n = len(prefix)
+    padded = n + steps + (-(n + steps) % 64)
+    key = (padded, id(table), id(getattr(grammar, "_tables", grammar)))
+    cache = model.__dict__.setdefault("_draft_steps", {})
+    ds = cache.get(key)
+    if ds is None or ds.rec.shape[1] < steps:
+        ds = cache[key] = _DraftStep(model, padded, table, grammar, max(steps, 16))
+    if model._graphs is not None and ds.graph is None:
+        ds.capture(model._pool)
+    host = torch.zeros(padded + 4, dtype=torch.long)
+    host[:n] = torch.tensor(prefix, dtype=torch.long)
+    host[padded:] = torch.tensor([n - 1, grammar.state_index(), 0, 0], dtype=torch.long)
+    host = host.pin_memory()
+    ds.ids.copy_(host[:padded], non_blocking=True)
+    ds.ctl.copy_(host[padded:], non_blocking=True)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ds.step()
+    got = ds.rec[:, :steps].cpu().tolist()
+    seconds = time.perf_counter() - t0
+    proposals: list[int] = []
+    for token, code, was_terminated in zip(*got):
+        if was_terminated:
+            break
+        if code:
+            raise ValueError(_STATUS_MESSAGES.get(code, f"native selection status {code}"))
+        if token in eos:
+            break
+        proposals.append(int(token))
+    return proposals, seconds
+
+
 @dataclass(frozen=True, slots=True)
 class DecodeResult:
     token_ids: tuple
@@ -195,6 +318,7 @@ class DecodeResult:
     proposed: int = 0
     accepted: int = 0
     select_seconds: float = field(default=0.0, compare=False)  # host time in selection and verification calls
+    draft_seconds: float = field(default=0.0, compare=False)  # host time in device-drafted rounds (launch to read-back)
 
 
 # ---------------------------------------------------------------- request loops
@@ -253,20 +377,24 @@ def speculative_c4(target, draft, prompt, grammar, *, max_new_tokens: int, eos=(
     ``verify_with_grammar`` (one launch pair, one sync); ``"lazy"`` with the reference's per-row
     loop (one masked argmax and one sync per consumed row) on the same target rows.  With ``table``
     (the grammar's state masks resident on the device) selections read their masks from it and
-    batched rounds upload table indices instead of mask words."""
+    batched rounds upload table indices instead of mask words; a grammar that also advances on the
+    device (``device_advance``) drafts each round on the device with one read-back
+    (``_device_draft``) instead of one synchronizing selection per draft token."""
     prompt = tuple(int(t) for t in prompt)
     eos = frozenset(int(t) for t in eos)
     policy = DensityPolicy() if policy is None else policy
     device = target.head.weight.device
     sel = selector or _Selector(target.vocab_size, device, table)
+    device_draft = table is not None and selector is None and hasattr(grammar, "device_advance")
     buf = buffer or (None if table is not None else DraftForkMasks(target.vocab_size, policy.max_budget + 1, device))
     out: list[int] = []
     rounds = proposed = accepted = 0
 
-    verify_seconds = 0.0
+    verify_seconds = draft_seconds = 0.0
 
     def finish(reason, token=None):
-        return DecodeResult(tuple(out), reason, token, rounds, proposed, accepted, sel.seconds + verify_seconds)
+        return DecodeResult(tuple(out), reason, token, rounds, proposed, accepted, sel.seconds + verify_seconds,
+                            draft_seconds)
 
     while len(out) < max_new_tokens:
         if grammar.is_terminated():
@@ -275,16 +403,20 @@ def speculative_c4(target, draft, prompt, grammar, *, max_new_tokens: int, eos=(
         budget = min(policy.budget(grammar.mask_density()), max_new_tokens - len(out))
         # Draft on a fork (decoding/speculative.py:63-95): stop before a draft EOS or at the fork's
         # termination; the fork is discarded before verification.
-        branch = grammar.fork()
-        proposals: list[int] = []
-        for _ in range(budget):
-            if branch.is_terminated():
-                break
-            ctx = prefix + tuple(proposals)
-            token = sel(draft.logits(ctx, len(ctx) - 1, 1)[0], branch)
-            if token in eos:
-                break
-            proposals.append(token)
+        if device_draft:
+            proposals, secs = _device_draft(draft, prefix, budget, grammar, table, eos)
+            draft_seconds += secs
+        else:
+            branch = grammar.fork()
+            proposals = []
+            for _ in range(budget):
+                if branch.is_terminated():
+                    break
+                ctx = prefix + tuple(proposals)
+                token = sel(draft.logits(ctx, len(ctx) - 1, 1)[0], branch)
+                if token in eos:
+                    break
+                proposals.append(token)
         proposed += len(proposals)
         rounds += 1
         seq = prefix + tuple(proposals)

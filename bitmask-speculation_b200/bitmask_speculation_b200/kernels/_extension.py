@@ -272,6 +272,24 @@ class NativeModule:
         return out
 
 
+    def select_indexed_into(self, logits, table, mask_rows, tokens, status, scratch):
+        """Masked argmax of each row of ``logits`` [R, V] under table row ``mask_rows[r]`` of
+        ``table`` (an index outside the table fails the row with status 8), written into
+        ``tokens`` (int64 [R]) and ``status`` (int32 [R]); ``scratch`` is an int32 device tensor of
+        at least 6 * R elements (zeroed lengths and per-sequence outputs).  One ``bms_verify_batch``
+        launch pair of one-row sequences on the current stream, no workspace, no allocation and
+        no host synchronization: the call a device-side decoding loop makes per step."""
+        rows, vocab = logits.shape
+        dev = logits.device
+        if scratch.numel() < 6 * rows:
+            raise RuntimeError("scratch must hold 6 int32 values per row")
+        s = scratch.data_ptr()
+        _native.check(self._lib.bms_verify_batch(
+            logits.data_ptr(), _dtype_code(logits), table.data_ptr(), rows, 1, vocab, None, s, None,
+            tokens.data_ptr(), None, status.data_ptr(), None, s + 4 * rows, s + 8 * rows, s + 16 * rows,
+            s + 20 * rows, mask_rows.data_ptr(), table.shape[0], None, 0, dev.index, _stream(dev)))
+
+
 @lru_cache(maxsize=1)
 def load_extension() -> NativeModule:
     """Load the prebuilt sm_100a library; never substitute CPU code for a CUDA call."""

@@ -322,6 +322,16 @@ class SyntheticDFAGrammar:
         """Row of ``mask_table()`` holding the current state's mask; -1 once terminated."""
         return -1 if self._terminated else self._state
 
+    def device_advance(self, state, token):
+        """``accept_token`` on the device for a token the state allows: int64 tensors ``state`` and
+        ``token`` of one shape give (next state, whether the token is an EOS, which terminates)."""
+        import torch
+        nxt = torch.remainder(state * 31 + token * 7 + 1, len(self._tables[1]))
+        eos = torch.zeros_like(token, dtype=torch.bool)
+        for e in sorted(self._tables[2]):
+            eos = eos | (token == e)
+        return nxt, eos
+
     def accept_token(self, token: int) -> bool:
         token = int(token)
         if self._terminated or not (0 <= token < self._vocab):
