@@ -128,3 +128,39 @@ def test_bad_lengths_are_flagged_per_sequence(cuda_module):
     host = verify_batch(logits, masks, proposals, lengths).to_host()
     assert host.seq_status == [6, 0]
     assert host.accept_len[1] == 2 and host.kind[1] == 1
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+def test_indexed_selection_into_caller_buffers(cuda_module, dtype):
+    """``select_indexed_into`` (one-row verification rounds through a device table index, no
+    workspace): every row's token and status equal the oracle's on its table row, an index past the
+    table fails its row with status 8, an all-zero table row with status 1; replayed from a CUDA
+    graph it gives the same results."""
+    rng = np.random.default_rng(31)
+    vocab, rows = 151936, 7
+    table = wl.pack_bits_np(rng.random((5, vocab)) < rng.choice([0.5, 0.01, 1e-4], size=(5, 1)))
+    table[4] = 0
+    index = np.array([0, 1, 2, 3, 4, 5, 2], dtype=np.int32)  # 4: empty row, 5: past the table
+    values = rng.standard_normal((rows, vocab), dtype=np.float32)
+    from helpers import as_dtype_bits
+    bits = as_dtype_bits(values, dtype)
+    dt = None if dtype == "float32" else dtype
+    want_tok, _, want_st = oracle.reduce_rows(bits, table[index.clip(0, 4)], dtype=dt)
+    want_st[5], want_tok[5] = 8, -1
+    logits, dtable = to_device(bits, dtype), torch.from_numpy(table).cuda()
+    didx = torch.from_numpy(index).cuda()
+    tokens = torch.full((rows,), -7, dtype=torch.int64, device="cuda")
+    status = torch.full((rows,), -7, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(6 * rows, dtype=torch.int32, device="cuda")
+    cuda_module.select_indexed_into(logits, dtable, didx, tokens, status, scratch)
+    assert status.cpu().tolist() == want_st.tolist()
+    assert tokens.cpu().tolist() == want_tok.tolist()
+    tokens.fill_(-7)
+    status.fill_(-7)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        cuda_module.select_indexed_into(logits, dtable, didx, tokens, status, scratch)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == want_st.tolist()
+    assert tokens.cpu().tolist() == want_tok.tolist()
