@@ -102,3 +102,29 @@ def test_flat_schedule_back_to_back_launches(module):
         uniforms = np.random.default_rng(200 + i).random(rows)
         got = _sample(module, bits, masks, dtype, temperature, uniforms, True)
         _check(bits, masks, dtype, temperature, uniforms, got)
+
+
+def test_flat_schedule_replayed_from_a_cuda_graph(module):
+    """The flat schedule's launch pair captured once and replayed with new uniforms each time (the
+    workspace's ticket counter and records are left ready by every launch): each replay equals a
+    direct call with the same inputs."""
+    rows, vocab, dtype, temperature = 64, 248320, "float16", 0.7
+    bits, masks, _ = _batch(rows, vocab, dtype, 5)
+    module.use_workspace = True
+    logits, dmasks = to_device(bits, dtype), torch.from_numpy(masks).cuda()
+    u = torch.empty(rows, dtype=torch.float64, device="cuda")
+    u.copy_(torch.from_numpy(np.random.default_rng(0).random(rows)))
+    module.masked_sample_batch(logits, dmasks, temperature, u)  # workspace and kernels set up
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        out = module.masked_sample_batch(logits, dmasks, temperature, u)
+    for seed in range(1, 5):
+        fresh = np.random.default_rng(seed).random(rows)
+        u.copy_(torch.from_numpy(fresh))
+        graph.replay()
+        got = [t.cpu().numpy() for t in out]
+        want = [t.cpu().numpy() for t in module.masked_sample_batch(logits, dmasks, temperature, u)]
+        for g, w in zip(got, want):
+            assert np.array_equal(g, w), seed
+        _check(bits, masks, dtype, temperature, fresh, got)
