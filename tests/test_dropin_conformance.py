@@ -1,8 +1,8 @@
 """Drop-in conformance with the reference's own call sites (CPU; no GPU needed).
 
 The reference is swapped in by making its ``kernels._extension.load_extension`` return this
-library's ``NativeModule``.  Its Python cannot run on the GPU machines of this build (its sources
-stay on the build host), so this test reads the reference's sources where they are present and
+library's ``NativeModule``.  The reference's sources are present only on the host where the
+library is built, not on the GPU machines, so this test reads them where they are present and
 skips elsewhere.  It checks, call site by call site, that ``NativeModule`` serves every call the
 reference makes on its native module -- in kernels/cuda.py, kernels/dispatch.py,
 benchmarks/reductions.py and its GPU tests -- with a method of that name that binds the same
