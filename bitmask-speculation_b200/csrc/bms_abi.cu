@@ -640,12 +640,60 @@ __device__ __forceinline__ RowNorm row_norm(const GatherSlot& g) {
     return r;
 }
 
+// Unnormalised weight of logit x in a row of maximum M: 2^((x - M) log2(e) / T) (fp32).  x == M
+// gives exactly 1 whatever the scale.
+__device__ __forceinline__ float spec_exp(float x, float M, float sc) {
+    const float d = x - M;
+    return ptx::ex2(d == 0.0f ? 0.0f : fminf(d * sc, 126.0f));
+}
+
 // Weight of logit x relative to a row normaliser: 2^((x - M) log2(e) / T) / S (fp32 exponential,
 // fp64 quotient).  x == M gives exactly 1 / S whatever the scale.
 __device__ __forceinline__ double spec_weight(float x, const RowNorm& n, float sc) {
-    const float d = x - n.M;
-    const float t = d == 0.0f ? 0.0f : fminf(d * sc, 126.0f);
-    return static_cast<double>(ptx::ex2(t)) * n.invS;
+    return static_cast<double>(spec_exp(x, n.M, sc)) * n.invS;
+}
+
+// Weights of tokens [a, a + 8) of the sampled row in the row's own units -- inverse-CDF sampling
+// needs only relative masses: e_t = 2^((x - M_t) sc), or in the residual pass max(0, e_t - ratio
+// e_q) with ratio = S_t / S_q (then p - q = that / S_t).  fp32 throughout, two tokens per f32x2
+// instruction: ratio is split into rhi + rlo and applied by two FMAs, whose roundings are relative
+// to the residual itself, so p - q stays accurate to about 1e-7 even where p and q nearly cancel.
+// Tokens outside the mask or past the vocabulary weigh 0 (selected, so whatever a masked logit
+// gives never enters a sum); a valid token has x <= M (M is the row's masked maximum), so its
+// exponent needs no clamp, and the host keeps sc finite, so x == M gives exactly 1.
+template <bool kRes>
+__device__ __forceinline__ void row_weights8(int64_t a, int64_t vocab, uint32_t bits, const float (&xt)[8],
+                                             const float (&xq)[8], float Mt, float Mq, float sc, float rhi,
+                                             float rlo, float (&w)[8]) {
+    if (a + 8 > vocab) bits &= a < vocab ? (1u << (vocab - a)) - 1u : 0u;
+    const uint64_t sc2 = ptx::pack2(sc, sc), nmt = ptx::pack2(-Mt, -Mt);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        float t0, t1;
+        ptx::unpack2(ptx::mul2(ptx::add2(ptx::pack2(xt[i], xt[i + 1]), nmt), sc2), t0, t1);
+        float e0 = ptx::ex2(t0), e1 = ptx::ex2(t1);
+        if constexpr (kRes) {
+            float q0, q1;
+            ptx::unpack2(ptx::mul2(ptx::add2(ptx::pack2(xq[i], xq[i + 1]), ptx::pack2(-Mq, -Mq)), sc2), q0, q1);
+            const uint64_t eq = ptx::pack2(ptx::ex2(q0), ptx::ex2(q1));
+            const uint64_t r = ptx::fma2(ptx::pack2(-rlo, -rlo), eq,
+                                         ptx::fma2(ptx::pack2(-rhi, -rhi), eq, ptx::pack2(e0, e1)));
+            ptx::unpack2(r, e0, e1);
+            e0 = fmaxf(0.0f, e0);
+            e1 = fmaxf(0.0f, e1);
+        }
+        w[i] = ((bits >> i) & 1u) ? e0 : 0.0f;
+        w[i + 1] = ((bits >> (i + 1)) & 1u) ? e1 : 0.0f;
+    }
+}
+
+// ((w0 + w1) + (w2 + w3)) + ((w4 + w5) + (w6 + w7)), the two halves side by side.
+__device__ __forceinline__ float sum8(const float (&w)[8]) {
+    const uint64_t h = ptx::add2(ptx::add2(ptx::pack2(w[0], w[4]), ptx::pack2(w[1], w[5])),
+                                 ptx::add2(ptx::pack2(w[2], w[6]), ptx::pack2(w[3], w[7])));
+    float lo, hi;
+    ptx::unpack2(h, lo, hi);
+    return lo + hi;
 }
 
 // Tokens [a, a + 8) of a row as floats (0 past `vocab`): one or two 16-byte loads when the row is
@@ -675,159 +723,377 @@ __device__ __forceinline__ void load8(const T* row, int64_t a, int64_t vocab, bo
     }
 }
 
-// Speculative sampling for S sequences, one CTA each.  Sequence s has lengths[s] = L drafts
-// proposals[s, i] drawn from the draft's masked softmax q_i (draft row s * (R - 1) + i), and target
-// rows s * R + i giving p_i (R = rows per sequence, both under mask row s * R + i).  Draft i is
-// accepted iff u_i q_i(d_i) < p_i(d_i) (probability min(1, p / q)); at the first rejection j the
-// replacement is drawn by inverse CDF with v_s from max(0, p_j - q_j) normalised, and after L
-// acceptances the bonus from p_L -- so every emitted token is distributed as the target's masked
-// softmax.  A replacement distribution that rounds to zero mass falls back to p_j.  Outputs: the
-// accepted length, the drawn token, its kind (0 replacement, 1 bonus, 2 fallback for L = 0) and a
-// status, nonzero when a row the procedure consumed cannot be sampled.
+// Tokens [a, a + 8) of a 16-byte aligned row as raw 16-byte vectors: issuing the loads of several
+// tiles before any of them is decoded keeps them in flight together.
 template <typename T>
-__global__ void __launch_bounds__(256) speculative_accept_kernel(
+struct Pack8 {
+    uint4 w[Elem<T>::kBytes / 2];
+};
+
+template <typename T>
+__device__ __forceinline__ void fetch8(const T* row, int64_t a, Pack8<T>& p) {
+    const uint4* src = reinterpret_cast<const uint4*>(row + a);
+#pragma unroll
+    for (int i = 0; i < Elem<T>::kBytes / 2; ++i) p.w[i] = __ldg(src + i);
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const Pack8<T>& p, float (&x)[8]) {
+    using E = Elem<T>;
+#pragma unroll
+    for (int i = 0; i < E::kBytes / 2; ++i) {
+        float v[E::kVec];
+        E::decode(p.w[i], v);
+#pragma unroll
+        for (int k = 0; k < E::kVec; ++k) x[i * E::kVec + k] = v[k];
+    }
+}
+
+// Acceptance tests of one sequence (one warp, 32 drafts per pass): the first position j whose
+// draft is rejected (u_i q_i(d_i) >= p_i(d_i), a token outside the mask or a row that cannot be
+// sampled), or L when all L drafts are accepted, and the status of that position's rows.
+template <typename T>
+__device__ void accept_prefix(const T* __restrict__ target, const T* __restrict__ draft,
+                              const int32_t* __restrict__ masks, int64_t seq, int64_t rows_per_seq, int64_t vocab,
+                              const int64_t* __restrict__ proposals, int32_t L, const GatherSlot* __restrict__ tpart,
+                              const GatherSlot* __restrict__ qpart, const double* __restrict__ u_accept, float sc,
+                              int lane, int32_t& j_out, int32_t& code_out) {
+    using E = Elem<T>;
+    const int64_t K = rows_per_seq - 1, words = (vocab + 31) / 32;
+    int32_t j = -1, code = kOk;
+    if (L < 0 || L > K) {
+        j = 0;
+        code = kBadLength;
+    }
+    for (int64_t i0 = 0; j < 0 && i0 < L; i0 += 32) {
+        const int64_t i = i0 + lane;
+        bool stop = false;
+        int32_t c = kOk;
+        if (i < L) {
+            const int64_t trow = seq * rows_per_seq + i, qrow = seq * K + i;
+            const RowNorm tn = row_norm(tpart[trow]), qn = row_norm(qpart[qrow]);
+            c = tn.code != kOk ? tn.code : qn.code;
+            const int64_t d = proposals[seq * K + i];
+            bool ok = false;
+            if (c == kOk && d >= 0 && d < vocab &&
+                ((static_cast<uint32_t>(masks[trow * words + (d >> 5)]) >> (d & 31)) & 1u)) {
+                const double p = spec_weight(E::load(target, trow * vocab + d), tn, sc);
+                const double q = spec_weight(E::load(draft, qrow * vocab + d), qn, sc);
+                ok = q > 0.0 && u_accept[seq * K + i] * q < p;
+            }
+            stop = c != kOk || !ok;
+        }
+        const uint32_t ballot = __ballot_sync(0xFFFFFFFFu, stop);
+        if (ballot) {
+            const int f = __ffs(ballot) - 1;
+            j = static_cast<int32_t>(i0 + f);
+            code = __shfl_sync(0xFFFFFFFFu, c, f);
+        }
+    }
+    j_out = j < 0 ? L : j;
+    code_out = code;
+}
+
+constexpr int kAcceptCluster = 8;  // CTAs per sequence at most (a portable cluster)
+// Streamed acceptance: each CTA's range of the sampled row arrives in chunks of kAccRowBytes per
+// row (target, and the draft in the residual pass) plus the chunk's mask words, kAccStages chunks
+// in flight by 1-D bulk copies.
+constexpr int kAccStages = 3;
+constexpr int kAccRowBytes = 8192;
+constexpr int kAccStageBytes = 2 * kAccRowBytes + 512;
+
+// Speculative sampling for S sequences, one cluster of kAcceptCluster CTAs each.  Sequence s has
+// lengths[s] = L drafts proposals[s, i] drawn from the draft's masked softmax q_i (draft row
+// s * (R - 1) + i), and target rows s * R + i giving p_i (R = rows per sequence, both under mask row
+// s * R + i).  Draft i is accepted iff u_i q_i(d_i) < p_i(d_i) (probability min(1, p / q)); at the
+// first rejection j the replacement is drawn by inverse CDF with v_s from max(0, p_j - q_j)
+// normalised, and after L acceptances the bonus from p_L -- so every emitted token is distributed
+// as the target's masked softmax.  A replacement distribution that rounds to zero mass falls back to
+// p_j.  Outputs: the accepted length, the drawn token, its kind (0 replacement, 1 bonus, 2 fallback
+// for L = 0) and a status, nonzero when a row the procedure consumed cannot be sampled.
+//
+// Every CTA of the cluster (1, 2, 4 or 8 CTAs, chosen by the host from the batch size) runs the
+// (cheap) acceptance tests itself; the sampled row is split into one contiguous range of 256-token
+// tiles per CTA.  Each CTA sums its tiles (a warp per tile, 8 consecutive tokens per lane) -- with
+// kStream, from shared-memory stages that thread 0 fills with 1-D bulk copies (kAccStages chunks in
+// flight, so the bytes in flight cost no registers); without (rows or mask rows not 16-byte
+// aligned), from global memory, four tiles' loads per warp issued together.  It pushes its total
+// to every CTA of the cluster (st.shared::cluster) and, after a cluster barrier, every CTA knows
+// the mass before its range and the total; the CTA whose range holds v * total (or, after
+// rounding, the last CTA with mass) scans its tile sums, walks the tile and pushes the token to
+// every CTA.  Every CTA of a cluster takes the same path and the same barriers (uniform decisions
+// from the same pushed values), so the hardware cluster barriers always complete.  A stage wait
+// that gives up (bounded, about a second) latches an abort: the CTA pushes the flag with its total,
+// the cluster reports kTimeout for the sequence, and the CTA lets its copies land before it exits.
+template <typename T, bool kStream>
+__global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kernel(
     const T* __restrict__ target, const T* __restrict__ draft, const int32_t* __restrict__ masks, int64_t seqs,
     int64_t rows_per_seq, int64_t vocab, const int64_t* __restrict__ proposals, const int32_t* __restrict__ lengths,
     const GatherSlot* __restrict__ tpart, const GatherSlot* __restrict__ qpart, const double* __restrict__ u_accept,
     const double* __restrict__ u_resample, float sc, int32_t* __restrict__ accept_len, int64_t* __restrict__ token,
     int32_t* __restrict__ kind, int32_t* __restrict__ status) {
-    using E = Elem<T>;
-    __shared__ double sums[256];
-    extern __shared__ double tile_sums[];  // one per 256 tokens of the vocabulary
-    __shared__ int32_t s_j, s_code, s_residual, s_last, s_cut_past, s_claim;
+    __shared__ double sums[8];
+    extern __shared__ __align__(128) uint8_t accept_smem[];  // [kStream: stages] [this CTA's tile sums]
+    double* tile_sums = reinterpret_cast<double*>(accept_smem + (kStream ? kAccStages * kAccStageBytes : 0));
+    __shared__ __align__(8) uint64_t s_full[kAccStages];  // a stage's chunk has landed
+    __shared__ __align__(8) uint64_t s_empty[kAccStages]; // every warp has read a stage's chunk
+    __shared__ uint32_t s_issued[kAccStages];             // chunks issued into each stage
+    __shared__ int32_t s_abort;                           // a stage wait gave up (latched)
+    __shared__ uint4 s_rank[kAcceptCluster];   // per CTA of the cluster: its mass (two words), positive
+    __shared__ uint4 s_pick;                   // the owning CTA's token (two words)
+    __shared__ int32_t s_j, s_code, s_last, s_cut_past, s_claim;
     __shared__ int64_t s_token, s_tile;
     __shared__ double s_prefix;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const uint32_t crank = ptx::cluster_ctarank(), csize = ptx::cluster_nctarank();
     const int64_t K = rows_per_seq - 1, words = (vocab + 31) / 32;
+    const int64_t ntiles = (vocab + 255) / 256;
+    const int64_t per_rank = (ntiles + csize - 1) / csize;
+    const int64_t r0 = min(ntiles, static_cast<int64_t>(crank) * per_rank), r1 = min(ntiles, r0 + per_rank);
+    const int64_t nt = r1 - r0;  // tiles of this CTA
+    // 16-byte loads need 16-byte aligned rows (row starts at multiples of vocab elements).
+    const bool vec = (reinterpret_cast<uintptr_t>(target) % 16 == 0) && (reinterpret_cast<uintptr_t>(draft) % 16 == 0) &&
+                     ((vocab * sizeof(T)) % 16 == 0);
     if (tid == 0) {
-        s_last = -1;
-        s_cut_past = 0;
+        for (int s = 0; s < kAccStages; ++s) {
+            ptx::mbar_init(ptx::smem_addr(&s_full[s]), 1);
+            ptx::mbar_init(ptx::smem_addr(&s_empty[s]), 8);
+            s_issued[s] = 0;
+        }
+        s_abort = 0;
+        ptx::fence_mbarrier_init();
     }
-    for (int64_t seq = blockIdx.x; seq < seqs; seq += gridDim.x) {
+    __syncthreads();
+    uint32_t gbase = 0;  // chunks this CTA has streamed so far (every thread counts them alike)
+    for (int64_t seq = ptx::cluster_id_x(); seq < seqs; seq += ptx::ncluster_x()) {
         const int32_t L = lengths[seq];
-        if (tid < 32) {
-            // Acceptance, 32 drafts per pass: the first rejected position (or L) and its status.
-            int32_t j = -1, code = kOk;
-            if (L < 0 || L > K) {
-                j = 0;
-                code = kBadLength;
-            }
-            for (int64_t i0 = 0; j < 0 && i0 < L; i0 += 32) {
-                const int64_t i = i0 + lane;
-                bool stop = false;
-                int32_t c = kOk;
-                if (i < L) {
-                    const int64_t trow = seq * rows_per_seq + i, qrow = seq * K + i;
-                    const RowNorm tn = row_norm(tpart[trow]), qn = row_norm(qpart[qrow]);
-                    c = tn.code != kOk ? tn.code : qn.code;
-                    const int64_t d = proposals[seq * K + i];
-                    bool ok = false;
-                    if (c == kOk && d >= 0 && d < vocab &&
-                        ((static_cast<uint32_t>(masks[trow * words + (d >> 5)]) >> (d & 31)) & 1u)) {
-                        const double p = spec_weight(E::load(target, trow * vocab + d), tn, sc);
-                        const double q = spec_weight(E::load(draft, qrow * vocab + d), qn, sc);
-                        ok = q > 0.0 && u_accept[seq * K + i] * q < p;
-                    }
-                    stop = c != kOk || !ok;
-                }
-                const uint32_t ballot = __ballot_sync(0xFFFFFFFFu, stop);
-                if (ballot) {
-                    const int f = __ffs(ballot) - 1;
-                    j = static_cast<int32_t>(i0 + f);
-                    code = __shfl_sync(0xFFFFFFFFu, c, f);
-                }
-            }
-            if (j < 0) j = L;
+        if (wid == 0) {
+            int32_t j, code;
+            accept_prefix<T>(target, draft, masks, seq, rows_per_seq, vocab, proposals, L, tpart, qpart, u_accept, sc,
+                             lane, j, code);
             if (lane == 0) {
                 s_j = j;
                 s_code = code;
-                s_residual = (code == kOk && j < L) ? 1 : 0;
             }
         }
         __syncthreads();
         const int32_t j = s_j;
         int32_t code = s_code;
+        const bool residual0 = code == kOk && j < L;
         const int64_t trow = seq * rows_per_seq + j;
-        RowNorm tn{0.0f, 1.0, kOk}, qn{0.0f, 1.0, kOk};
+        RowNorm tn{0.0f, 1.0, kOk, 1.0}, qn{0.0f, 1.0, kOk, 1.0};
         if (code == kOk) {
             tn = row_norm(tpart[trow]);
             code = tn.code;
-            if (s_residual) qn = row_norm(qpart[seq * K + j]);  // usable: its acceptance test ran
+            if (residual0) qn = row_norm(qpart[seq * K + j]);  // usable: its acceptance test ran
         }
+        const double ratio = residual0 && code == kOk ? tn.S / qn.S : 0.0;  // S_t / S_q, in [1/V, V]
+        const float rhi = static_cast<float>(ratio), rlo = static_cast<float>(ratio - static_cast<double>(rhi));
+        const T* trow_p = target + trow * vocab;
+        const T* qrow_p = draft + (seq * K + (residual0 ? j : 0)) * vocab;
+        const int32_t* mrow = masks + trow * words;
+        const double cut_u = u_resample[seq];
         int64_t chosen = -1;
-        if (code == kOk) {
-            // Inverse CDF over the row's valid tokens in tiles of 256: a warp per tile, 8
-            // consecutive tokens per lane (coalesced), tile sums in shared memory; then a scan of
-            // the tile sums finds the tile holding v * total and one warp walks it.
-            const T* trow_p = target + trow * vocab;
-            const T* qrow_p = draft + (seq * K + j) * vocab;
-            const int32_t* mrow = masks + trow * words;
-            const int64_t ntiles = (vocab + 255) / 256;
-            // 16-byte loads need 16-byte aligned rows (row starts at multiples of vocab elements).
-            const bool vec = (reinterpret_cast<uintptr_t>(target) % 16 == 0) &&
-                             (reinterpret_cast<uintptr_t>(draft) % 16 == 0) && ((vocab * sizeof(T)) % 16 == 0);
-            for (int pass = 0; pass < 2 && chosen < 0; ++pass) {
-                const bool residual = s_residual && pass == 0;
-                // Lane sum of tokens [t0 + 8 lane, +8) of the tile starting at t0.
-                auto lane_sum = [&](int64_t t0) -> double {
-                    const int64_t a = t0 + 8 * lane;
-                    if (a >= vocab) return 0.0;
-                    const uint32_t bits = (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu;
-                    float xt[8], xq[8];
-                    load8<T>(trow_p, a, vocab, vec, xt);
-                    if (residual) load8<T>(qrow_p, a, vocab, vec, xq);
-                    double acc = 0.0;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        if (!((bits >> i) & 1u) || a + i >= vocab) continue;
-                        const double w = spec_weight(xt[i], tn, sc);
-                        acc += residual ? fmax(0.0, w - spec_weight(xq[i], qn, sc)) : w;
-                    }
-                    return acc;
+        for (int pass = 0; pass < 2 && code == kOk && chosen < 0; ++pass) {
+            const bool residual = residual0 && pass == 0;
+            // Weight sum of tokens [a, a + 8) from their decoded logits (mask bits `bits`).
+            auto weights8 = [&](int64_t a, uint32_t bits, const float (&xt)[8], const float (&xq)[8], float (&w)[8]) {
+                if (residual) row_weights8<true>(a, vocab, bits, xt, xq, tn.M, qn.M, sc, rhi, rlo, w);
+                else row_weights8<false>(a, vocab, bits, xt, xq, tn.M, qn.M, sc, rhi, rlo, w);
+            };
+            auto weigh8 = [&](int64_t a, uint32_t bits, const float (&xt)[8], const float (&xq)[8]) -> double {
+                float w[8];
+                weights8(a, bits, xt, xq, w);
+                return static_cast<double>(sum8(w));
+            };
+            if constexpr (kStream) {
+                // This CTA's tokens [A, B) in chunks of kTok tokens, chunk c in stage (gbase + c) %
+                // kAccStages.  Every chunk starts on a 256-token tile; its byte counts are multiples
+                // of 16 (the host streams only rows of a multiple of 16 bytes and mask rows of a
+                // multiple of 4 words).
+                constexpr int64_t kTok = kAccRowBytes / sizeof(T);
+                const int64_t A = r0 * 256, B = min(r1 * 256, vocab);
+                const int64_t n = B > A ? (B - A + kTok - 1) / kTok : 0;
+                // Thread 0 refills a stage once all eight warps have read its previous chunk (the
+                // warps run up to kAccStages - 1 chunks apart; a warp ahead waits only on a full
+                // barrier of a chunk already issued).
+                auto issue = [&](int64_t c) {
+                    const uint32_t G = gbase + static_cast<uint32_t>(c), st = G % kAccStages, use = G / kAccStages;
+                    if (use > 0 && !wait_bounded(ptx::smem_addr(&s_empty[st]), (use - 1u) & 1u, &s_abort)) return;
+                    const int64_t t0 = A + c * kTok, t1 = min(B, t0 + kTok);
+                    const uint32_t tb = static_cast<uint32_t>((t1 - t0) * static_cast<int64_t>(sizeof(T)));
+                    const uint32_t mb = static_cast<uint32_t>(((t1 + 31) / 32 - t0 / 32) * 4);
+                    const uint32_t bar = ptx::smem_addr(&s_full[st]);
+                    const uint32_t dst = ptx::smem_addr(accept_smem + st * kAccStageBytes);
+                    ptx::mbar_arrive_expect_tx(bar, tb * (residual ? 2u : 1u) + mb);
+                    ptx::bulk_load(dst, trow_p + t0, tb, bar);
+                    if (residual) ptx::bulk_load(dst + kAccRowBytes, qrow_p + t0, tb, bar);
+                    ptx::bulk_load(dst + 2 * kAccRowBytes, mrow + t0 / 32, mb, bar);
+                    ++s_issued[st];
                 };
-                // Four tiles per warp and iteration (their loads overlap), 32 tiles apart.
-                for (int64_t tile = wid; tile < ntiles; tile += 32) {
-                    double v[4];
+                if (tid == 0 && !s_abort)
+                    for (int64_t c = 0; c < n && c < kAccStages; ++c) issue(c);
+                for (int64_t c = 0; c < n; ++c) {
+                    const uint32_t G = gbase + static_cast<uint32_t>(c), st = G % kAccStages;
+                    if (wait_bounded(ptx::smem_addr(&s_full[st]), (G / kAccStages) & 1u, &s_abort)) {
+                        const uint8_t* stage = accept_smem + st * kAccStageBytes;
+                        const int64_t t0 = A + c * kTok;
+                        const int64_t ntc = (min(B, t0 + kTok) - t0 + 255) / 256;  // tiles of the chunk
+                        for (int64_t tl = wid; tl < ntc; tl += 8) {
+                            const int64_t off = tl * 256 + 8 * lane, a = t0 + off;
+                            double v = 0.0;
+                            if (a < vocab) {
+                                const uint32_t word = reinterpret_cast<const uint32_t*>(stage + 2 * kAccRowBytes)[off >> 5];
+                                const uint32_t bits = (word >> (off & 31)) & 0xFFu;
+                                Pack8<T> pk;
+                                float xt[8], xq[8] = {};
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) v[q] = tile + 8 * q < ntiles ? lane_sum((tile + 8 * q) * 256) : 0.0;
+                                for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
+                                    pk.w[i] = reinterpret_cast<const uint4*>(stage + off * sizeof(T))[i];
+                                unpack8<T>(pk, xt);
+                                if (residual) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                                    for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
+                                        pk.w[i] = reinterpret_cast<const uint4*>(stage + kAccRowBytes + off * sizeof(T))[i];
+                                    unpack8<T>(pk, xq);
+                                }
+                                v = weigh8(a, bits, xt, xq);
+                            }
+#pragma unroll
+                            for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+                            if (lane == 0) tile_sums[(t0 - A) / 256 + tl] = v;
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&s_empty[st]));
+                    if (tid == 0 && c + kAccStages < n && !s_abort) issue(c + kAccStages);
+                }
+                gbase += static_cast<uint32_t>(n);
+            } else {
+                // This CTA's tile sums, kBatch tiles per warp and iteration (64 bytes a lane and row in
+                // flight): every raw 16-byte load of the batch is issued before the first weight is
+                // computed.  Rows that are not 16-byte aligned and the row's last partial group take
+                // load8's scalar loads instead.
+                constexpr int kBatch = Elem<T>::kBytes == 2 ? 4 : 2;
+                for (int64_t lt = wid; lt < nt; lt += 8 * kBatch) {
+                    Pack8<T> pt[kBatch], pq[kBatch];
+                    uint32_t bits[kBatch];
+                    bool fast[kBatch];
+#pragma unroll
+                    for (int q = 0; q < kBatch; ++q) {
+                        const int64_t a = (r0 + lt + 8 * q) * 256 + 8 * lane;
+                        const bool live = lt + 8 * q < nt && a < vocab;
+                        bits[q] = live ? (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu : 0u;
+                        fast[q] = live && vec && a + 8 <= vocab;
+                        if (fast[q]) {
+                            fetch8<T>(trow_p, a, pt[q]);
+                            if (residual) fetch8<T>(qrow_p, a, pq[q]);
+                        }
+                    }
+                    double v[kBatch];
+#pragma unroll
+                    for (int q = 0; q < kBatch; ++q) {
+                        const int64_t a = (r0 + lt + 8 * q) * 256 + 8 * lane;
+                        float xt[8], xq[8] = {};
+                        v[q] = 0.0;
+                        if (fast[q]) {
+                            unpack8<T>(pt[q], xt);
+                            if (residual) unpack8<T>(pq[q], xq);
+                            v[q] = weigh8(a, bits[q], xt, xq);
+                        } else if (bits[q]) {
+                            load8<T>(trow_p, a, vocab, vec, xt);
+                            if (residual) load8<T>(qrow_p, a, vocab, vec, xq);
+                            v[q] = weigh8(a, bits[q], xt, xq);
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < kBatch; ++q) {
 #pragma unroll
                         for (int o = 16; o >= 1; o >>= 1) v[q] += __shfl_xor_sync(0xFFFFFFFFu, v[q], o);
-                        if (lane == 0 && tile + 8 * q < ntiles) tile_sums[tile + 8 * q] = v[q];
+                        if (lane == 0 && lt + 8 * q < nt) tile_sums[lt + 8 * q] = v[q];
                     }
                 }
-                if (tid == 0) {
-                    s_tile = -1;
-                    s_token = -1;
-                    s_last = -1;
-                    s_claim = 0;
-                }
-                __syncthreads();
-                // Scan of the tile sums in order: thread tid owns tiles [tid * per, (tid + 1) * per).
-                const int64_t per = (ntiles + 255) / 256;
-                const int64_t a0 = tid * per < ntiles ? tid * per : ntiles;
-                const int64_t a1 = a0 + per < ntiles ? a0 + per : ntiles;
-                double local = 0.0;
-                for (int64_t t = a0; t < a1; ++t) local += tile_sums[t];
-                double v = local;
+            }
+            if (tid == 0) {
+                s_tile = -1;
+                s_token = -1;
+                s_last = -1;
+                s_claim = 0;
+                s_cut_past = 0;
+            }
+            __syncthreads();
+            // Scan of this CTA's tile sums in order: thread tid owns tiles [tid * per, (tid + 1) * per).
+            const int64_t per = (nt + 255) / 256;
+            const int64_t a0 = min(nt, tid * per), a1 = min(nt, a0 + per);
+            double local = 0.0;
+            for (int64_t t = a0; t < a1; ++t) local += tile_sums[t];
+            double v = local;
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const double n = __shfl_up_sync(0xFFFFFFFFu, v, o);
-                    if (lane >= o) v += n;
+            for (int o = 1; o < 32; o <<= 1) {
+                const double n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                if (lane >= o) v += n;
+            }
+            if (lane == 31) sums[wid] = v;
+            __syncthreads();
+            const bool aborted = kStream && s_abort != 0;  // every stage wait has ended by now
+            double before = 0.0, ctotal = 0.0;
+            for (int w = 0; w < 8; ++w) {
+                if (w < wid) before += sums[w];
+                ctotal += sums[w];
+            }
+            // This CTA's mass to every CTA of the cluster, then the cluster's prefix and total.
+            if (tid < static_cast<int>(csize)) {
+                uint32_t lo, hi;
+                memcpy(&lo, &ctotal, 4);
+                memcpy(&hi, reinterpret_cast<const uint8_t*>(&ctotal) + 4, 4);
+                ptx::st_cluster_v4(ptx::mapa(ptx::smem_addr(&s_rank[crank]), static_cast<uint32_t>(tid)), lo, hi,
+                                   ctotal > 0.0 ? 1u : 0u, aborted ? 1u : 0u);
+            }
+            ptx::cluster_arrive();
+            ptx::cluster_wait();
+            auto rank_mass = [&](uint32_t q) -> double {
+                const uint4 r = s_rank[q];
+                const uint64_t bits = (static_cast<uint64_t>(r.y) << 32) | r.x;
+                return __longlong_as_double(static_cast<long long>(bits));
+            };
+            double rbefore = 0.0, total = 0.0;
+            int last_pos = -1;
+            bool any_abort = false;
+            for (uint32_t q = 0; q < csize; ++q) {
+                const double m = rank_mass(q);
+                if (q < crank) rbefore += m;
+                if (s_rank[q].z) last_pos = static_cast<int>(q);
+                any_abort |= s_rank[q].w != 0u;
+                total += m;
+            }
+            // The CTA whose range holds the cut (the masses before it summed in the same order as
+            // rbefore), else -- rounding put the cut past the last mass -- the last CTA with mass.
+            const double cut = cut_u * total;
+            int owner = -1;
+            bool past = false;
+            {
+                double acc = 0.0;
+                for (uint32_t q = 0; q < csize; ++q) {
+                    const double m = rank_mass(q);
+                    if (owner < 0 && m > 0.0 && cut < acc + m) owner = static_cast<int>(q);
+                    acc += m;
                 }
-                if (lane == 31) sums[wid] = v;
-                __syncthreads();
-                double before = 0.0, total = 0.0;
-                for (int w = 0; w < 8; ++w) {
-                    if (w < wid) before += sums[w];
-                    total += sums[w];
-                }
-                const double incl = before + v;
-                const double cut = u_resample[seq] * total;
-                if (total > 0.0 && local > 0.0) {
-                    atomicMax(&s_last, static_cast<int>(tid));
-                    if (cut >= incl - local && cut < incl) {
+            }
+            if (owner < 0 && last_pos >= 0) {
+                owner = last_pos;
+                past = true;
+            }
+            if (any_abort) {  // a CTA's stream gave up: the sequence reports a timeout
+                owner = -1;
+                code = kTimeout;
+            }
+            if (static_cast<int>(crank) == owner) {
+                // This CTA holds the cut: its tile, by the scan of its tile sums (masses before it:
+                // rbefore + the scan), or its last tile with mass when the cut lies past it.
+                const double incl = rbefore + before + v;
+                if (local > 0.0) {
+                    atomicMax(&s_last, tid);
+                    if (!past && cut >= incl - local && cut < incl) {
                         double acc = incl - local;
                         int64_t pick = -1;
                         double pick_prefix = 0.0;
@@ -847,8 +1113,6 @@ __global__ void __launch_bounds__(256) speculative_accept_kernel(
                 }
                 __syncthreads();
                 if (s_tile < 0 && tid == s_last) {
-                    // Rounding put the cut past the last positive tile sum: that tile is walked,
-                    // and its last positive token taken.
                     int64_t pick = -1;
                     double acc = incl - local;
                     double pick_prefix = 0.0;
@@ -864,44 +1128,62 @@ __global__ void __launch_bounds__(256) speculative_accept_kernel(
                 }
                 __syncthreads();
                 if (wid == 0 && s_tile >= 0) {
-                    const int64_t t0 = s_tile * 256;
-                    const double ls = lane_sum(t0);
+                    // Each lane's 8 tokens of the tile, decoded once: the lane sums and the walk.
+                    const int64_t a = (r0 + s_tile) * 256 + 8 * lane;
+                    float xt[8] = {}, xq[8] = {};
+                    uint32_t bits = 0u;
+                    if (a < vocab) {
+                        bits = (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu;
+                        load8<T>(trow_p, a, vocab, vec, xt);
+                        if (residual) load8<T>(qrow_p, a, vocab, vec, xq);
+                    }
+                    float w[8];
+                    weights8(a, bits, xt, xq, w);
+                    const double ls = static_cast<double>(sum8(w));
                     double li = ls;
 #pragma unroll
                     for (int o = 1; o < 32; o <<= 1) {
                         const double n = __shfl_up_sync(0xFFFFFFFFu, li, o);
                         if (lane >= o) li += n;
                     }
-                    const bool past = s_cut_past != 0;
+                    const bool cut_past = s_cut_past != 0;
                     const uint32_t pos = __ballot_sync(0xFFFFFFFFu, ls > 0.0);
-                    const uint32_t hit = __ballot_sync(0xFFFFFFFFu, !past && ls > 0.0 && cut < s_prefix + li);
-                    const int L = hit ? __ffs(hit) - 1 : (pos ? 31 - __clz(pos) : -1);
-                    if (lane == L) {
-                        const int64_t a = t0 + 8 * lane;
-                        const uint32_t bits = (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu;
+                    const uint32_t hit = __ballot_sync(0xFFFFFFFFu, !cut_past && ls > 0.0 && cut < s_prefix + li);
+                    const int Lw = hit ? __ffs(hit) - 1 : (pos ? 31 - __clz(pos) : -1);
+                    if (lane == Lw) {
                         double acc = s_prefix + li - ls;
                         int64_t pick = -1;
+                        bool done = false;
+#pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            if (!((bits >> i) & 1u) || a + i >= vocab) continue;
-                            double w = spec_weight(E::load(trow_p, a + i), tn, sc);
-                            if (residual) w = fmax(0.0, w - spec_weight(E::load(qrow_p, a + i), qn, sc));
-                            if (w > 0.0) {
-                                pick = a + i;
-                                if (hit && cut < acc + w) break;
-                                acc += w;
-                            }
+                            if (done || !(w[i] > 0.0f)) continue;
+                            pick = a + i;
+                            if (hit && cut < acc + static_cast<double>(w[i])) done = true;
+                            else acc += static_cast<double>(w[i]);
                         }
                         s_token = pick;
                     }
                 }
                 __syncthreads();
-                chosen = s_token;
-                if (tid == 0) s_cut_past = 0;
-                __syncthreads();
+                // The token to every CTA of the cluster (-1 if the walk found no weight).
+                if (tid < static_cast<int>(csize)) {
+                    const int64_t tkn = s_token;
+                    uint32_t lo, hi;
+                    memcpy(&lo, &tkn, 4);
+                    memcpy(&hi, reinterpret_cast<const uint8_t*>(&tkn) + 4, 4);
+                    ptx::st_cluster_v4(ptx::mapa(ptx::smem_addr(&s_pick), static_cast<uint32_t>(tid)), lo, hi, 0u, 0u);
+                }
             }
-            if (chosen < 0) code = kNoMass;
+            ptx::cluster_arrive();
+            ptx::cluster_wait();
+            if (owner >= 0) {
+                const uint4 r = s_pick;
+                const uint32_t w2[2] = {r.x, r.y};
+                memcpy(&chosen, w2, 8);
+            }
         }
-        if (tid == 0) {
+        if (code == kOk && chosen < 0) code = kNoMass;
+        if (crank == 0 && tid == 0) {
             accept_len[seq] = j;
             status[seq] = code;
             token[seq] = code == kOk ? chosen : -1;
@@ -909,6 +1191,76 @@ __global__ void __launch_bounds__(256) speculative_accept_kernel(
         }
         __syncthreads();
     }
+    // Copies still in flight after an abort land before the CTA exits, and no CTA exits while a
+    // peer can still write into its shared memory.
+    if (kStream && tid == 0)
+        for (int st = 0; st < kAccStages; ++st)
+            if (s_issued[st] > 0) drain_wait(ptx::smem_addr(&s_full[st]), (s_issued[st] - 1u) & 1u);
+    ptx::cluster_arrive();
+    ptx::cluster_wait();
+}
+
+// Dynamic shared memory of the acceptance kernel: the streamed variant's stages, then one double
+// per 256-token tile of a CTA's range.
+constexpr size_t kAcceptSmemLimit = 200 * 1024;
+
+size_t accept_smem_bytes(int64_t vocab, int csize, bool stream) {
+    const int64_t ntiles = (vocab + 255) / 256;
+    return (stream ? static_cast<size_t>(kAccStages) * kAccStageBytes : 0) +
+           static_cast<size_t>((ntiles + csize - 1) / csize) * sizeof(double);
+}
+
+// Resident clusters of the acceptance kernel for 1, 2, 4 and 8 CTAs per cluster (0 where the
+// shared memory does not fit), cached per device and type for the last vocabulary size seen.
+struct AcceptInfo {
+    int64_t vocab = -1;
+    int clusters[4] = {0, 0, 0, 0};
+};
+
+template <typename T, bool kStream>
+int accept_info(int device, int64_t vocab, AcceptInfo& out) {
+    static AcceptInfo table[kMaxDevices];
+    int sms = 0;
+    BMS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+    std::lock_guard<std::mutex> lock(g_mutex);
+    AcceptInfo& info = table[device];
+    if (info.vocab != vocab) {
+        auto kernel = speculative_accept_kernel<T, kStream>;
+        size_t most = 0;  // the largest size that fits: the function's dynamic shared memory limit
+        for (int i = 0; i < 4; ++i) {
+            const size_t smem = accept_smem_bytes(vocab, 1 << i, kStream);
+            if (smem <= kAcceptSmemLimit) most = std::max(most, smem);
+        }
+        if (most > 48 * 1024)
+            BMS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(most)),
+                     "cudaFuncSetAttribute(smem)");
+        for (int i = 0; i < 4; ++i) {
+            const int c = 1 << i;
+            const size_t smem = accept_smem_bytes(vocab, c, kStream);
+            int n = 0;
+            if (smem <= kAcceptSmemLimit) {
+                cudaLaunchConfig_t cfg = {};
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = c;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.gridDim = dim3(c * sms);
+                cfg.blockDim = dim3(256);
+                cfg.dynamicSmemBytes = smem;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    n = 0;
+                }
+            }
+            info.clusters[i] = n;
+        }
+        info.vocab = vocab;
+    }
+    out = info;
+    return BMS_SUCCESS;
 }
 
 // Longest-prefix acceptance, one warp per sequence: lane i looks at row i of a 32-row window,
@@ -1377,33 +1729,70 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     BMS_CHECK(check_ptr(status, device, "status", 4));
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
-    const float sc = static_cast<float>(1.4426950408889634 / temperature);
-    // One double per 256 tokens of shared memory (7.8 KB at V = 248,320).
-    const size_t smem = static_cast<size_t>((vocab + 255) / 256) * sizeof(double);
-    if (smem > 200 * 1024) return fail(BMS_ERROR_UNSUPPORTED, "vocabulary too large for the acceptance kernel");
-    if (smem > 48 * 1024) {
-        BMS_CUDA(cudaFuncSetAttribute(speculative_accept_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)), "cudaFuncSetAttribute(smem)");
-        BMS_CUDA(cudaFuncSetAttribute(speculative_accept_kernel<__nv_bfloat16>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
-                 "cudaFuncSetAttribute(smem)");
-        BMS_CUDA(cudaFuncSetAttribute(speculative_accept_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)), "cudaFuncSetAttribute(smem)");
+    // log2(e) / T, kept finite (so that a token at the row maximum weighs exactly 1 at any T).
+    const float sc = static_cast<float>(std::min(1.4426950408889634 / temperature, 3.0e38));
+    // CTAs per sequence, c in {1, 2, 4, 8}, by a cost model: the resident clusters take the
+    // sequences in ceil(seqs / resident) rounds, each costing sigma + 1 / c -- streaming the sampled
+    // rows split c ways, plus the serial part of a sequence (the acceptance tests, its rows' norms,
+    // the first chunk's latency, two cluster barriers, the walk) that every CTA of the cluster
+    // waits through.  sigma = kAcceptSerialBytes / row bytes: measured on B200 at V = 248,320 bf16,
+    // one CTA streams a sequence's target and draft rows in about 86 us and the serial part takes
+    // about 13 us, as long as streaming 77.5 KB of one row.
+    // Rows stream through shared memory when every bulk copy can be 16-byte aligned and sized.
+    const auto aligned = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    const bool streamed = aligned(target_logits) && aligned(draft_logits) && aligned(masks) &&
+                        (vocab * static_cast<int64_t>(eb)) % 16 == 0 && ((vocab + 31) / 32) % 4 == 0;
+    AcceptInfo ai;
+#define BMS_SPEC_INFO(T)                                                                       \
+    BMS_CHECK((streamed ? accept_info<T, true>(device, vocab, ai) : accept_info<T, false>(device, vocab, ai)))
+    if (dtype == BMS_FLOAT32) BMS_SPEC_INFO(float);
+    else if (dtype == BMS_BFLOAT16) BMS_SPEC_INFO(__nv_bfloat16);
+    else BMS_SPEC_INFO(__half);
+#undef BMS_SPEC_INFO
+    constexpr double kAcceptSerialBytes = 77500.0;
+    const double sigma = kAcceptSerialBytes / (static_cast<double>(vocab) * static_cast<double>(eb));
+    int ci = -1;
+    double best = 0.0;
+    for (int i = 0; i < 4; ++i) {
+        if (ai.clusters[i] <= 0) continue;
+        const double rounds = static_cast<double>((seqs + ai.clusters[i] - 1) / ai.clusters[i]);
+        const double cost = rounds * (sigma + 1.0 / static_cast<double>(1 << i));
+        if (ci < 0 || cost < best) {
+            ci = i;
+            best = cost;
+        }
     }
-    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 8;
-    const unsigned grid = static_cast<unsigned>(seqs < cap ? seqs : cap);
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (ci < 0) return fail(BMS_ERROR_UNSUPPORTED, "vocabulary too large for the acceptance kernel");
+    for (int i = 0; i < 4; ++i)  // the tests' launch override (1, 2, 4 or 8 CTAs per sequence)
+        if (g_force_cluster == (1 << i) && ai.clusters[i] > 0) ci = i;
+    const int csize = 1 << ci;
+    const int64_t clusters = std::min<int64_t>(seqs, g_force_clusters > 0 ? g_force_clusters : ai.clusters[ci]);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters * csize));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = accept_smem_bytes(vocab, csize, streamed);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     auto tp = reinterpret_cast<const GatherSlot*>(target_partials);
     auto qp = reinterpret_cast<const GatherSlot*>(draft_partials);
-#define BMS_SPEC(T)                                                                                                  \
-    speculative_accept_kernel<T><<<grid, 256, smem, st>>>(                                                           \
-        static_cast<const T*>(target_logits), static_cast<const T*>(draft_logits), masks, seqs, rows_per_seq, vocab, \
-        proposals, lengths, tp, qp, accept_uniforms, resample_uniforms, sc, accept_len, token, kind, status)
-    if (dtype == BMS_FLOAT32) BMS_SPEC(float);
-    else if (dtype == BMS_BFLOAT16) BMS_SPEC(__nv_bfloat16);
-    else BMS_SPEC(__half);
+#define BMS_SPEC_S(T, S)                                                                                    \
+    cudaLaunchKernelEx(&cfg, speculative_accept_kernel<T, S>, static_cast<const T*>(target_logits),            \
+                       static_cast<const T*>(draft_logits), masks, seqs, rows_per_seq, vocab, proposals, lengths, tp, \
+                       qp, accept_uniforms, resample_uniforms, sc, accept_len, token, kind, status)
+#define BMS_SPEC(T) (streamed ? BMS_SPEC_S(T, true) : BMS_SPEC_S(T, false))
+    cudaError_t launched;
+    if (dtype == BMS_FLOAT32) launched = BMS_SPEC(float);
+    else if (dtype == BMS_BFLOAT16) launched = BMS_SPEC(__nv_bfloat16);
+    else launched = BMS_SPEC(__half);
 #undef BMS_SPEC
-    BMS_CUDA(cudaGetLastError(), "speculative acceptance launch");
+#undef BMS_SPEC_S
+    BMS_CUDA(launched, "speculative acceptance launch");
     return BMS_SUCCESS;
 }
 

@@ -134,3 +134,93 @@ def test_failed_and_invalid_rows_report_statuses():
     assert out.status.cpu().tolist() == [2, 1, 6]
     with pytest.raises(ValueError, match="NaN"):
         out.events(0, [0, 0])
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+def test_results_do_not_depend_on_how_many_ctas_share_a_sequence(dtype):
+    """The kernel splits each sequence's row over 8, 4, 2 or 1 CTAs (one cluster) by the batch size:
+    8 sequences take 8 CTAs each, 40 take 4, 100 take 2 and 300 take one (a grid-stride loop).  The
+    first 8 sequences, embedded in each batch, must give the same results every time, and those of
+    the restated rule."""
+    from bitmask_speculation_b200.kernels._extension import load_extension
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    dev = torch.device("cuda")
+    temp, k, vocab, seqs = 0.8, wl.DRAFT_K, wl.VOCAB, 300
+    logits, masks, _, _ = wl.verify_batch_torch(seqs, seed=21, device=dev)
+    words = masks.shape[1]
+    g = torch.Generator(device=dev).manual_seed(5)
+    first_k = logits.view(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab)
+    draft = (first_k.float() + 0.7 * torch.randn(first_k.shape, generator=g, device=dev)).to(torch.bfloat16)
+    dmasks = masks.view(seqs, k + 1, words)[:, :k].reshape(seqs * k, words).contiguous()
+    u = torch.rand(seqs * k, dtype=torch.float64, generator=g, device=dev)
+    proposals = load_extension().masked_sample_batch(draft, dmasks, temp, u)[0].view(seqs, k).contiguous()
+    lengths = torch.randint(0, k + 1, (seqs,), generator=g, device=dev).to(torch.int32)
+    ua = torch.rand((seqs, k), dtype=torch.float64, generator=g, device=dev)
+    ur = torch.rand(seqs, dtype=torch.float64, generator=g, device=dev)
+    if dtype == "float32":
+        logits, draft = logits.float(), draft.float()
+    results = []
+    for n in (8, 40, 100, 300):
+        out = speculative_accept(logits[: n * (k + 1)], draft[: n * k], masks[: n * (k + 1)], proposals[:n],
+                                 lengths[:n], temperature=temp, accept_uniforms=ua[:n], resample_uniforms=ur[:n])
+        assert (out.status == 0).all()
+        results.append([t[:8].cpu() for t in (out.accept_len, out.token, out.kind)])
+    for other in results[1:]:
+        for a, b in zip(results[0], other):
+            assert torch.equal(a, b)
+    n_chk = 6
+    tf = _widen(logits[: n_chk * (k + 1)].to(torch.bfloat16))
+    df = _widen(draft[: n_chk * k].to(torch.bfloat16))
+    want = oracle.speculative_accept(tf, df, masks[: n_chk * (k + 1)].cpu().numpy(), proposals[:n_chk].cpu().numpy(),
+                                     lengths[:n_chk].cpu().numpy(), temp, ua[:n_chk].cpu().numpy(),
+                                     ur[:n_chk].cpu().numpy())
+    acc, tok, kind = (t.numpy() for t in results[0])
+    for s, (j, t, kd, margin, dist) in enumerate(want):
+        if margin < 1e-5:
+            continue
+        assert acc[s] == j and kind[s] == kd, s
+        if tok[s] != t:
+            cum = np.cumsum(dist)
+            lo, hi = cum[tok[s]] - dist[tok[s]], cum[tok[s]]
+            assert min(abs(ur[s].item() - lo), abs(ur[s].item() - hi)) <= 1e-5, (s, tok[s], t)
+
+
+@pytest.mark.parametrize("vocab", [1001, 4104, 4096])
+def test_rows_that_cannot_be_bulk_copied_agree_with_the_restated_rule(vocab):
+    """Rows stream through shared memory by 16-byte bulk copies only when a row is a multiple of 16
+    bytes and a mask row a multiple of 4 words; V = 1001 (2002-byte rows) and V = 4104 (129 mask
+    words) take the register path instead, V = 4096 streams.  All three must follow the rule."""
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rng = np.random.default_rng(vocab)
+    seqs, k, temp = 24, 4, 0.9
+    rows = seqs * (k + 1)
+    valid = rng.random((rows, vocab)) < 0.6
+    masks = wl.pack_bits_np(valid)
+    tvals = _bf16(rng.standard_normal((rows, vocab), dtype=np.float32) * np.float32(1.5))
+    dvals_np = _widen(tvals).reshape(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab).copy()
+    dvals_np += rng.standard_normal(dvals_np.shape, dtype=np.float32) * np.float32(0.5)
+    dvals = _bf16(dvals_np)
+    tf, df = _widen(tvals), _widen(dvals)
+    proposals = np.zeros((seqs, k), dtype=np.int64)
+    lengths = rng.integers(0, k + 1, size=seqs).astype(np.int32)
+    for s in range(seqs):
+        for i in range(lengths[s]):
+            proposals[s, i] = rng.choice(vocab, p=oracle.masked_softmax(df[s * k + i], masks[s * (k + 1) + i], temp))
+    ua, ur = rng.random((seqs, k)), rng.random(seqs)
+    out = speculative_accept(tvals.cuda(), dvals.cuda(), torch.from_numpy(masks).cuda(), torch.from_numpy(proposals).cuda(),
+                             torch.from_numpy(lengths).cuda(), temperature=temp,
+                             accept_uniforms=torch.from_numpy(ua).cuda(), resample_uniforms=torch.from_numpy(ur).cuda())
+    acc, tok, kind, st = (t.cpu().numpy() for t in (out.accept_len, out.token, out.kind, out.status))
+    assert (st == 0).all()
+    want = oracle.speculative_accept(tf, df, masks, proposals, lengths, temp, ua, ur)
+    checked = 0
+    for s, (j, t, kd, margin, dist) in enumerate(want):
+        if margin < 1e-5:
+            continue
+        assert acc[s] == j and kind[s] == kd, s
+        if tok[s] != t:
+            cum = np.cumsum(dist)
+            lo, hi = cum[tok[s]] - dist[tok[s]], cum[tok[s]]
+            assert dist[tok[s]] > 0 and min(abs(ur[s] - lo), abs(ur[s] - hi)) <= 1e-5, (s, tok[s], t)
+        checked += 1
+    assert checked >= seqs - 2
