@@ -34,7 +34,8 @@ EXPORTS = (
     "bms_last_error", "bms_runtime_version", "bms_mask_count", "bms_masked_argmax",
     "bms_masked_reduce_batch", "bms_masked_sample", "bms_masked_sample_batch",
     "bms_mask_budget", "bms_expand_token_lists", "bms_expand_token_gaps", "bms_speculative_accept", "bms_verify_batch", "bms_set_launch_override", "bms_shard_granule_bytes",
-    "bms_shard_partials", "bms_shard_merge", "bms_workspace_bytes", "bms_masked_reduce_batch_noalloc",
+    "bms_shard_partials", "bms_shard_partials_indexed", "bms_shard_merge", "bms_workspace_bytes",
+    "bms_masked_reduce_batch_noalloc",
     "bms_exchange_bytes", "bms_exchange_create", "bms_exchange_open", "bms_exchange_close", "bms_exchange_destroy",
     "bms_shard_partials_exchange", "bms_shard_merge_exchange",
 )
@@ -66,6 +67,7 @@ def _declare(lib) -> None:
                              p, p, p, p, p, i64, p, i64, i32, p],
         "bms_set_launch_override": [i32, i32],
         "bms_shard_partials": [p, i32, p, i64, i64, i64, i64, f64, p, p, i64, i32, p],
+        "bms_shard_partials_indexed": [p, i32, p, i64, p, i64, i64, i64, i64, f64, p, p, i64, i32, p],
         "bms_shard_merge": [p, i32, i32, i64, f64, p, p, i32, p, i64, i64, i64, p, i64, p, p, p, i32, p],
         "bms_exchange_create": [i32, i32, i64, ctypes.POINTER(p), ctypes.POINTER(IpcHandle)],
         "bms_exchange_open": [i32, ctypes.POINTER(IpcHandle), ctypes.POINTER(p)],

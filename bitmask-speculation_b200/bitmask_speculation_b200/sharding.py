@@ -53,7 +53,9 @@ def row_shard(rows: int, world: int, rank: int) -> slice:
 class NativeShardBackend:
     """The CUDA kernels behind ``vocab_sharded_select`` (the only product backend)."""
 
-    def partials(self, logits, masks, token_offset, temperature):
+    def partials(self, logits, masks, token_offset, temperature, mask_rows=None):
+        """Per-row partials of ``logits`` under ``masks`` (row r's mask is ``masks[mask_rows[r]]``
+        when the int32 device table ``mask_rows`` is given: ``bms_shard_partials_indexed``)."""
         import torch
         rows, vocab_shard = logits.shape
         dev = logits.device
@@ -65,10 +67,12 @@ class NativeShardBackend:
             stride = int(lib.bms_shard_granule_bytes(dtype, vocab_shard))
             stride = (stride + 15) // 16 * 16
             granules = torch.empty((rows, stride), dtype=torch.uint8, device=dev)
-        _native.check(lib.bms_shard_partials(
-            logits.data_ptr(), dtype, masks.data_ptr(), masks.shape[1], rows, vocab_shard, token_offset,
-            float(temperature), partials.data_ptr(), granules.data_ptr() if granules is not None else None,
-            stride, dev.index, torch.cuda.current_stream(dev).cuda_stream))
+        _native.check(lib.bms_shard_partials_indexed(
+            logits.data_ptr(), dtype, masks.data_ptr(), masks.shape[1],
+            mask_rows.data_ptr() if mask_rows is not None else None, masks.shape[0], rows, vocab_shard,
+            token_offset, float(temperature), partials.data_ptr(),
+            granules.data_ptr() if granules is not None else None, stride, dev.index,
+            torch.cuda.current_stream(dev).cuda_stream))
         return partials, (granules, stride)
 
     def merge(self, gathered, shard, temperature, uniforms, logits, masks, token_offset, aux):

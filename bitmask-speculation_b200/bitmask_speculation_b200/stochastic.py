@@ -9,8 +9,10 @@ max(0, p_j - q_j) normalised, and if all L drafts are accepted a bonus token is 
 Every emitted token is then distributed exactly as target sampling would give it.
 
 Device work per round: the selection kernel's sampler partials (row max and mass, one streaming
-pass) for the target rows and the draft rows, then ``bms_speculative_accept`` (one CTA per sequence:
-the acceptance tests, then an inverse-CDF pass over the one row that is sampled).
+pass) for the target rows and the draft rows -- the draft rows read the round's mask rows through
+a table (``bms_shard_partials_indexed``), no gathered copy -- then ``bms_speculative_accept`` (a
+cluster of 1-8 CTAs per sequence: the acceptance tests, then an inverse-CDF pass over the one row
+that is sampled).
 """
 
 from __future__ import annotations
@@ -20,6 +22,22 @@ from dataclasses import dataclass
 from . import _native
 from .kernels._validation import temperature_input
 from .verification import KINDS, VerifiedToken
+
+_DRAFT_MASK_ROWS: dict = {}  # (seqs, K, device) -> int32 table: draft row s*K + i -> mask row s*(K+1) + i
+
+
+def _draft_mask_rows(seqs: int, k: int, device):
+    import torch
+    key = (seqs, k, str(device))
+    table = _DRAFT_MASK_ROWS.get(key)
+    if table is None:
+        r = torch.arange(seqs * k, dtype=torch.int64, device=device)
+        table = ((r // k) * (k + 1) + r % k).to(torch.int32)
+        if len(_DRAFT_MASK_ROWS) >= 16:
+            _DRAFT_MASK_ROWS.clear()
+        _DRAFT_MASK_ROWS[key] = table
+    return table
+
 
 _ERRORS = {1: "mask has no valid token", 2: "logits contain NaN", 4: "valid logits have no finite probability mass",
            5: "positive infinity is unsupported for stochastic sampling", 6: "proposal count outside [0, K]",
@@ -78,8 +96,8 @@ def speculative_accept(target_logits, draft_logits, masks, proposals, lengths, *
     tpart, _ = backend.partials(target_logits.contiguous(), masks, 0, temperature)
     qpart = None
     if seqs * k:
-        draft_masks = masks.view(seqs, k + 1, words)[:, :k].reshape(seqs * k, words).contiguous()
-        qpart, _ = backend.partials(draft_logits.contiguous(), draft_masks, 0, temperature)
+        qpart, _ = backend.partials(draft_logits.contiguous(), masks, 0, temperature,
+                                    mask_rows=_draft_mask_rows(seqs, k, dev))
     if accept_uniforms is None:
         accept_uniforms = torch.rand((seqs, k), dtype=torch.float64, device=dev, generator=generator)
     if resample_uniforms is None:

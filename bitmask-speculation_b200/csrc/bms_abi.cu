@@ -939,29 +939,55 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
                         const uint8_t* stage = accept_smem + st * kAccStageBytes;
                         const int64_t t0 = A + c * kTok;
                         const int64_t ntc = (min(B, t0 + kTok) - t0 + 255) / 256;  // tiles of the chunk
-                        for (int64_t tl = wid; tl < ntc; tl += 8) {
-                            const int64_t off = tl * 256 + 8 * lane, a = t0 + off;
-                            double v = 0.0;
-                            if (a < vocab) {
-                                const uint32_t word = reinterpret_cast<const uint32_t*>(stage + 2 * kAccRowBytes)[off >> 5];
-                                const uint32_t bits = (word >> (off & 31)) & 0xFFu;
-                                Pack8<T> pk;
-                                float xt[8], xq[8] = {};
+                        // fp32 lane sum of tile tl of the chunk (tokens past the vocabulary weigh 0).
+                        auto lane_tile = [&](int64_t tl) -> float {
+                            const int64_t off = tl * 256 + 8 * lane;
+                            const uint32_t word = reinterpret_cast<const uint32_t*>(stage + 2 * kAccRowBytes)[off >> 5];
+                            Pack8<T> pk;
+                            float xt[8], xq[8] = {}, w[8];
+#pragma unroll
+                            for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
+                                pk.w[i] = reinterpret_cast<const uint4*>(stage + off * sizeof(T))[i];
+                            unpack8<T>(pk, xt);
+                            if (residual) {
 #pragma unroll
                                 for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
-                                    pk.w[i] = reinterpret_cast<const uint4*>(stage + off * sizeof(T))[i];
-                                unpack8<T>(pk, xt);
-                                if (residual) {
-#pragma unroll
-                                    for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
-                                        pk.w[i] = reinterpret_cast<const uint4*>(stage + kAccRowBytes + off * sizeof(T))[i];
-                                    unpack8<T>(pk, xq);
-                                }
-                                v = weigh8(a, bits, xt, xq);
+                                    pk.w[i] = reinterpret_cast<const uint4*>(stage + kAccRowBytes + off * sizeof(T))[i];
+                                unpack8<T>(pk, xq);
                             }
+                            weights8(t0 + off, (word >> (off & 31)) & 0xFFu, xt, xq, w);
+                            return sum8(w);
+                        };
+                        // A full chunk has kPerWarp tiles per warp: both computed in one unrolled block
+                        // (independent work to interleave), then one fp32 butterfly for both sums --
+                        // after the xor-16 step the low half-warp holds tile wid's pairs, the high half
+                        // tile wid + 8's.
+                        constexpr int kPerWarp = static_cast<int>(kTok / 256 / 8);  // 2 (16-bit), 1 (fp32)
+                        float sk[kPerWarp];
+                        if (ntc * 256 == kTok && t0 + kTok <= vocab) {
+#pragma unroll
+                            for (int k = 0; k < kPerWarp; ++k) sk[k] = lane_tile(wid + 8 * k);
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < kPerWarp; ++k) {
+                                const int64_t tl = wid + 8 * k;
+                                sk[k] = tl < ntc && t0 + tl * 256 + 8 * lane < vocab ? lane_tile(tl) : 0.0f;
+                            }
+                        }
+                        const int64_t tbase = (t0 - A) / 256;
+                        if constexpr (kPerWarp == 2) {
+                            const bool high = (lane & 16) != 0;
+                            float v = high ? sk[1] : sk[0];
+                            v += __shfl_xor_sync(0xFFFFFFFFu, high ? sk[0] : sk[1], 16);
+#pragma unroll
+                            for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+                            if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
+                            if (lane == 16 && wid + 8 < ntc) tile_sums[tbase + wid + 8] = v;
+                        } else {
+                            float v = sk[0];
 #pragma unroll
                             for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-                            if (lane == 0) tile_sums[(t0 - A) / 256 + tl] = v;
+                            if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
                         }
                     }
                     __syncwarp();
@@ -1922,6 +1948,14 @@ int64_t bms_shard_granule_bytes(int32_t dtype, int64_t vocab_shard) {
 int bms_shard_partials(const void* logits, int32_t dtype, const int32_t* masks, int64_t mask_words, int64_t rows,
                        int64_t vocab_shard, int64_t token_offset, double temperature, bms_partial* partials,
                        void* granules, int64_t granule_stride, int32_t device, void* stream) {
+    return bms_shard_partials_indexed(logits, dtype, masks, mask_words, nullptr, 0, rows, vocab_shard, token_offset,
+                                      temperature, partials, granules, granule_stride, device, stream);
+}
+
+int bms_shard_partials_indexed(const void* logits, int32_t dtype, const int32_t* masks, int64_t mask_words,
+                               const int32_t* mask_rows, int64_t mask_table_rows, int64_t rows, int64_t vocab_shard,
+                               int64_t token_offset, double temperature, bms_partial* partials, void* granules,
+                               int64_t granule_stride, int32_t device, void* stream) {
     if (!std::isfinite(temperature) || temperature < 0)
         return fail(BMS_ERROR_INVALID_ARGUMENT, "temperature must be finite and nonnegative");
     if (token_offset < 0 || token_offset % 32 != 0)
@@ -1942,7 +1976,13 @@ int bms_shard_partials(const void* logits, int32_t dtype, const int32_t* masks, 
     }
     DeviceGuard guard;
     BMS_CUDA(guard.enter(device), "cudaSetDevice");
+    if (mask_rows != nullptr) {
+        if (mask_table_rows < 1) return fail(BMS_ERROR_INVALID_ARGUMENT, "mask_table_rows must be at least 1");
+        BMS_CHECK(check_ptr(mask_rows, device, "mask_rows", 4));
+    }
     SelectParams p = base_params(logits, masks, rows, vocab_shard);
+    p.mask_rows = mask_rows;
+    p.mask_table_rows = mask_table_rows;
     p.mask_stride = mask_words;
     p.mask_word_offset = token_offset / 32;
     p.token_offset = token_offset;

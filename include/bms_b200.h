@@ -211,6 +211,17 @@ BMS_API int bms_shard_partials(const void *logits, int32_t dtype, const int32_t 
                                bms_partial *partials, void *granules, int64_t granule_stride, int32_t device,
                                void *stream);
 
+/* bms_shard_partials with a mask table: row r's mask is row mask_rows[r] of `masks`
+ * ([mask_table_rows, mask_words] int32; mask_rows int32 on the device), so rows that share mask
+ * rows need no gathered copy -- the draft rows of bms_speculative_accept: draft row s * K + i takes
+ * mask row s * (K + 1) + i.  An index outside [0, mask_table_rows) fails its row with
+ * BMS_STATUS_BAD_MASK_ROW.  mask_rows NULL is bms_shard_partials. */
+BMS_API int bms_shard_partials_indexed(const void *logits, int32_t dtype, const int32_t *masks, int64_t mask_words,
+                                       const int32_t *mask_rows, int64_t mask_table_rows, int64_t rows,
+                                       int64_t vocab_shard, int64_t token_offset, double temperature,
+                                       bms_partial *partials, void *granules, int64_t granule_stride,
+                                       int32_t device, void *stream);
+
 /* Merge `shards` ranks' partials ([shards, rows] in rank order) on rank `shard`.  temperature 0:
  * final argmax tokens, counts and status of every row (identical on every rank).  Sampler: status
  * and counts of every row; `tokens[row]` is the sampled token if it lies in this rank's shard and

@@ -102,3 +102,35 @@ def test_shard_bounds_match_cluster_segments():
     assert shard_bounds(248320, 2) == [(0, 124160), (124160, 124160)]
     b = shard_bounds(151936, 8)
     assert all(off % 32 == 0 for off, _ in b) and sum(s for _, s in b) == 151936
+
+
+@pytest.mark.parametrize("temperature", [0.0, 0.8])
+def test_partials_through_a_mask_table_equal_gathered_masks(temperature):
+    """``bms_shard_partials_indexed`` reads row r's mask from ``masks[mask_rows[r]]``: its partials
+    (and sampler granules) must equal those of the gathered mask rows bit for bit, and an index
+    outside the table must fail its row with status 8."""
+    rng = np.random.default_rng(9)
+    rows, table_rows, vocab = 96, 40, 20_000
+    bits, masks = make_rows(5, table_rows, vocab, "bfloat16")
+    values = rng.standard_normal((rows, vocab), dtype=np.float32) * np.float32(3)
+    logits = to_device(as_dtype_bits(values, "bfloat16"), "bfloat16")
+    table = rng.integers(0, table_rows, size=rows).astype(np.int32)
+    backend = NativeShardBackend()
+    gathered = torch.from_numpy(masks[table]).cuda()
+    dev_masks = torch.from_numpy(masks).cuda()
+    pa, (ga, _) = backend.partials(logits, gathered, 0, temperature)
+    pb, (gb, _) = backend.partials(logits, dev_masks, 0, temperature, mask_rows=torch.from_numpy(table).cuda())
+    assert torch.equal(pa, pb)
+    if temperature:
+        assert torch.equal(ga, gb)
+    bad = table.copy()
+    bad[7], bad[50] = table_rows, -1
+    pc, ax = backend.partials(logits, dev_masks, 0, 0.0, mask_rows=torch.from_numpy(bad).cuda())
+    _, _, status = backend.merge(pc[None], 0, 0.0, None, logits, gathered, 0, ax)
+    st = status.cpu().numpy()
+    assert st[7] == 8 and st[50] == 8
+    ok = np.ones(rows, dtype=bool)
+    ok[[7, 50]] = False
+    _, _, want = backend.merge(pa[None] if temperature == 0 else backend.partials(logits, gathered, 0, 0.0)[0][None],
+                               0, 0.0, None, logits, gathered, 0, ax)
+    assert np.array_equal(st[ok], want.cpu().numpy()[ok])
