@@ -795,12 +795,15 @@ __device__ void accept_prefix(const T* __restrict__ target, const T* __restrict_
 }
 
 constexpr int kAcceptCluster = 8;  // CTAs per sequence at most (a portable cluster)
-// Streamed acceptance: each CTA's range of the sampled row arrives in chunks of kAccRowBytes per
-// row (target, and the draft in the residual pass) plus the chunk's mask words, kAccStages chunks
-// in flight by 1-D bulk copies.
+// Acceptance CTAs have kAccWarps warps.  Streamed, each CTA's range of the sampled row arrives in
+// chunks of kAccRowBytes per row (target, and the draft in the residual pass; two 256-token tiles
+// per warp of 16-bit logits, one of fp32) plus the chunk's mask words, kAccStages chunks in flight
+// by 1-D bulk copies.
+constexpr int kAccWarps = 12;
+constexpr int kAccThreads = 32 * kAccWarps;
 constexpr int kAccStages = 3;
-constexpr int kAccRowBytes = 8192;
-constexpr int kAccStageBytes = 2 * kAccRowBytes + 512;
+constexpr int kAccRowBytes = 1024 * kAccWarps;
+constexpr int kAccStageBytes = 2 * kAccRowBytes + kAccRowBytes / 16;
 
 // Speculative sampling for S sequences, one cluster of kAcceptCluster CTAs each.  Sequence s has
 // lengths[s] = L drafts proposals[s, i] drawn from the draft's masked softmax q_i (draft row
@@ -826,13 +829,13 @@ constexpr int kAccStageBytes = 2 * kAccRowBytes + 512;
 // that gives up (bounded, about a second) latches an abort: the CTA pushes the flag with its total,
 // the cluster reports kTimeout for the sequence, and the CTA lets its copies land before it exits.
 template <typename T, bool kStream>
-__global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kernel(
+__global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_accept_kernel(
     const T* __restrict__ target, const T* __restrict__ draft, const int32_t* __restrict__ masks, int64_t seqs,
     int64_t rows_per_seq, int64_t vocab, const int64_t* __restrict__ proposals, const int32_t* __restrict__ lengths,
     const GatherSlot* __restrict__ tpart, const GatherSlot* __restrict__ qpart, const double* __restrict__ u_accept,
     const double* __restrict__ u_resample, float sc, int32_t* __restrict__ accept_len, int64_t* __restrict__ token,
     int32_t* __restrict__ kind, int32_t* __restrict__ status) {
-    __shared__ double sums[8];
+    __shared__ double sums[kAccWarps];
     extern __shared__ __align__(128) uint8_t accept_smem[];  // [kStream: stages] [this CTA's tile sums]
     double* tile_sums = reinterpret_cast<double*>(accept_smem + (kStream ? kAccStages * kAccStageBytes : 0));
     __shared__ __align__(8) uint64_t s_full[kAccStages];  // a stage's chunk has landed
@@ -857,7 +860,7 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
     if (tid == 0) {
         for (int s = 0; s < kAccStages; ++s) {
             ptx::mbar_init(ptx::smem_addr(&s_full[s]), 1);
-            ptx::mbar_init(ptx::smem_addr(&s_empty[s]), 8);
+            ptx::mbar_init(ptx::smem_addr(&s_empty[s]), kAccWarps);
             s_issued[s] = 0;
         }
         s_abort = 0;
@@ -961,16 +964,17 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
                         // A full chunk has kPerWarp tiles per warp: both computed in one unrolled block
                         // (independent work to interleave), then one fp32 butterfly for both sums --
                         // after the xor-16 step the low half-warp holds tile wid's pairs, the high half
-                        // tile wid + 8's.
-                        constexpr int kPerWarp = static_cast<int>(kTok / 256 / 8);  // 2 (16-bit), 1 (fp32)
+                        // tile wid + kAccWarps's.
+                        constexpr int kPerWarp = static_cast<int>(kTok / 256 / kAccWarps);  // 2 (16-bit), 1 (fp32)
+                        static_assert(kPerWarp * 256 * kAccWarps == kTok, "a chunk is whole tiles per warp");
                         float sk[kPerWarp];
                         if (ntc * 256 == kTok && t0 + kTok <= vocab) {
 #pragma unroll
-                            for (int k = 0; k < kPerWarp; ++k) sk[k] = lane_tile(wid + 8 * k);
+                            for (int k = 0; k < kPerWarp; ++k) sk[k] = lane_tile(wid + kAccWarps * k);
                         } else {
 #pragma unroll
                             for (int k = 0; k < kPerWarp; ++k) {
-                                const int64_t tl = wid + 8 * k;
+                                const int64_t tl = wid + kAccWarps * k;
                                 sk[k] = tl < ntc && t0 + tl * 256 + 8 * lane < vocab ? lane_tile(tl) : 0.0f;
                             }
                         }
@@ -982,7 +986,7 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
 #pragma unroll
                             for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
                             if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
-                            if (lane == 16 && wid + 8 < ntc) tile_sums[tbase + wid + 8] = v;
+                            if (lane == 16 && wid + kAccWarps < ntc) tile_sums[tbase + wid + kAccWarps] = v;
                         } else {
                             float v = sk[0];
 #pragma unroll
@@ -1001,14 +1005,14 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
                 // computed.  Rows that are not 16-byte aligned and the row's last partial group take
                 // load8's scalar loads instead.
                 constexpr int kBatch = Elem<T>::kBytes == 2 ? 4 : 2;
-                for (int64_t lt = wid; lt < nt; lt += 8 * kBatch) {
+                for (int64_t lt = wid; lt < nt; lt += kAccWarps * kBatch) {
                     Pack8<T> pt[kBatch], pq[kBatch];
                     uint32_t bits[kBatch];
                     bool fast[kBatch];
 #pragma unroll
                     for (int q = 0; q < kBatch; ++q) {
-                        const int64_t a = (r0 + lt + 8 * q) * 256 + 8 * lane;
-                        const bool live = lt + 8 * q < nt && a < vocab;
+                        const int64_t a = (r0 + lt + kAccWarps * q) * 256 + 8 * lane;
+                        const bool live = lt + kAccWarps * q < nt && a < vocab;
                         bits[q] = live ? (static_cast<uint32_t>(mrow[a >> 5]) >> (a & 31)) & 0xFFu : 0u;
                         fast[q] = live && vec && a + 8 <= vocab;
                         if (fast[q]) {
@@ -1019,7 +1023,7 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
                     double v[kBatch];
 #pragma unroll
                     for (int q = 0; q < kBatch; ++q) {
-                        const int64_t a = (r0 + lt + 8 * q) * 256 + 8 * lane;
+                        const int64_t a = (r0 + lt + kAccWarps * q) * 256 + 8 * lane;
                         float xt[8], xq[8] = {};
                         v[q] = 0.0;
                         if (fast[q]) {
@@ -1036,7 +1040,7 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
                     for (int q = 0; q < kBatch; ++q) {
 #pragma unroll
                         for (int o = 16; o >= 1; o >>= 1) v[q] += __shfl_xor_sync(0xFFFFFFFFu, v[q], o);
-                        if (lane == 0 && lt + 8 * q < nt) tile_sums[lt + 8 * q] = v[q];
+                        if (lane == 0 && lt + kAccWarps * q < nt) tile_sums[lt + kAccWarps * q] = v[q];
                     }
                 }
             }
@@ -1049,7 +1053,7 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
             }
             __syncthreads();
             // Scan of this CTA's tile sums in order: thread tid owns tiles [tid * per, (tid + 1) * per).
-            const int64_t per = (nt + 255) / 256;
+            const int64_t per = (nt + kAccThreads - 1) / kAccThreads;
             const int64_t a0 = min(nt, tid * per), a1 = min(nt, a0 + per);
             double local = 0.0;
             for (int64_t t = a0; t < a1; ++t) local += tile_sums[t];
@@ -1063,7 +1067,7 @@ __global__ void __launch_bounds__(256, kStream ? 3 : 2) speculative_accept_kerne
             __syncthreads();
             const bool aborted = kStream && s_abort != 0;  // every stage wait has ended by now
             double before = 0.0, ctotal = 0.0;
-            for (int w = 0; w < 8; ++w) {
+            for (int w = 0; w < kAccWarps; ++w) {
                 if (w < wid) before += sums[w];
                 ctotal += sums[w];
             }
@@ -1272,7 +1276,7 @@ int accept_info(int device, int64_t vocab, AcceptInfo& out) {
                 attr[0].val.clusterDim.y = 1;
                 attr[0].val.clusterDim.z = 1;
                 cfg.gridDim = dim3(c * sms);
-                cfg.blockDim = dim3(256);
+                cfg.blockDim = dim3(kAccThreads);
                 cfg.dynamicSmemBytes = smem;
                 cfg.attrs = attr;
                 cfg.numAttrs = 1;
@@ -1762,8 +1766,8 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     // rows split c ways, plus the serial part of a sequence (the acceptance tests, its rows' norms,
     // the first chunk's latency, two cluster barriers, the walk) that every CTA of the cluster
     // waits through.  sigma = kAcceptSerialBytes / row bytes: measured on B200 at V = 248,320 bf16,
-    // one CTA streams a sequence's target and draft rows in about 86 us and the serial part takes
-    // about 13 us, as long as streaming 77.5 KB of one row.
+    // one CTA streams a sequence's target and draft rows in about 70 us and the serial part takes
+    // about 15 us, as long as streaming 109 KB of one row.
     // Rows stream through shared memory when every bulk copy can be 16-byte aligned and sized.
     const auto aligned = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
     const bool streamed = aligned(target_logits) && aligned(draft_logits) && aligned(masks) &&
@@ -1775,7 +1779,7 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     else if (dtype == BMS_BFLOAT16) BMS_SPEC_INFO(__nv_bfloat16);
     else BMS_SPEC_INFO(__half);
 #undef BMS_SPEC_INFO
-    constexpr double kAcceptSerialBytes = 77500.0;
+    constexpr double kAcceptSerialBytes = 109000.0;
     const double sigma = kAcceptSerialBytes / (static_cast<double>(vocab) * static_cast<double>(eb));
     int ci = -1;
     double best = 0.0;
@@ -1800,7 +1804,7 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(static_cast<unsigned>(clusters * csize));
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(kAccThreads);
     cfg.dynamicSmemBytes = accept_smem_bytes(vocab, csize, streamed);
     cfg.stream = static_cast<cudaStream_t>(stream);
     cfg.attrs = attr;
