@@ -224,3 +224,44 @@ def test_rows_that_cannot_be_bulk_copied_agree_with_the_restated_rule(vocab):
             assert dist[tok[s]] > 0 and min(abs(ur[s] - lo), abs(ur[s] - hi)) <= 1e-5, (s, tok[s], t)
         checked += 1
     assert checked >= seqs - 2
+
+
+@pytest.mark.parametrize("vocab", [4096, 4104])
+def test_long_draft_windows_in_half_precision_agree_with_the_restated_rule(vocab):
+    """K = 40 drafts take two 32-lane ballot passes of the acceptance tests; fp16 logits; V = 4096
+    streams through shared memory, V = 4104 (129 mask words) takes the register path.  A close
+    draft model keeps many sequences accepting past position 32."""
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rng = np.random.default_rng(vocab + 40)
+    seqs, k, temp = 12, 40, 1.0
+    rows = seqs * (k + 1)
+    valid = rng.random((rows, vocab)) < 0.7
+    masks = wl.pack_bits_np(valid)
+    tvals = (rng.standard_normal((rows, vocab), dtype=np.float32) * np.float32(0.3)).astype(np.float16)
+    dvals = (tvals.astype(np.float32).reshape(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab)
+             + rng.standard_normal((seqs * k, vocab), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    tf, df = tvals.astype(np.float32), dvals.astype(np.float32)
+    proposals = np.zeros((seqs, k), dtype=np.int64)
+    lengths = rng.integers(30, k + 1, size=seqs).astype(np.int32)
+    for s in range(seqs):
+        for i in range(lengths[s]):
+            proposals[s, i] = rng.choice(vocab, p=oracle.masked_softmax(df[s * k + i], masks[s * (k + 1) + i], temp))
+    ua, ur = rng.random((seqs, k)), rng.random(seqs)
+    out = speculative_accept(torch.from_numpy(tvals).cuda(), torch.from_numpy(dvals).cuda(),
+                             torch.from_numpy(masks).cuda(), torch.from_numpy(proposals).cuda(),
+                             torch.from_numpy(lengths).cuda(), temperature=temp,
+                             accept_uniforms=torch.from_numpy(ua).cuda(), resample_uniforms=torch.from_numpy(ur).cuda())
+    acc, tok, kind, st = (t.cpu().numpy() for t in (out.accept_len, out.token, out.kind, out.status))
+    assert (st == 0).all()
+    want = oracle.speculative_accept(tf, df, masks, proposals, lengths, temp, ua, ur)
+    checked = 0
+    for s, (j, t, kd, margin, dist) in enumerate(want):
+        if margin < 1e-5:
+            continue
+        assert acc[s] == j and kind[s] == kd, s
+        if tok[s] != t:
+            cum = np.cumsum(dist)
+            lo, hi = cum[tok[s]] - dist[tok[s]], cum[tok[s]]
+            assert dist[tok[s]] > 0 and min(abs(ur[s] - lo), abs(ur[s] - hi)) <= 1e-5, (s, tok[s], t)
+        checked += 1
+    assert checked >= seqs - 2 and (acc > 32).any()
