@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--prompts", type=int, default=32, help="prompts for the decode workload")
     ap.add_argument("--new-tokens", type=int, default=256, help="tokens generated per prompt (decode workload)")
     ap.add_argument("--seqs", type=int, default=256, help="verification sequences per GPU")
+    ap.add_argument("--draft-noise", type=float, default=0.7,
+                    help="stochastic workload: std of the noise between target and draft logits")
     ap.add_argument("--rows", type=int, default=8192, help="rows per GPU for the scale workload")
     ap.add_argument("--sample-rows", type=int, default=8,
                     help="rows per sampling batch (the 8 configuration rows tiled, fresh uniforms)")
@@ -985,9 +987,13 @@ def run_stochastic(args):
     """Stochastic speculative acceptance at the verification round's shape: 256 sequences x K = 8
     drafts (``--seqs``), target rows bf16 N(0, 3^2) with the round's masks, draft rows = the target's
     first K rows of each sequence plus N(0, 0.7^2) noise (a close draft model), drafts sampled from
-    the draft's masked softmax at T = 0.8 with the batched sampler.  One step = the target and draft
-    rows' sampler partials (two selection launches) and the acceptance kernel, on device-resident
-    inputs; rows/s counts target rows.  No reference implementation exists (the reference's
+    the draft's masked softmax at T = 0.8 with the batched sampler.  One step = one round through
+    ``speculative_accept`` on device-resident inputs: the target and draft rows' sampler partials
+    (two selection launches) and the acceptance kernel; rows/s counts the round's target rows.  The
+    lazy round (``lazy=True``: one launch normalising only the positions it consumes, up to the
+    first rejection) is timed beside it, with the bytes it must read (each consumed position's
+    target and draft rows and mask row, then the sampled rows again).  ``--draft-noise`` sets how
+    close the draft model is (smaller: longer accepted runs).  No reference implementation exists (the reference's
     contract is greedy), so there is no reference arm; the CPU figure is this rule restated in fp64
     (``oracle.speculative_accept``) on a few sequences."""
     import numpy as np
@@ -1007,7 +1013,8 @@ def run_stochastic(args):
     words = masks.shape[1]
     g = torch.Generator(device=device).manual_seed(7)
     first_k = logits.view(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab)
-    draft = (first_k.float() + 0.7 * torch.randn(first_k.shape, generator=g, device=device)).to(torch.bfloat16)
+    draft = (first_k.float() + args.draft_noise * torch.randn(first_k.shape, generator=g, device=device)).to(
+        torch.bfloat16)
     del first_k
     dmasks = masks.view(seqs, k + 1, words)[:, :k].reshape(seqs * k, words).contiguous()
     native = load_extension()
@@ -1017,9 +1024,9 @@ def run_stochastic(args):
     ua = torch.rand((seqs, k), dtype=torch.float64, generator=g, device=device)
     ur = torch.rand(seqs, dtype=torch.float64, generator=g, device=device)
 
-    def step():
+    def step(lazy=False):
         return speculative_accept(logits, draft, masks, proposals, lengths, temperature=temp, accept_uniforms=ua,
-                                  resample_uniforms=ur)
+                                  resample_uniforms=ur, lazy=lazy)
     out = step()
     # Untimed check against the fp64 restatement on the first sequences.
     n_chk = 6
@@ -1031,15 +1038,27 @@ def run_stochastic(args):
     for s_, (j, _, _, margin, _) in enumerate(want):
         if margin > 1e-5 and acc[s_] != j:
             raise SystemExit("stochastic acceptance differs from the restated rule")
+    lazy_out = step(lazy=True)
+    same = float((lazy_out.accept_len == out.accept_len).logical_and(lazy_out.token == out.token).double().mean().item())
     with ClockSampler(local) as clocks:
         for _ in range(max(3, args.warmup)):
             step()
         torch.cuda.nvtx.range_push("timed")
         seconds = timed_loop(step, args.steps, device)
         torch.cuda.nvtx.range_pop()
+        for _ in range(3):
+            step(lazy=True)
+        seconds_lazy = timed_loop(lambda: step(lazy=True), args.steps, device)
     per_step = seconds / args.steps
     rows = seqs * (k + 1)
     algorithmic = (rows + seqs * k) * (vocab * 2 + words * 4 + 32) + seqs * 2 * vocab * 2
+    # Bytes the lazy launch reads: positions 0..j of each sequence (target row, mask row, and the
+    # draft row below L), then the sampled target row, its mask row and, for a replacement, the
+    # draft row again.
+    row_b, mask_b = vocab * 2, words * 4
+    jj, ll = acc.astype(np.int64), lengths.cpu().numpy().astype(np.int64)
+    lazy_bytes = int(((jj + 1) * (row_b + mask_b) + np.minimum(jj + 1, ll) * row_b
+                      + row_b + mask_b + (jj < ll) * row_b).sum())
     t0 = time.perf_counter()
     oracle.speculative_accept(tf, df, masks[: n_chk * (k + 1)].cpu().numpy(), proposals[:n_chk].cpu().numpy(),
                               lengths[:n_chk].cpu().numpy(), temp, ua[:n_chk].cpu().numpy(), ur[:n_chk].cpu().numpy())
@@ -1049,13 +1068,17 @@ def run_stochastic(args):
         "metric": "rows/s", "value": rows / per_step, "unit": "rows/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, generated on device)",
-        "config": {"workload": (f"stochastic: {seqs} sequences x K={k} drafts sampled from a draft model at T={temp}, "
-                                f"V={vocab} bf16, verification-round masks; target rows/s"),
+        "config": {"workload": (f"stochastic: {seqs} sequences x K={k} drafts sampled from a draft model at T={temp} "
+                                f"(draft = target + N(0, {args.draft_noise}^2)), V={vocab} bf16, "
+                                "verification-round masks; target rows/s"),
                    "rows_per_gpu": rows, "draft_rows": seqs * k},
         "roofline": {"bound": "hbm", "achieved": algorithmic / per_step / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": algorithmic / per_step / 1e9 / peak, "peak_kind": peak_kind,
                      "kernel": "whole step (two sampler-partials launches + acceptance kernel)",
                      "bytes_per_step": algorithmic},
+        "lazy": {"ms_per_step": seconds_lazy / args.steps * 1e3, "bytes_per_step": lazy_bytes,
+                 "frac": lazy_bytes / (seconds_lazy / args.steps) / 1e9 / peak,
+                 "same_accept_len_and_token": same},
         "gpu_launches": 3 * args.steps, "clocks": clocks.summary(),
         "acceptance_rate": float(out.accept_len.double().mean().item()) / k,
         "cpu_baseline": {"value": cpu_rows, "unit": "rows/s", "cores": 1, "kind": "port",

@@ -12,7 +12,8 @@ Device work per round: the selection kernel's sampler partials (row max and mass
 pass) for the target rows and the draft rows -- the draft rows read the round's mask rows through
 a table (``bms_shard_partials_indexed``), no gathered copy -- then ``bms_speculative_accept`` (a
 cluster of 1-8 CTAs per sequence: the acceptance tests, then an inverse-CDF pass over the one row
-that is sampled).
+that is sampled).  ``lazy=True`` instead lets that one launch stream, position by position, the
+target and draft rows to their normalisers and test each draft, stopping at the first rejection.
 """
 
 from __future__ import annotations
@@ -65,7 +66,8 @@ class SpeculativeAcceptance:
 
 
 def speculative_accept(target_logits, draft_logits, masks, proposals, lengths, *, temperature: float,
-                       accept_uniforms=None, resample_uniforms=None, generator=None) -> SpeculativeAcceptance:
+                       accept_uniforms=None, resample_uniforms=None, generator=None,
+                       lazy: bool = False) -> SpeculativeAcceptance:
     """One stochastic verification round for S sequences of up to K drafts.
 
     ``target_logits`` [S*(K+1), V] (row s*(K+1)+i scores position i of sequence s), ``draft_logits``
@@ -74,6 +76,13 @@ def speculative_accept(target_logits, draft_logits, masks, proposals, lengths, *
     models at position i; ``proposals`` int64 [S, K]; ``lengths`` int32 [S].  Uniforms float64
     ``accept_uniforms`` [S, K] and ``resample_uniforms`` [S] are drawn from ``generator`` when not
     given.  No host synchronization.
+
+    By default the sampler partials of every target and draft row come first (two selection
+    launches), then the acceptance kernel.  ``lazy=True`` (rows and mask rows 16-byte aligned, rows a
+    multiple of 16 bytes, mask rows a multiple of 4 words): one launch computes the normalisers of
+    only the positions it consumes, stopping at the first rejection -- fewer bytes, but each
+    sequence's positions run one after another, so it pays when accepted runs are short.  Both
+    follow the same rule; they can differ only where a uniform sits within rounding of a decision.
     """
     import torch
     temperature = temperature_input(temperature)
@@ -92,12 +101,19 @@ def speculative_accept(target_logits, draft_logits, masks, proposals, lengths, *
         raise ValueError("masks must be a contiguous int32 [S*(K+1), ceil(V/32)] tensor")
     if proposals.dtype != torch.int64 or lengths.dtype != torch.int32 or tuple(lengths.shape) != (seqs,):
         raise ValueError("proposals must be int64 [S, K] and lengths int32 [S]")
-    backend = NativeShardBackend()
-    tpart, _ = backend.partials(target_logits.contiguous(), masks, 0, temperature)
-    qpart = None
-    if seqs * k:
-        qpart, _ = backend.partials(draft_logits.contiguous(), masks, 0, temperature,
-                                    mask_rows=_draft_mask_rows(seqs, k, dev))
+    target_logits, draft_logits = target_logits.contiguous(), draft_logits.contiguous()
+    tensors = (target_logits, masks) + ((draft_logits,) if draft_logits.numel() else ())
+    streamable = ((vocab * target_logits.element_size()) % 16 == 0 and words % 4 == 0
+                  and all(t.data_ptr() % 16 == 0 for t in tensors))
+    if lazy and not streamable:
+        raise ValueError("lazy acceptance needs 16-byte aligned rows of a multiple of 16 bytes and mask rows "
+                         "of a multiple of 4 words")
+    tpart = qpart = None
+    if not lazy:
+        backend = NativeShardBackend()
+        tpart, _ = backend.partials(target_logits, masks, 0, temperature)
+        if seqs * k:
+            qpart, _ = backend.partials(draft_logits, masks, 0, temperature, mask_rows=_draft_mask_rows(seqs, k, dev))
     if accept_uniforms is None:
         accept_uniforms = torch.rand((seqs, k), dtype=torch.float64, device=dev, generator=generator)
     if resample_uniforms is None:
@@ -115,7 +131,7 @@ def speculative_accept(target_logits, draft_logits, masks, proposals, lengths, *
     ptr = (lambda t: None if t is None or t.numel() == 0 else t.data_ptr())
     _native.check(_native.library().bms_speculative_accept(
         target_logits.data_ptr(), ptr(draft_logits), dtype, masks.data_ptr(), seqs, k + 1, vocab, ptr(proposals),
-        lengths.data_ptr(), tpart.data_ptr(), ptr(qpart), temperature, ptr(accept_uniforms),
+        lengths.data_ptr(), ptr(tpart), ptr(qpart), temperature, ptr(accept_uniforms),
         resample_uniforms.data_ptr(), out.accept_len.data_ptr(), out.token.data_ptr(), out.kind.data_ptr(),
         out.status.data_ptr(), dev.index, torch.cuda.current_stream(dev).cuda_stream))
     return out

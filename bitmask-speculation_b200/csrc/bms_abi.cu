@@ -749,6 +749,47 @@ __device__ __forceinline__ void unpack8(const Pack8<T>& p, float (&x)[8]) {
     }
 }
 
+// Online normaliser of a row's valid tokens, 8 consecutive logits at a time: m is the lane's running
+// maximum, s the mass 2^((x - m) sc) of its tokens so far (fp64; each group of 8 summed in fp32
+// first).  Invalid tokens enter as -inf.  A NaN or +inf valid logit leaves s meaningless; the row's
+// status reports it.
+__device__ __forceinline__ void norm_update8(const float (&x)[8], uint32_t bits, float sc, float& m, double& s) {
+    const float kInf = __int_as_float(0x7F800000);
+    float v[8];
+    float tmax = -kInf;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] = ((bits >> i) & 1u) ? x[i] : -kInf;
+        tmax = fmaxf(tmax, v[i]);
+    }
+    if (tmax > m) {
+        s *= static_cast<double>(ptx::ex2((m - tmax) * sc));
+        m = tmax;
+    }
+    if (m > -kInf && m < kInf) {
+        const uint64_t sc2 = ptx::pack2(sc, sc), nm = ptx::pack2(-m, -m);
+        float w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            float t0, t1;
+            ptx::unpack2(ptx::mul2(ptx::add2(ptx::pack2(v[i], v[i + 1]), nm), sc2), t0, t1);
+            w[i] = ptx::ex2(t0);
+            w[i + 1] = ptx::ex2(t1);
+        }
+        s += static_cast<double>(sum8(w));
+    }
+}
+
+// Merge of two (maximum, mass relative to it) parts of a row into (m, s).
+__device__ __forceinline__ void norm_merge(float& m, double& s, float m2, double s2, float sc) {
+    const float kInf = __int_as_float(0x7F800000);
+    const float M = fmaxf(m, m2);
+    const double a = m > -kInf ? s * static_cast<double>(ptx::ex2((m - M) * sc)) : 0.0;
+    const double b = m2 > -kInf ? s2 * static_cast<double>(ptx::ex2((m2 - M) * sc)) : 0.0;
+    m = M;
+    s = a + b;
+}
+
 // Acceptance tests of one sequence (one warp, 32 drafts per pass): the first position j whose
 // draft is rejected (u_i q_i(d_i) >= p_i(d_i), a token outside the mask or a row that cannot be
 // sampled), or L when all L drafts are accepted, and the status of that position's rows.
@@ -828,7 +869,17 @@ constexpr int kAccStageBytes = 2 * kAccRowBytes + kAccRowBytes / 16;
 // from the same pushed values), so the hardware cluster barriers always complete.  A stage wait
 // that gives up (bounded, about a second) latches an abort: the CTA pushes the flag with its total,
 // the cluster reports kTimeout for the sequence, and the CTA lets its copies land before it exits.
-template <typename T, bool kStream>
+//
+// kLazy (streamed only; tpart and qpart unused): the row normalisers are computed here, only for the
+// positions the procedure consumes.  For i = 0, 1, ... the cluster streams target row i and draft
+// row i (only the target row at i = L), each CTA keeping an online (max, mass) per lane, reduces
+// them per CTA and exchanges them over distributed shared memory (identical merges in every CTA),
+// and tests draft i -- stopping at the first rejection, so a round reads the rows up to the first
+// rejection plus the sampled row again, not all 2K + 1 rows.  Thread 0 reads the test's inputs
+// (the draft token, its mask bit, both logits, the uniform) while the rows stream.  The statuses
+// follow the sampler partials: NaN anywhere in the row, a +inf valid logit, no valid token, no
+// finite mass.
+template <typename T, bool kStream, bool kLazy = false>
 __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_accept_kernel(
     const T* __restrict__ target, const T* __restrict__ draft, const int32_t* __restrict__ masks, int64_t seqs,
     int64_t rows_per_seq, int64_t vocab, const int64_t* __restrict__ proposals, const int32_t* __restrict__ lengths,
@@ -847,6 +898,17 @@ __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_acce
     __shared__ int32_t s_j, s_code, s_last, s_cut_past, s_claim;
     __shared__ int64_t s_token, s_tile;
     __shared__ double s_prefix;
+    // kLazy: per CTA of the cluster its normalisers {Mt, count, flags, Mq}, {St, Sq}, by pass parity
+    // (a peer's next push cannot overtake a read of this pass's slot); the draft test's inputs by
+    // pass parity; per-warp partial normalisers.
+    __shared__ uint4 s_norm[kLazy ? 2 : 1][kAcceptCluster][2];
+    __shared__ double s_tu[2];
+    __shared__ float s_txt[2], s_txq[2];
+    __shared__ int32_t s_tbit[2];
+    __shared__ float s_wm[2][kAccWarps];
+    __shared__ double s_ws[2][kAccWarps];
+    __shared__ uint32_t s_wcnt[kAccWarps], s_wfl[kAccWarps];
+    static_assert(!kLazy || kStream, "lazy normalisers stream their rows");
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const uint32_t crank = ptx::cluster_ctarank(), csize = ptx::cluster_nctarank();
     const int64_t K = rows_per_seq - 1, words = (vocab + 31) / 32;
@@ -868,28 +930,227 @@ __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_acce
     }
     __syncthreads();
     uint32_t gbase = 0;  // chunks this CTA has streamed so far (every thread counts them alike)
+    // kStream: streams this CTA's tokens [r0 * 256, min(r1 * 256, V)) of a target row -- with
+    // `with_q` also of a draft row -- and their mask words through the stages, kTok tokens a chunk
+    // (chunk c in stage (gbase + c) % kAccStages), and calls consume(stage, t0, ntc) in every warp
+    // for every chunk (ntc = the chunk's 256-token tiles).  Every chunk starts on a tile; its byte
+    // counts are multiples of 16 (the host streams only rows of a multiple of 16 bytes and mask rows
+    // of a multiple of 4 words).  Thread 0 refills a stage once all warps have read its previous
+    // chunk (the warps run up to kAccStages - 1 chunks apart; a warp ahead waits only on a full
+    // barrier of a chunk already issued).  A wait that gives up latches s_abort.
+    constexpr int64_t kTok = kAccRowBytes / sizeof(T);
+    constexpr int kPerWarp = static_cast<int>(kTok / 256 / kAccWarps);  // tiles per warp and chunk: 2 (16-bit), 1
+    static_assert(kPerWarp * 256 * kAccWarps == kTok, "a chunk is whole tiles per warp");
+    auto stream_pass = [&](const T* rt, const T* rq, const int32_t* mr, bool with_q, auto&& consume) {
+        const int64_t A = r0 * 256, B = min(r1 * 256, vocab);
+        const int64_t n = B > A ? (B - A + kTok - 1) / kTok : 0;
+        auto issue = [&](int64_t c) {
+            const uint32_t G = gbase + static_cast<uint32_t>(c), st = G % kAccStages, use = G / kAccStages;
+            if (use > 0 && !wait_bounded(ptx::smem_addr(&s_empty[st]), (use - 1u) & 1u, &s_abort)) return;
+            const int64_t t0 = A + c * kTok, t1 = min(B, t0 + kTok);
+            const uint32_t tb = static_cast<uint32_t>((t1 - t0) * static_cast<int64_t>(sizeof(T)));
+            const uint32_t mb = static_cast<uint32_t>(((t1 + 31) / 32 - t0 / 32) * 4);
+            const uint32_t bar = ptx::smem_addr(&s_full[st]);
+            const uint32_t dst = ptx::smem_addr(accept_smem + st * kAccStageBytes);
+            ptx::mbar_arrive_expect_tx(bar, tb * (with_q ? 2u : 1u) + mb);
+            ptx::bulk_load(dst, rt + t0, tb, bar);
+            if (with_q) ptx::bulk_load(dst + kAccRowBytes, rq + t0, tb, bar);
+            ptx::bulk_load(dst + 2 * kAccRowBytes, mr + t0 / 32, mb, bar);
+            ++s_issued[st];
+        };
+        if (tid == 0 && !s_abort)
+            for (int64_t c = 0; c < n && c < kAccStages; ++c) issue(c);
+        for (int64_t c = 0; c < n; ++c) {
+            const uint32_t G = gbase + static_cast<uint32_t>(c), st = G % kAccStages;
+            if (wait_bounded(ptx::smem_addr(&s_full[st]), (G / kAccStages) & 1u, &s_abort)) {
+                const int64_t t0 = A + c * kTok;
+                consume(static_cast<const uint8_t*>(accept_smem + st * kAccStageBytes), t0,
+                        (min(B, t0 + kTok) - t0 + 255) / 256);
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&s_empty[st]));
+            if (tid == 0 && c + kAccStages < n && !s_abort) issue(c + kAccStages);
+        }
+        gbase += static_cast<uint32_t>(n);
+    };
     for (int64_t seq = ptx::cluster_id_x(); seq < seqs; seq += ptx::ncluster_x()) {
         const int32_t L = lengths[seq];
-        if (wid == 0) {
-            int32_t j, code;
-            accept_prefix<T>(target, draft, masks, seq, rows_per_seq, vocab, proposals, L, tpart, qpart, u_accept, sc,
-                             lane, j, code);
-            if (lane == 0) {
-                s_j = j;
-                s_code = code;
+        int32_t j = -1, code = kOk;
+        RowNorm tn{0.0f, 1.0, kOk, 1.0}, qn{0.0f, 1.0, kOk, 1.0};
+        bool residual0;
+        if constexpr (kLazy) {
+            const float kInf = __int_as_float(0x7F800000);
+            if (L < 0 || L > K) {
+                j = 0;
+                code = kBadLength;
+            }
+            for (int32_t i = 0; j < 0; ++i) {
+                const bool with_q = i < L;  // position L: the bonus row, target only
+                const int slot = i & 1;
+                const int64_t ti = seq * rows_per_seq + i, qi = seq * K + i;
+                if (tid == 32 && with_q) {  // draft i's test inputs, read while the rows stream
+                    const int64_t d = proposals[qi];
+                    int32_t bit = 0;
+                    float xt = 0.0f, xq = 0.0f;
+                    if (d >= 0 && d < vocab) {
+                        bit = static_cast<int32_t>((static_cast<uint32_t>(masks[ti * words + (d >> 5)]) >> (d & 31)) & 1u);
+                        xt = Elem<T>::load(target, ti * vocab + d);
+                        xq = Elem<T>::load(draft, qi * vocab + d);
+                    }
+                    s_tbit[slot] = bit;
+                    s_txt[slot] = xt;
+                    s_txq[slot] = xq;
+                    s_tu[slot] = u_accept[qi];
+                }
+                float mt = -kInf, mq = -kInf;
+                double stl = 0.0, sql = 0.0;
+                uint32_t cnt = 0u;
+                typename Elem<T>::NanAcc nant = Elem<T>::nan_init(), nanq = Elem<T>::nan_init();
+                bool tnan = false, qnan = false;  // NaN among the row's last partial group
+                stream_pass(target + ti * vocab, draft + qi * vocab, masks + ti * words, with_q,
+                            [&](const uint8_t* stage, int64_t t0, int64_t ntc) {
+#pragma unroll
+                    for (int k = 0; k < kPerWarp; ++k) {
+                        const int64_t tl = wid + kAccWarps * k;
+                        const int64_t off = tl * 256 + 8 * lane, a = t0 + off;
+                        if (tl < ntc && a < vocab) {
+                            uint32_t bits =
+                                (reinterpret_cast<const uint32_t*>(stage + 2 * kAccRowBytes)[off >> 5] >> (off & 31)) & 0xFFu;
+                            const bool tail = a + 8 > vocab;
+                            if (tail) bits &= (1u << (vocab - a)) - 1u;
+                            cnt += __popc(bits);
+                            Pack8<T> pk;
+                            float x[8];
+#pragma unroll
+                            for (int w = 0; w < Elem<T>::kBytes / 2; ++w)
+                                pk.w[w] = reinterpret_cast<const uint4*>(stage + off * sizeof(T))[w];
+                            unpack8<T>(pk, x);
+                            if (!tail) {
+#pragma unroll
+                                for (int w = 0; w < Elem<T>::kBytes / 2; ++w) Elem<T>::nan_update(nant, pk.w[w]);
+                            } else {
+                                for (int e = 0; e < 8; ++e) tnan |= a + e < vocab && x[e] != x[e];
+                            }
+                            norm_update8(x, bits, sc, mt, stl);
+                            if (with_q) {
+#pragma unroll
+                                for (int w = 0; w < Elem<T>::kBytes / 2; ++w)
+                                    pk.w[w] = reinterpret_cast<const uint4*>(stage + kAccRowBytes + off * sizeof(T))[w];
+                                unpack8<T>(pk, x);
+                                if (!tail) {
+#pragma unroll
+                                    for (int w = 0; w < Elem<T>::kBytes / 2; ++w) Elem<T>::nan_update(nanq, pk.w[w]);
+                                } else {
+                                    for (int e = 0; e < 8; ++e) qnan |= a + e < vocab && x[e] != x[e];
+                                }
+                                norm_update8(x, bits, sc, mq, sql);
+                            }
+                        }
+                    }
+                });
+                // Lanes -> warp -> CTA (the same merge order in every thread), then every CTA's
+                // normalisers to every CTA of the cluster.
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) {
+                    norm_merge(mt, stl, __shfl_xor_sync(0xFFFFFFFFu, mt, o), __shfl_xor_sync(0xFFFFFFFFu, stl, o), sc);
+                    norm_merge(mq, sql, __shfl_xor_sync(0xFFFFFFFFu, mq, o), __shfl_xor_sync(0xFFFFFFFFu, sql, o), sc);
+                }
+                cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+                const uint32_t wfl = (__any_sync(0xFFFFFFFFu, tnan || Elem<T>::has_nan(nant)) ? 1u : 0u) |
+                                     (__any_sync(0xFFFFFFFFu, qnan || Elem<T>::has_nan(nanq)) ? 2u : 0u);
+                if (lane == 0) {
+                    s_wm[0][wid] = mt;
+                    s_ws[0][wid] = stl;
+                    s_wm[1][wid] = mq;
+                    s_ws[1][wid] = sql;
+                    s_wcnt[wid] = cnt;
+                    s_wfl[wid] = wfl;
+                }
+                __syncthreads();
+                if (tid < static_cast<int>(csize)) {
+                    float Mt = s_wm[0][0], Mq = s_wm[1][0];
+                    double St = s_ws[0][0], Sq = s_ws[1][0];
+                    uint32_t ccnt = s_wcnt[0], cfl = s_wfl[0];
+                    for (int w = 1; w < kAccWarps; ++w) {
+                        norm_merge(Mt, St, s_wm[0][w], s_ws[0][w], sc);
+                        norm_merge(Mq, Sq, s_wm[1][w], s_ws[1][w], sc);
+                        ccnt += s_wcnt[w];
+                        cfl |= s_wfl[w];
+                    }
+                    if (s_abort) cfl |= 4u;
+                    uint32_t sw[4];
+                    memcpy(&sw[0], &St, 8);
+                    memcpy(&sw[2], &Sq, 8);
+                    const uint32_t peer = static_cast<uint32_t>(tid);
+                    ptx::st_cluster_v4(ptx::mapa(ptx::smem_addr(&s_norm[slot][crank][0]), peer), __float_as_uint(Mt),
+                                       ccnt, cfl, __float_as_uint(Mq));
+                    ptx::st_cluster_v4(ptx::mapa(ptx::smem_addr(&s_norm[slot][crank][1]), peer), sw[0], sw[1], sw[2],
+                                       sw[3]);
+                }
+                ptx::cluster_arrive();
+                ptx::cluster_wait();
+                {
+                    float Mt = -kInf, Mq = -kInf;
+                    double St = 0.0, Sq = 0.0;
+                    uint32_t rcnt = 0u, rfl = 0u;
+                    for (uint32_t q = 0; q < csize; ++q) {
+                        const uint4 h = s_norm[slot][q][0], v = s_norm[slot][q][1];
+                        double a, b;
+                        const uint32_t va[2] = {v.x, v.y}, vb[2] = {v.z, v.w};
+                        memcpy(&a, va, 8);
+                        memcpy(&b, vb, 8);
+                        norm_merge(Mt, St, __uint_as_float(h.x), a, sc);
+                        norm_merge(Mq, Sq, __uint_as_float(h.w), b, sc);
+                        rcnt += h.y;
+                        rfl |= h.z;
+                    }
+                    auto make_norm = [&](float M, double S, bool nan) -> RowNorm {
+                        RowNorm r{M, S, kOk, S > 0.0 ? 1.0 / S : 0.0};
+                        r.code = (rfl & 4u) ? kTimeout : nan ? kNaN : (M == kInf) ? kPosInf : (rcnt == 0u) ? kEmpty
+                                 : (M == -kInf || !(S > 0.0)) ? kNoMass : kOk;
+                        return r;
+                    };
+                    tn = make_norm(Mt, St, (rfl & 1u) != 0u);
+                    qn = make_norm(Mq, Sq, (rfl & 2u) != 0u);
+                }
+                if (!with_q) {
+                    j = i;
+                    code = tn.code;
+                    break;
+                }
+                const int32_t c = tn.code != kOk ? tn.code : qn.code;
+                bool ok = false;
+                if (c == kOk && s_tbit[slot]) {
+                    const double p = spec_weight(s_txt[slot], tn, sc), q = spec_weight(s_txq[slot], qn, sc);
+                    ok = q > 0.0 && s_tu[slot] * q < p;
+                }
+                if (!ok) {
+                    j = i;
+                    code = c;
+                }
+            }
+            residual0 = code == kOk && j < L;
+        } else {
+            if (wid == 0) {
+                int32_t jw, cw;
+                accept_prefix<T>(target, draft, masks, seq, rows_per_seq, vocab, proposals, L, tpart, qpart, u_accept,
+                                 sc, lane, jw, cw);
+                if (lane == 0) {
+                    s_j = jw;
+                    s_code = cw;
+                }
+            }
+            __syncthreads();
+            j = s_j;
+            code = s_code;
+            residual0 = code == kOk && j < L;
+            if (code == kOk) {
+                tn = row_norm(tpart[seq * rows_per_seq + j]);
+                code = tn.code;
+                if (residual0) qn = row_norm(qpart[seq * K + j]);  // usable: its acceptance test ran
             }
         }
-        __syncthreads();
-        const int32_t j = s_j;
-        int32_t code = s_code;
-        const bool residual0 = code == kOk && j < L;
         const int64_t trow = seq * rows_per_seq + j;
-        RowNorm tn{0.0f, 1.0, kOk, 1.0}, qn{0.0f, 1.0, kOk, 1.0};
-        if (code == kOk) {
-            tn = row_norm(tpart[trow]);
-            code = tn.code;
-            if (residual0) qn = row_norm(qpart[seq * K + j]);  // usable: its acceptance test ran
-        }
         const double ratio = residual0 && code == kOk ? tn.S / qn.S : 0.0;  // S_t / S_q, in [1/V, V]
         const float rhi = static_cast<float>(ratio), rlo = static_cast<float>(ratio - static_cast<double>(rhi));
         const T* trow_p = target + trow * vocab;
@@ -910,95 +1171,58 @@ __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_acce
                 return static_cast<double>(sum8(w));
             };
             if constexpr (kStream) {
-                // This CTA's tokens [A, B) in chunks of kTok tokens, chunk c in stage (gbase + c) %
-                // kAccStages.  Every chunk starts on a 256-token tile; its byte counts are multiples
-                // of 16 (the host streams only rows of a multiple of 16 bytes and mask rows of a
-                // multiple of 4 words).
-                constexpr int64_t kTok = kAccRowBytes / sizeof(T);
-                const int64_t A = r0 * 256, B = min(r1 * 256, vocab);
-                const int64_t n = B > A ? (B - A + kTok - 1) / kTok : 0;
-                // Thread 0 refills a stage once all eight warps have read its previous chunk (the
-                // warps run up to kAccStages - 1 chunks apart; a warp ahead waits only on a full
-                // barrier of a chunk already issued).
-                auto issue = [&](int64_t c) {
-                    const uint32_t G = gbase + static_cast<uint32_t>(c), st = G % kAccStages, use = G / kAccStages;
-                    if (use > 0 && !wait_bounded(ptx::smem_addr(&s_empty[st]), (use - 1u) & 1u, &s_abort)) return;
-                    const int64_t t0 = A + c * kTok, t1 = min(B, t0 + kTok);
-                    const uint32_t tb = static_cast<uint32_t>((t1 - t0) * static_cast<int64_t>(sizeof(T)));
-                    const uint32_t mb = static_cast<uint32_t>(((t1 + 31) / 32 - t0 / 32) * 4);
-                    const uint32_t bar = ptx::smem_addr(&s_full[st]);
-                    const uint32_t dst = ptx::smem_addr(accept_smem + st * kAccStageBytes);
-                    ptx::mbar_arrive_expect_tx(bar, tb * (residual ? 2u : 1u) + mb);
-                    ptx::bulk_load(dst, trow_p + t0, tb, bar);
-                    if (residual) ptx::bulk_load(dst + kAccRowBytes, qrow_p + t0, tb, bar);
-                    ptx::bulk_load(dst + 2 * kAccRowBytes, mrow + t0 / 32, mb, bar);
-                    ++s_issued[st];
-                };
-                if (tid == 0 && !s_abort)
-                    for (int64_t c = 0; c < n && c < kAccStages; ++c) issue(c);
-                for (int64_t c = 0; c < n; ++c) {
-                    const uint32_t G = gbase + static_cast<uint32_t>(c), st = G % kAccStages;
-                    if (wait_bounded(ptx::smem_addr(&s_full[st]), (G / kAccStages) & 1u, &s_abort)) {
-                        const uint8_t* stage = accept_smem + st * kAccStageBytes;
-                        const int64_t t0 = A + c * kTok;
-                        const int64_t ntc = (min(B, t0 + kTok) - t0 + 255) / 256;  // tiles of the chunk
-                        // fp32 lane sum of tile tl of the chunk (tokens past the vocabulary weigh 0).
-                        auto lane_tile = [&](int64_t tl) -> float {
-                            const int64_t off = tl * 256 + 8 * lane;
-                            const uint32_t word = reinterpret_cast<const uint32_t*>(stage + 2 * kAccRowBytes)[off >> 5];
-                            Pack8<T> pk;
-                            float xt[8], xq[8] = {}, w[8];
+                const int64_t A = r0 * 256;
+                stream_pass(trow_p, qrow_p, mrow, residual, [&](const uint8_t* stage, int64_t t0, int64_t ntc) {
+                    // fp32 lane sum of tile tl of the chunk (tokens past the vocabulary weigh 0).
+                    auto lane_tile = [&](int64_t tl) -> float {
+                        const int64_t off = tl * 256 + 8 * lane;
+                        const uint32_t word = reinterpret_cast<const uint32_t*>(stage + 2 * kAccRowBytes)[off >> 5];
+                        Pack8<T> pk;
+                        float xt[8], xq[8] = {}, w[8];
+#pragma unroll
+                        for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
+                            pk.w[i] = reinterpret_cast<const uint4*>(stage + off * sizeof(T))[i];
+                        unpack8<T>(pk, xt);
+                        if (residual) {
 #pragma unroll
                             for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
-                                pk.w[i] = reinterpret_cast<const uint4*>(stage + off * sizeof(T))[i];
-                            unpack8<T>(pk, xt);
-                            if (residual) {
-#pragma unroll
-                                for (int i = 0; i < Elem<T>::kBytes / 2; ++i)
-                                    pk.w[i] = reinterpret_cast<const uint4*>(stage + kAccRowBytes + off * sizeof(T))[i];
-                                unpack8<T>(pk, xq);
-                            }
-                            weights8(t0 + off, (word >> (off & 31)) & 0xFFu, xt, xq, w);
-                            return sum8(w);
-                        };
-                        // A full chunk has kPerWarp tiles per warp: both computed in one unrolled block
-                        // (independent work to interleave), then one fp32 butterfly for both sums --
-                        // after the xor-16 step the low half-warp holds tile wid's pairs, the high half
-                        // tile wid + kAccWarps's.
-                        constexpr int kPerWarp = static_cast<int>(kTok / 256 / kAccWarps);  // 2 (16-bit), 1 (fp32)
-                        static_assert(kPerWarp * 256 * kAccWarps == kTok, "a chunk is whole tiles per warp");
-                        float sk[kPerWarp];
-                        if (ntc * 256 == kTok && t0 + kTok <= vocab) {
-#pragma unroll
-                            for (int k = 0; k < kPerWarp; ++k) sk[k] = lane_tile(wid + kAccWarps * k);
-                        } else {
-#pragma unroll
-                            for (int k = 0; k < kPerWarp; ++k) {
-                                const int64_t tl = wid + kAccWarps * k;
-                                sk[k] = tl < ntc && t0 + tl * 256 + 8 * lane < vocab ? lane_tile(tl) : 0.0f;
-                            }
+                                pk.w[i] = reinterpret_cast<const uint4*>(stage + kAccRowBytes + off * sizeof(T))[i];
+                            unpack8<T>(pk, xq);
                         }
-                        const int64_t tbase = (t0 - A) / 256;
-                        if constexpr (kPerWarp == 2) {
-                            const bool high = (lane & 16) != 0;
-                            float v = high ? sk[1] : sk[0];
-                            v += __shfl_xor_sync(0xFFFFFFFFu, high ? sk[0] : sk[1], 16);
+                        weights8(t0 + off, (word >> (off & 31)) & 0xFFu, xt, xq, w);
+                        return sum8(w);
+                    };
+                    // A full chunk has kPerWarp tiles per warp: both computed in one unrolled block
+                    // (independent work to interleave), then one fp32 butterfly for both sums --
+                    // after the xor-16 step the low half-warp holds tile wid's pairs, the high half
+                    // tile wid + kAccWarps's.
+                    float sk[kPerWarp];
+                    if (ntc * 256 == kTok && t0 + kTok <= vocab) {
 #pragma unroll
-                            for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-                            if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
-                            if (lane == 16 && wid + kAccWarps < ntc) tile_sums[tbase + wid + kAccWarps] = v;
-                        } else {
-                            float v = sk[0];
+                        for (int k = 0; k < kPerWarp; ++k) sk[k] = lane_tile(wid + kAccWarps * k);
+                    } else {
 #pragma unroll
-                            for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-                            if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
+                        for (int k = 0; k < kPerWarp; ++k) {
+                            const int64_t tl = wid + kAccWarps * k;
+                            sk[k] = tl < ntc && t0 + tl * 256 + 8 * lane < vocab ? lane_tile(tl) : 0.0f;
                         }
                     }
-                    __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&s_empty[st]));
-                    if (tid == 0 && c + kAccStages < n && !s_abort) issue(c + kAccStages);
-                }
-                gbase += static_cast<uint32_t>(n);
+                    const int64_t tbase = (t0 - A) / 256;
+                    if constexpr (kPerWarp == 2) {
+                        const bool high = (lane & 16) != 0;
+                        float v = high ? sk[1] : sk[0];
+                        v += __shfl_xor_sync(0xFFFFFFFFu, high ? sk[0] : sk[1], 16);
+#pragma unroll
+                        for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+                        if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
+                        if (lane == 16 && wid + kAccWarps < ntc) tile_sums[tbase + wid + kAccWarps] = v;
+                    } else {
+                        float v = sk[0];
+#pragma unroll
+                        for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+                        if (lane == 0 && wid < ntc) tile_sums[tbase + wid] = v;
+                    }
+                });
             } else {
                 // This CTA's tile sums, kBatch tiles per warp and iteration (64 bytes a lane and row in
                 // flight): every raw 16-byte load of the batch is issued before the first weight is
@@ -1247,7 +1471,7 @@ struct AcceptInfo {
     int clusters[4] = {0, 0, 0, 0};
 };
 
-template <typename T, bool kStream>
+template <typename T, bool kStream, bool kLazy = false>
 int accept_info(int device, int64_t vocab, AcceptInfo& out) {
     static AcceptInfo table[kMaxDevices];
     int sms = 0;
@@ -1255,7 +1479,7 @@ int accept_info(int device, int64_t vocab, AcceptInfo& out) {
     std::lock_guard<std::mutex> lock(g_mutex);
     AcceptInfo& info = table[device];
     if (info.vocab != vocab) {
-        auto kernel = speculative_accept_kernel<T, kStream>;
+        auto kernel = speculative_accept_kernel<T, kStream, kLazy>;
         size_t most = 0;  // the largest size that fits: the function's dynamic shared memory limit
         for (int i = 0; i < 4; ++i) {
             const size_t smem = accept_smem_bytes(vocab, 1 << i, kStream);
@@ -1745,12 +1969,16 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     BMS_CHECK(check_ptr(target_logits, device, "target_logits", eb));
     BMS_CHECK(check_ptr(masks, device, "masks", 4));
     BMS_CHECK(check_ptr(lengths, device, "lengths", 4));
-    BMS_CHECK(check_ptr(target_partials, device, "target_partials", 16));
+    // No partials: the kernel computes the consumed positions' normalisers itself (lazy).
+    const bool lazy = target_partials == nullptr;
+    if (lazy && draft_partials != nullptr)
+        return fail(BMS_ERROR_INVALID_ARGUMENT, "target_partials and draft_partials must both be given or both be NULL");
+    if (!lazy) BMS_CHECK(check_ptr(target_partials, device, "target_partials", 16));
     BMS_CHECK(check_ptr(resample_uniforms, device, "resample_uniforms", 8));
     if (rows_per_seq > 1) {
         BMS_CHECK(check_ptr(draft_logits, device, "draft_logits", eb));
         BMS_CHECK(check_ptr(proposals, device, "proposals", 8));
-        BMS_CHECK(check_ptr(draft_partials, device, "draft_partials", 16));
+        if (!lazy) BMS_CHECK(check_ptr(draft_partials, device, "draft_partials", 16));
         BMS_CHECK(check_ptr(accept_uniforms, device, "accept_uniforms", 8));
     }
     BMS_CHECK(check_ptr(accept_len, device, "accept_len", 4));
@@ -1772,9 +2000,14 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     const auto aligned = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
     const bool streamed = aligned(target_logits) && aligned(draft_logits) && aligned(masks) &&
                         (vocab * static_cast<int64_t>(eb)) % 16 == 0 && ((vocab + 31) / 32) % 4 == 0;
+    if (lazy && !streamed)
+        return fail(BMS_ERROR_UNSUPPORTED,
+                    "without partials, rows must be 16-byte aligned multiples of 16 bytes and mask rows multiples "
+                    "of 4 words");
     AcceptInfo ai;
-#define BMS_SPEC_INFO(T)                                                                       \
-    BMS_CHECK((streamed ? accept_info<T, true>(device, vocab, ai) : accept_info<T, false>(device, vocab, ai)))
+#define BMS_SPEC_INFO(T)                                                                                      \
+    BMS_CHECK((lazy ? accept_info<T, true, true>(device, vocab, ai)                                         \
+                    : streamed ? accept_info<T, true>(device, vocab, ai) : accept_info<T, false>(device, vocab, ai)))
     if (dtype == BMS_FLOAT32) BMS_SPEC_INFO(float);
     else if (dtype == BMS_BFLOAT16) BMS_SPEC_INFO(__nv_bfloat16);
     else BMS_SPEC_INFO(__half);
@@ -1793,6 +2026,14 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
         }
     }
     if (ci < 0) return fail(BMS_ERROR_UNSUPPORTED, "vocabulary too large for the acceptance kernel");
+    // Lazy normalisers: a sequence's positions run one after another, so its chain of passes, not
+    // the rounds, sets the time -- 8 CTAs per sequence when every cluster is resident at once, else
+    // 4 (measured on B200, 256 sequences x K = 8, V = 248,320 bf16: 1 / 2 / 4 / 8 CTAs 840 / 725 /
+    // 563 / 709 us with a mean accepted run of 2.6, 368 / 330 / 284 / 382 us with 0.36).
+    if (lazy) {
+        if (ai.clusters[3] > 0 && seqs <= ai.clusters[3]) ci = 3;
+        else if (ai.clusters[2] > 0) ci = 2;
+    }
     for (int i = 0; i < 4; ++i)  // the tests' launch override (1, 2, 4 or 8 CTAs per sequence)
         if (g_force_cluster == (1 << i) && ai.clusters[i] > 0) ci = i;
     const int csize = 1 << ci;
@@ -1811,11 +2052,12 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     cfg.numAttrs = 1;
     auto tp = reinterpret_cast<const GatherSlot*>(target_partials);
     auto qp = reinterpret_cast<const GatherSlot*>(draft_partials);
-#define BMS_SPEC_S(T, S)                                                                                    \
-    cudaLaunchKernelEx(&cfg, speculative_accept_kernel<T, S>, static_cast<const T*>(target_logits),            \
+#define BMS_SPEC_S(T, S, LZ)                                                                                \
+    cudaLaunchKernelEx(&cfg, speculative_accept_kernel<T, S, LZ>, static_cast<const T*>(target_logits),        \
                        static_cast<const T*>(draft_logits), masks, seqs, rows_per_seq, vocab, proposals, lengths, tp, \
                        qp, accept_uniforms, resample_uniforms, sc, accept_len, token, kind, status)
-#define BMS_SPEC(T) (streamed ? BMS_SPEC_S(T, true) : BMS_SPEC_S(T, false))
+#define BMS_SPEC(T) \
+    (lazy ? BMS_SPEC_S(T, true, true) : streamed ? BMS_SPEC_S(T, true, false) : BMS_SPEC_S(T, false, false))
     cudaError_t launched;
     if (dtype == BMS_FLOAT32) launched = BMS_SPEC(float);
     else if (dtype == BMS_BFLOAT16) launched = BMS_SPEC(__nv_bfloat16);

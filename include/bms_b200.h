@@ -239,7 +239,10 @@ BMS_API int bms_shard_merge(const bms_partial *partials, int32_t shards, int32_t
  * masked softmax q_i at `temperature` (draft logits row s * K + i); target logits row
  * s * rows_per_seq + i gives p_i; both use mask row s * rows_per_seq + i.  The partials are
  * bms_shard_partials outputs (whole rows, token_offset 0, the same temperature) of the target rows
- * and of the draft rows.  Draft i is accepted iff accept_uniforms[s, i] * q_i(d_i) < p_i(d_i); at the
+ * and of the draft rows (bms_shard_partials_indexed for the draft rows' mask rows).  Both NULL: the
+ * kernel computes the normalisers of the positions it consumes itself, position by position up to
+ * the first rejection (rows and mask rows must then be 16-byte aligned, rows a multiple of 16 bytes,
+ * mask rows a multiple of 4 words; else BMS_ERROR_UNSUPPORTED).  Draft i is accepted iff accept_uniforms[s, i] * q_i(d_i) < p_i(d_i); at the
  * first rejection j the token is drawn by inverse CDF with resample_uniforms[s] from
  * max(0, p_j - q_j) normalised (from p_j if that rounds to zero mass), after L acceptances from p_L:
  * every emitted token is distributed as the target's masked softmax.  Outputs per sequence: accepted

@@ -120,7 +120,8 @@ def test_full_vocabulary_rounds_agree_with_the_restated_rule():
     assert checked >= seqs - 2 and (acc > 0).any() and (acc < lengths).any()
 
 
-def test_failed_and_invalid_rows_report_statuses():
+@pytest.mark.parametrize("lazy", [False, True])
+def test_failed_and_invalid_rows_report_statuses(lazy):
     from bitmask_speculation_b200.stochastic import speculative_accept
     vocab, k = 256, 2
     tvals = torch.zeros((3 * (k + 1), vocab), device="cuda")
@@ -130,14 +131,15 @@ def test_failed_and_invalid_rows_report_statuses():
     masks[3 * 1 + 0].zero_()            # sequence 1: the first row has no valid token
     lengths = torch.tensor([2, 1, 3], dtype=torch.int32, device="cuda")  # sequence 2: L > K
     out = speculative_accept(tvals, dvals, masks, torch.zeros((3, k), dtype=torch.int64, device="cuda"), lengths,
-                             temperature=1.0)
+                             temperature=1.0, lazy=lazy)
     assert out.status.cpu().tolist() == [2, 1, 6]
     with pytest.raises(ValueError, match="NaN"):
         out.events(0, [0, 0])
 
 
+@pytest.mark.parametrize("lazy", [True, False])
 @pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
-def test_results_do_not_depend_on_how_many_ctas_share_a_sequence(dtype):
+def test_results_do_not_depend_on_how_many_ctas_share_a_sequence(dtype, lazy):
     """The kernel splits each sequence's row over 8, 4, 2 or 1 CTAs (one cluster) by the batch size:
     8 sequences take 8 CTAs each, 40 take 4, 100 take 2 and 300 take one (a grid-stride loop).  The
     first 8 sequences, embedded in each batch, must give the same results every time, and those of
@@ -162,7 +164,8 @@ def test_results_do_not_depend_on_how_many_ctas_share_a_sequence(dtype):
     results = []
     for n in (8, 40, 100, 300):
         out = speculative_accept(logits[: n * (k + 1)], draft[: n * k], masks[: n * (k + 1)], proposals[:n],
-                                 lengths[:n], temperature=temp, accept_uniforms=ua[:n], resample_uniforms=ur[:n])
+                                 lengths[:n], temperature=temp, accept_uniforms=ua[:n], resample_uniforms=ur[:n],
+                                 lazy=lazy)
         assert (out.status == 0).all()
         results.append([t[:8].cpu() for t in (out.accept_len, out.token, out.kind)])
     for other in results[1:]:
@@ -265,3 +268,31 @@ def test_long_draft_windows_in_half_precision_agree_with_the_restated_rule(vocab
             assert dist[tok[s]] > 0 and min(abs(ur[s] - lo), abs(ur[s] - hi)) <= 1e-5, (s, tok[s], t)
         checked += 1
     assert checked >= seqs - 2 and (acc > 32).any()
+
+
+def test_lazy_normalisers_agree_with_full_partials():
+    """The lazy round (normalisers computed by the acceptance kernel for the consumed positions only)
+    and the round on every row's sampler partials follow the same rule: at full vocabulary they
+    agree on every sequence except where a uniform sits within rounding of a decision."""
+    from bitmask_speculation_b200.kernels._extension import load_extension
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    dev = torch.device("cuda")
+    temp, k, vocab, seqs = 0.8, wl.DRAFT_K, wl.VOCAB, 160
+    logits, masks, _, _ = wl.verify_batch_torch(seqs, seed=33, device=dev)
+    words = masks.shape[1]
+    g = torch.Generator(device=dev).manual_seed(8)
+    first_k = logits.view(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab)
+    draft = (first_k.float() + 0.3 * torch.randn(first_k.shape, generator=g, device=dev)).to(torch.bfloat16)
+    dmasks = masks.view(seqs, k + 1, words)[:, :k].reshape(seqs * k, words).contiguous()
+    u = torch.rand(seqs * k, dtype=torch.float64, generator=g, device=dev)
+    proposals = load_extension().masked_sample_batch(draft, dmasks, temp, u)[0].view(seqs, k).contiguous()
+    lengths = torch.randint(0, k + 1, (seqs,), generator=g, device=dev).to(torch.int32)
+    ua = torch.rand((seqs, k), dtype=torch.float64, generator=g, device=dev)
+    ur = torch.rand(seqs, dtype=torch.float64, generator=g, device=dev)
+    outs = [speculative_accept(logits, draft, masks, proposals, lengths, temperature=temp, accept_uniforms=ua,
+                               resample_uniforms=ur, lazy=lazy) for lazy in (True, False)]
+    for o in outs:
+        assert (o.status == 0).all()
+    same = (outs[0].accept_len == outs[1].accept_len) & (outs[0].token == outs[1].token) & (outs[0].kind == outs[1].kind)
+    assert int(same.sum()) >= seqs - 2
+    assert (outs[0].accept_len > 0).any() and (outs[0].accept_len < lengths).any()
