@@ -840,7 +840,7 @@ constexpr int kAcceptCluster = 8;  // CTAs per sequence at most (a portable clus
 // chunks of kAccRowBytes per row (target, and the draft in the residual pass; two 256-token tiles
 // per warp of 16-bit logits, one of fp32) plus the chunk's mask words, kAccStages chunks in flight
 // by 1-D bulk copies.
-constexpr int kAccWarps = 12;
+constexpr int kAccWarps = 16;  // 2 CTAs per SM (64 registers streamed): 32 warps
 constexpr int kAccThreads = 32 * kAccWarps;
 constexpr int kAccStages = 3;
 constexpr int kAccRowBytes = 1024 * kAccWarps;
