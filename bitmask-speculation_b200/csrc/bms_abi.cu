@@ -2028,8 +2028,8 @@ int bms_speculative_accept(const void* target_logits, const void* draft_logits, 
     if (ci < 0) return fail(BMS_ERROR_UNSUPPORTED, "vocabulary too large for the acceptance kernel");
     // Lazy normalisers: a sequence's positions run one after another, so its chain of passes, not
     // the rounds, sets the time -- 8 CTAs per sequence when every cluster is resident at once, else
-    // 4 (measured on B200, 256 sequences x K = 8, V = 248,320 bf16: 1 / 2 / 4 / 8 CTAs 840 / 725 /
-    // 563 / 709 us with a mean accepted run of 2.6, 368 / 330 / 284 / 382 us with 0.36).
+    // 4 (measured on B200, 256 sequences x K = 8, V = 248,320 bf16: 1 / 2 / 4 / 8 CTAs 793 / 656 /
+    // 543 / 727 us with a mean accepted run of 2.6, 335 / 297 / 266 / 374 us with 0.36).
     if (lazy) {
         if (ai.clusters[3] > 0 && seqs <= ai.clusters[3]) ci = 3;
         else if (ai.clusters[2] > 0) ci = 2;
