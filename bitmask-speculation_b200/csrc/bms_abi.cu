@@ -899,8 +899,7 @@ __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_acce
     __shared__ int64_t s_token, s_tile;
     __shared__ double s_prefix;
     // kLazy: per CTA of the cluster its normalisers {Mt, count, flags, Mq}, {St, Sq}, by pass parity
-    // (a peer's next push cannot overtake a read of this pass's slot); the draft test's inputs by
-    // pass parity; per-warp partial normalisers.
+    // (see npass below); the draft test's inputs by pass parity; per-warp partial normalisers.
     __shared__ uint4 s_norm[kLazy ? 2 : 1][kAcceptCluster][2];
     __shared__ double s_tu[2];
     __shared__ float s_txt[2], s_txq[2];
@@ -930,6 +929,11 @@ __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_acce
     }
     __syncthreads();
     uint32_t gbase = 0;  // chunks this CTA has streamed so far (every thread counts them alike)
+    // kLazy: normaliser passes so far, over all sequences.  Pass n uses slot n & 1 of s_norm and of
+    // the test inputs: a peer's push for pass n + 2 follows pass n + 1's cluster barrier, which every
+    // thread reaches only after reading pass n's slot -- also when a sequence ends without a
+    // sampling pass (and its two cluster barriers) before the next sequence's first push.
+    uint32_t npass = 0;
     // kStream: streams this CTA's tokens [r0 * 256, min(r1 * 256, V)) of a target row -- with
     // `with_q` also of a draft row -- and their mask words through the stages, kTok tokens a chunk
     // (chunk c in stage (gbase + c) % kAccStages), and calls consume(stage, t0, ntc) in every warp
@@ -986,7 +990,7 @@ __global__ void __launch_bounds__(kAccThreads, kStream ? 2 : 1) speculative_acce
             }
             for (int32_t i = 0; j < 0; ++i) {
                 const bool with_q = i < L;  // position L: the bonus row, target only
-                const int slot = i & 1;
+                const int slot = static_cast<int>(npass++ & 1u);
                 const int64_t ti = seq * rows_per_seq + i, qi = seq * K + i;
                 if (tid == 32 && with_q) {  // draft i's test inputs, read while the rows stream
                     const int64_t d = proposals[qi];
