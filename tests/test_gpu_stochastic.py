@@ -296,3 +296,32 @@ def test_lazy_normalisers_agree_with_full_partials():
     same = (outs[0].accept_len == outs[1].accept_len) & (outs[0].token == outs[1].token) & (outs[0].kind == outs[1].kind)
     assert int(same.sum()) >= seqs - 2
     assert (outs[0].accept_len > 0).any() and (outs[0].accept_len < lengths).any()
+
+
+def test_lazy_clusters_looping_over_sequences_that_fail_early():
+    """600 sequences, so every cluster loops over several; every third fails on its first target row
+    (NaN) and so ends without a sampling pass, one in seven has a length outside [0, K].  The lazy
+    round must report what the full-partials round reports for every sequence."""
+    from bitmask_speculation_b200.stochastic import speculative_accept
+    rng = np.random.default_rng(600)
+    seqs, k, vocab, temp = 600, 4, 4096, 1.0
+    rows = seqs * (k + 1)
+    tvals = rng.standard_normal((rows, vocab), dtype=np.float32)
+    tvals[np.arange(0, seqs, 3) * (k + 1), 7] = np.nan
+    dvals = tvals.reshape(seqs, k + 1, vocab)[:, :k].reshape(seqs * k, vocab) * np.float32(0.9)
+    masks = wl.pack_bits_np(rng.random((rows, vocab)) < 0.5)
+    proposals = rng.integers(0, vocab, size=(seqs, k))
+    lengths = rng.integers(0, k + 1, size=seqs).astype(np.int32)
+    lengths[::7] = k + 1
+    args = [_bf16(tvals).cuda(), _bf16(dvals).cuda(), torch.from_numpy(masks).cuda(),
+            torch.from_numpy(proposals).cuda(), torch.from_numpy(lengths).cuda()]
+    ua = torch.from_numpy(rng.random((seqs, k))).cuda()
+    ur = torch.from_numpy(rng.random(seqs)).cuda()
+    lazy, full = (speculative_accept(*args, temperature=temp, accept_uniforms=ua, resample_uniforms=ur, lazy=z)
+                  for z in (True, False))
+    st = lazy.status.cpu().numpy()
+    assert np.array_equal(st, full.status.cpu().numpy())
+    assert (st[::7] == 6).all() and (st[3::21] == 2).all() and (st == 0).sum() > seqs // 3
+    ok = st == 0
+    for a, b in ((lazy.accept_len, full.accept_len), (lazy.token, full.token), (lazy.kind, full.kind)):
+        assert np.array_equal(a.cpu().numpy()[ok], b.cpu().numpy()[ok])
