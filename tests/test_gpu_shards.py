@@ -104,16 +104,17 @@ def test_shard_bounds_match_cluster_segments():
     assert all(off % 32 == 0 for off, _ in b) and sum(s for _, s in b) == 151936
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
 @pytest.mark.parametrize("temperature", [0.0, 0.8])
-def test_partials_through_a_mask_table_equal_gathered_masks(temperature):
+def test_partials_through_a_mask_table_equal_gathered_masks(temperature, dtype):
     """``bms_shard_partials_indexed`` reads row r's mask from ``masks[mask_rows[r]]``: its partials
     (and sampler granules) must equal those of the gathered mask rows bit for bit, and an index
     outside the table must fail its row with status 8."""
     rng = np.random.default_rng(9)
     rows, table_rows, vocab = 96, 40, 20_000
-    bits, masks = make_rows(5, table_rows, vocab, "bfloat16")
+    _, masks = make_rows(5, table_rows, vocab, dtype)
     values = rng.standard_normal((rows, vocab), dtype=np.float32) * np.float32(3)
-    logits = to_device(as_dtype_bits(values, "bfloat16"), "bfloat16")
+    logits = to_device(as_dtype_bits(values, dtype), dtype)
     table = rng.integers(0, table_rows, size=rows).astype(np.int32)
     backend = NativeShardBackend()
     gathered = torch.from_numpy(masks[table]).cuda()
