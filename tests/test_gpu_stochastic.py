@@ -188,11 +188,13 @@ def test_results_do_not_depend_on_how_many_ctas_share_a_sequence(dtype, lazy):
             assert min(abs(ur[s].item() - lo), abs(ur[s].item() - hi)) <= 1e-5, (s, tok[s], t)
 
 
-@pytest.mark.parametrize("vocab", [1001, 4104, 4096])
-def test_rows_that_cannot_be_bulk_copied_agree_with_the_restated_rule(vocab):
+@pytest.mark.parametrize("vocab,lazy", [(1001, False), (4104, False), (4096, False), (3968, False), (4096, True),
+                                        (3968, True)])
+def test_rows_that_cannot_be_bulk_copied_agree_with_the_restated_rule(vocab, lazy):
     """Rows stream through shared memory by 16-byte bulk copies only when a row is a multiple of 16
     bytes and a mask row a multiple of 4 words; V = 1001 (2002-byte rows) and V = 4104 (129 mask
-    words) take the register path instead, V = 4096 streams.  All three must follow the rule."""
+    words) take the register path instead, V = 4096 and V = 3968 (a last 256-token tile of 128
+    tokens) stream, in both modes.  All must follow the rule."""
     from bitmask_speculation_b200.stochastic import speculative_accept
     rng = np.random.default_rng(vocab)
     seqs, k, temp = 24, 4, 0.9
@@ -212,7 +214,8 @@ def test_rows_that_cannot_be_bulk_copied_agree_with_the_restated_rule(vocab):
     ua, ur = rng.random((seqs, k)), rng.random(seqs)
     out = speculative_accept(tvals.cuda(), dvals.cuda(), torch.from_numpy(masks).cuda(), torch.from_numpy(proposals).cuda(),
                              torch.from_numpy(lengths).cuda(), temperature=temp,
-                             accept_uniforms=torch.from_numpy(ua).cuda(), resample_uniforms=torch.from_numpy(ur).cuda())
+                             accept_uniforms=torch.from_numpy(ua).cuda(), resample_uniforms=torch.from_numpy(ur).cuda(),
+                             lazy=lazy)
     acc, tok, kind, st = (t.cpu().numpy() for t in (out.accept_len, out.token, out.kind, out.status))
     assert (st == 0).all()
     want = oracle.speculative_accept(tf, df, masks, proposals, lengths, temp, ua, ur)
