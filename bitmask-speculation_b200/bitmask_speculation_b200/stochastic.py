@@ -137,4 +137,33 @@ def speculative_accept(target_logits, draft_logits, masks, proposals, lengths, *
     return out
 
 
-__all__ = ["SpeculativeAcceptance", "speculative_accept"]
+class AcceptancePolicy:
+    """Chooses ``speculative_accept``'s mode from the rounds seen so far: the lazy round reads only
+    the positions up to the first rejection but runs each sequence's positions one after another,
+    so it pays when accepted runs are short.  Measured on B200 (256 sequences x K = 8, V = 248,320
+    bf16): lazy 0.27 ms against 0.48 ms with a mean accepted run of 0.36 drafts, 0.54 ms against
+    0.48 ms with 2.6.  ``observe(accept_len)`` takes a round's accepted lengths (host values, the
+    ones an engine reads anyway); ``lazy`` is the mode for the next round: lazy while the moving
+    average of the mean accepted run stays below ``threshold``.  Rounds that cannot stream (see
+    ``speculative_accept``) must pass ``lazy=False`` whatever this says."""
+
+    def __init__(self, threshold: float = 1.5, decay: float = 0.8, initial: float | None = None):
+        if not 0.0 <= decay < 1.0:
+            raise ValueError("decay must be in [0, 1)")
+        self.threshold = float(threshold)
+        self.decay = float(decay)
+        self.mean_run = initial
+
+    def observe(self, accept_len) -> None:
+        values = [int(a) for a in accept_len]
+        if not values:
+            return
+        run = sum(values) / len(values)
+        self.mean_run = run if self.mean_run is None else self.decay * self.mean_run + (1.0 - self.decay) * run
+
+    @property
+    def lazy(self) -> bool:
+        return self.mean_run is not None and self.mean_run < self.threshold
+
+
+__all__ = ["AcceptancePolicy", "SpeculativeAcceptance", "speculative_accept"]

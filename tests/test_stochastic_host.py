@@ -46,3 +46,18 @@ def test_lazy_needs_bulk_copyable_rows():
         t, d, m, p, l = _inputs(vocab=vocab)
         with pytest.raises(ValueError, match="lazy acceptance needs"):
             speculative_accept(t, d, m, p, l, temperature=1.0, lazy=True)
+
+
+def test_acceptance_policy_follows_the_mean_accepted_run():
+    from bitmask_speculation_b200.stochastic import AcceptancePolicy
+    pol = AcceptancePolicy(threshold=1.5, decay=0.5)
+    assert not pol.lazy                      # nothing observed yet: every row's partials first
+    pol.observe([0, 0, 1, 0])                # mean 0.25
+    assert pol.lazy and pol.mean_run == 0.25
+    pol.observe([8, 8, 8, 8])                # 0.5 * 0.25 + 0.5 * 8
+    assert not pol.lazy and abs(pol.mean_run - 4.125) < 1e-12
+    pol.observe([])                          # an empty round changes nothing
+    assert abs(pol.mean_run - 4.125) < 1e-12
+    assert AcceptancePolicy(initial=0.5).lazy
+    with pytest.raises(ValueError):
+        AcceptancePolicy(decay=1.0)
