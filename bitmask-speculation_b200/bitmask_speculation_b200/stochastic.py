@@ -141,8 +141,8 @@ class AcceptancePolicy:
     """Chooses ``speculative_accept``'s mode from the rounds seen so far: the lazy round reads only
     the positions up to the first rejection but runs each sequence's positions one after another,
     so it pays when accepted runs are short.  Measured on B200 (256 sequences x K = 8, V = 248,320
-    bf16): lazy 0.27 ms against 0.48 ms with a mean accepted run of 0.36 drafts, 0.54 ms against
-    0.48 ms with 2.6.  ``observe(accept_len)`` takes a round's accepted lengths (host values, the
+    bf16), lazy against full partials: 0.27 / 0.48 ms with a mean accepted run of 0.36 drafts,
+    0.39 / 0.48 with 1.05, 0.51 / 0.48 with 1.93, 0.54 / 0.48 with 2.6.  ``observe(accept_len)`` takes a round's accepted lengths (host values, the
     ones an engine reads anyway); ``lazy`` is the mode for the next round: lazy while the moving
     average of the mean accepted run stays below ``threshold``.  Rounds that cannot stream (see
     ``speculative_accept``) must pass ``lazy=False`` whatever this says."""
